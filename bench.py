@@ -1,0 +1,319 @@
+"""Benchmark of the device path (one JSON line on rank 0).
+
+Headline workload (BASELINE config [3]): BrFS of the 4x4 sliding-tile task (60 seeded random blank moves from the
+solved layout, seed 0) to depth 22, the whole reachable space below that depth, witness pruning and canonical order on
+(mymyr::brfs defaults), stop_at_goal off. One step = one complete BrFS (22 expanded layers). Metric: BrFS expanded
+states/s. Secondary: env steps/s of config [2] (65,536 envs of the two-room, 40-ball transport task).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs under torchrun, one process per GPU. --impl reference times the reference's own CPU BrFS
+(oracle/_ref, mymyr::brfs with deterministic ids, all host threads) on the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "BrFS expanded states/sec"
+UNIT = "states/s"
+DEPTH = 22
+WORKLOAD = "sliding-tile 4x4 BrFS to depth 22 (BASELINE configs[2], seed 0, 60 scramble moves)"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--env-steps", type=int, default=200)
+    ap.add_argument("--no-secondary", action="store_true")
+    return ap.parse_args()
+
+
+def algorithmic_bytes(layer_counts, W):
+    """Per-layer algorithmic bytes of expansion + dedup: parent rows 8W*E, one 32-byte sector per probe 32*G, a stored
+    row compare per duplicate 32*ceil(8W/32)*D, and per new state its row, slot sector and node record."""
+    total = 0
+    for E, G, N in layer_counts:
+        D = G - N
+        total += 8 * W * E + 32 * G + 32 * -(-8 * W // 32) * D + (8 * W + 32 + 8) * N
+    return total
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+        self.f = None
+
+    def __enter__(self):
+        try:
+            self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or self.f is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.f.flush()
+        rows = []
+        for line in open(self.f.name):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def run_reference(args, world, rank):
+    """The reference arm: mymyr::brfs on the host cores (rank 0 only)."""
+    if rank != 0:
+        return
+    from mymyr_b200 import tasks
+    from oracle import ref
+
+    if not ref.available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref not built (make -C oracle)"}))
+        return
+    threads = os.cpu_count() or 1
+    rt = ref.RefTask(tasks.sliding_tile(4, 4, 60, 0))
+    for _ in range(args.warmup):
+        rt.brfs(threads=threads, max_depth=DEPTH, stop_at_goal=False, store="concurrent")
+    times, expanded = [], 0
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        r = rt.brfs(threads=threads, max_depth=DEPTH, stop_at_goal=False, store="concurrent")
+        times.append(time.perf_counter() - t0)
+        expanded = r["expanded"]
+    total = sum(times)
+    value = expanded * args.steps / total
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000 * total / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u64", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "threads": threads, "store": "concurrent", "deterministic_ids": True},
+            "impl": "reference",
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference",
+                             "sample": f"full workload x {args.steps} runs"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline(steps_hint=1):
+    from mymyr_b200 import tasks
+    from oracle import ref
+
+    if not ref.available():
+        return None
+    threads = os.cpu_count() or 1
+    rt = ref.RefTask(tasks.sliding_tile(4, 4, 60, 0))
+    t0 = time.perf_counter()
+    r = rt.brfs(threads=threads, max_depth=DEPTH, stop_at_goal=False, store="concurrent")
+    dt = time.perf_counter() - t0
+    return {"value": r["expanded"] / dt, "unit": UNIT, "cores": threads, "kind": "reference",
+            "sample": f"one full BrFS to depth {DEPTH} ({r['expanded']} expanded, {dt:.2f} s, mymyr::brfs "
+                      f"concurrent store, {threads} threads)"}
+
+
+def env_secondary(args, device):
+    import torch
+
+    from mymyr_b200 import rl as b2rl
+    from mymyr_b200 import tasks
+    from mymyr_b200.task import Task
+
+    t = Task.from_text(tasks.transport(2, 40, 2, 0))
+    n = 65536
+    env = b2rl.BatchedEnv(t, n, seed=0, device=device)
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        env.reset(stream=stream.cuda_stream)
+        for _ in range(20):
+            env.step(stream=stream.cuda_stream)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(args.env_steps):
+            env.step(stream=stream.cuda_stream)
+        b.record(stream)
+    stream.synchronize()
+    ms = a.elapsed_time(b)
+    return {"metric": "env steps/sec (BASELINE configs[1]: 65,536 envs, transport 2 rooms/40 balls/2 grippers)",
+            "value": n * args.env_steps / (ms / 1000.0), "unit": "steps/s", "steps_timed": args.env_steps,
+            "ms_per_step": ms / args.env_steps}
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        return
+    import torch
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+        pg = dist
+    from mymyr_b200 import cuda as b2cuda
+    from mymyr_b200 import tasks
+    from mymyr_b200.task import Context, Task
+
+    ctx = Context(local)
+    text = tasks.sliding_tile(4, 4, 60, 0)
+    task = Task.from_text(text, ctx)
+    stream = torch.cuda.Stream(device)
+    sp = stream.cuda_stream
+
+    def one(expected=None):
+        return b2cuda.brfs(task, max_depth=DEPTH, stop_at_goal=False, timings=True, expected_states=expected,
+                           stream=sp)
+
+    r = one()
+    expected = r.states
+    for _ in range(max(0, args.warmup - 1)):
+        r = one(expected)
+
+    def barrier():
+        torch.cuda.synchronize(device)
+        if pg is not None:
+            pg.barrier()
+        torch.cuda.synchronize(device)
+
+    # ---------------------------------------------------------------- timed region (device events)
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    results = []
+    with Clocks(local) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            results.append(one(expected))
+        ev1.record(stream)
+        stream.synchronize()
+    barrier()
+    ms = ev0.elapsed_time(ev1)
+    clocks = clk.summary()
+    if pg is not None:
+        t = torch.tensor([ms], dtype=torch.float64, device=device)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms = float(t.item())
+    expanded = results[-1].expanded
+    value = world * expanded * args.steps / (ms / 1000.0)
+    # roofline of expansion + dedup (k_expand and the winners' scan), from its device events
+    W = task.words
+    bytes_run = algorithmic_bytes(results[-1].layer_counts, W)
+    kern_ms = statistics.mean(r.stats.gen_ms + r.stats.dedup_ms for r in results)
+    peak, peak_kind = measured_peaks()
+    achieved = bytes_run / (kern_ms / 1000.0) / 1e9
+    launches = sum(r.stats.kernel_launches for r in results)
+
+    # ---------------------------------------------------------------- end to end through the public API
+    barrier()
+    e2e_times = []
+    h2d = len(text.encode())
+    d2h = 0
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        t2 = Task.from_text(text, ctx)
+        rr = b2cuda.brfs(t2, max_depth=DEPTH, stop_at_goal=False, expected_states=expected, stream=sp)
+        hashes = rr.state_hashes()
+        e2e_times.append(time.perf_counter() - t0)
+        d2h = hashes.nbytes + 24 * rr.layers
+    e2e_s = sum(e2e_times)
+    if pg is not None:
+        t = torch.tensor([e2e_s], dtype=torch.float64, device=device)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_value = world * expanded * args.steps / e2e_s
+
+    secondary = None if args.no_secondary else env_secondary(args, device)
+    base = cpu_baseline() if rank == 0 and world == 1 else None
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u64", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "states": results[-1].states, "expanded": expanded,
+                       "generated": results[-1].generated, "layers": results[-1].layers, "words": W,
+                       "parallelism": "replicas" if world > 1 else "single",
+                       "l2": "working set > L2 (rows, table and frontiers are several hundred MB)",
+                       "expected_states": "presized from the warm-up run"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None, "kernel": "k_expand + winners scan",
+                         "algorithmic_bytes_per_run": bytes_run, "kernel_ms_per_run": kern_ms,
+                         "peak_source": peak_kind},
+            "cpu_baseline": base,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches,
+            "clocks": clocks,
+            "phases_ms_per_run": {"count": statistics.mean(r.stats.count_ms for r in results),
+                                  "expand": statistics.mean(r.stats.gen_ms for r in results),
+                                  "rank": statistics.mean(r.stats.dedup_ms for r in results),
+                                  "wall": statistics.mean(r.search_s * 1000 for r in results)},
+            "secondary": secondary,
+        }
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

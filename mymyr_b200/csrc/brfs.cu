@@ -1,0 +1,766 @@
+// Layer-synchronous device BrFS (cuda::DeviceBrfs / mymyr::brfs with deterministic ids,
+// include/mymyr/cuda/brfs.hpp:96-123, include/mymyr/search/brfs.hpp:140; loop semantics of run_flat,
+// src/mymyr/search/brfs.cpp:273-404).
+//
+// Data layout in HBM. Every successor ever generated has a global candidate index g: a layer's candidates are
+// numbered in canonical order (parent id, successor index) after the previous layers'. Per candidate (written only
+// when it takes a hash-set slot): its row rows[g * W .. +W), its hash, its parent's index in its layer and its
+// successor index. Per state id: state_g[id], the candidate that discovered it; a layer's frontier is the id range
+// [begin, end) of state_g. The hash set is open addressing over u64 slots (hash >> 32) << 32 | g, linear probing
+// from hash & mask; EMPTY is all ones.
+//
+// Deterministic ids without a sort: within a slot's lifetime every value refers to the same state, so an equal
+// successor replaces a larger candidate index with atomicMin (the tag sits above g, equal tags compare by g). The
+// smallest g of a state, its first discovery in canonical order, always ends up in the slot, and a state found in an
+// earlier layer keeps its smaller g. A candidate that took a slot marks itself `claimed`; one that displaces a
+// larger candidate of the layer marks that one `lost`. New states are the claimed, not lost candidates; an exclusive
+// scan over the layer's candidates in order gives their ids, in the order of the reference's (parent id, successor
+// index) discoverer keys (src/mymyr/search/brfs.cpp:1657-1778).
+//
+// Per layer: k_count (goal test + successor counts per parent) -> scan (candidate offsets) -> host reads the layer's
+// candidate count -> k_expand (regenerate, hash, insert) -> scan of winners (ids) -> host reads the new-state count.
+
+#include "scan.cuh"
+
+#include <chrono>
+
+namespace b2
+{
+namespace
+{
+constexpr u64 kEmpty = ~u64{0};
+
+struct LayerMisc
+{
+    u64 total_cand;  // candidates of the layer (scan total)
+    u64 total_new;   // new states of the layer (scan total)
+    u64 fingerprint;
+    u32 goals;       // goal states among the layer's parents
+    u32 first_goal;  // smallest parent index that is a goal (0xFFFFFFFF: none)
+    u32 status;
+    u32 pad;
+};
+
+__device__ __forceinline__ u64 ld_acquire(const u64* p)
+{
+    u64 v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+struct Store
+{
+    u64* rows;
+    u64* hash;
+    u32* par;
+    u32* kid;
+    u64* table;
+    u64 mask;
+    u32 W;
+    u32 max_probe;
+    u8* claimed;  // per layer candidate
+    u8* lost;
+    u64 layer_cand_begin;
+    u32* status;
+};
+
+/// Inserts candidate g (row `s`, hash h) of parent i, successor index k.
+template<class Row>
+__device__ __forceinline__ void insert(const Store& S, const Row& s, u64 h, u64 g, u32 i, u32 k)
+{
+    const u64 mine = (h & 0xFFFFFFFF00000000ull) | g;
+    u64 j = h & S.mask;
+    bool written = false;
+    auto write_row = [&]() {
+        if (written)
+            return;
+        u64* r = S.rows + g * S.W;
+        for (u32 w = 0; w < S.W; ++w)
+            r[w] = s.word(w);
+        S.hash[g] = h;
+        S.par[g] = i;
+        S.kid[g] = k;
+        __threadfence();
+        written = true;
+    };
+    for (u32 probe = 0; probe < S.max_probe; ++probe, j = (j + 1) & S.mask)
+    {
+        u64 cur = ld_acquire(S.table + j);
+        if (cur == kEmpty)
+        {
+            write_row();
+            const u64 prev = atomicCAS(reinterpret_cast<unsigned long long*>(S.table + j), kEmpty, mine);
+            if (prev == kEmpty)
+            {
+                S.claimed[g - S.layer_cand_begin] = 1;
+                return;
+            }
+            cur = prev;
+        }
+        if ((cur >> 32) != (mine >> 32))
+            continue;
+        const u64 og = cur & 0xFFFFFFFFull;
+        const u64* r = S.rows + og * S.W;
+        bool eq = true;
+        for (u32 w = 0; w < S.W && eq; ++w)
+            eq = __ldcg(r + w) == s.word(w);
+        if (!eq)
+            continue;
+        if (og < g)
+            return;  // an earlier discovery of the same state
+        write_row();
+        const u64 prev = atomicMin(reinterpret_cast<unsigned long long*>(S.table + j), mine);
+        if (prev > mine)
+        {
+            S.claimed[g - S.layer_cand_begin] = 1;
+            S.lost[(prev & 0xFFFFFFFFull) - S.layer_cand_begin] = 1;
+        }
+        return;
+    }
+    atomicOr(S.status, kStatusProbeLimit);
+}
+
+template<int OW, int WR>
+__global__ void __launch_bounds__(128) k_count(DevTask T, u32 pi, const u64* __restrict__ rows, u32 W,
+                                               const u32* __restrict__ frontier, u64 E, u32* __restrict__ counts,
+                                               LayerMisc* misc)
+{
+    for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < E; i += static_cast<u64>(gridDim.x) * blockDim.x)
+    {
+        const u64 g = frontier[i];
+        const auto st = load_row<WR>(rows + g * W, W);
+        if (goal_holds(T, st))
+        {
+            atomicAdd(&misc->goals, 1u);
+            atomicMin(&misc->first_goal, static_cast<u32>(i));
+        }
+        u32 c = 0;
+        u32 bind[kMaxLevels] = {};
+        for (u32 s = 0; s < T.nschemas; ++s)
+            enumerate<OW>(T, T.schemas[s].prog[pi], st, bind, [&](const u32*) {
+                ++c;
+                return true;
+            });
+        counts[i] = c;
+    }
+}
+
+template<int OW, int WR>
+__global__ void __launch_bounds__(128) k_expand(DevTask T, u32 pi, const u32* __restrict__ frontier, u64 E,
+                                                const u64* __restrict__ cand_base, Store S)
+{
+    for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < E; i += static_cast<u64>(gridDim.x) * blockDim.x)
+    {
+        const u64 pg = frontier[i];
+        const auto st = load_row<WR>(S.rows + pg * S.W, S.W);
+        const u64 g0 = S.layer_cand_begin + cand_base[i];
+        u32 k = 0;
+        u32 bind[kMaxLevels] = {};
+        for (u32 s = 0; s < T.nschemas; ++s)
+        {
+            const DSchema& sc = T.schemas[s];
+            enumerate<OW>(T, sc.prog[pi], st, bind, [&](const u32* b) {
+                Effects e;
+                collect_effects(T, sc, b, e);
+                if constexpr (WR > 0)
+                {
+                    RegRow<WR> nx;
+#pragma unroll
+                    for (int q = 0; q < WR; ++q)
+                        nx.w[q] = succ_word(st, e, q);
+                    const u64 h = hash_words([&](u32 q) { return nx.word(q); }, S.W);
+                    insert(S, nx, h, g0 + k, static_cast<u32>(i), k);
+                }
+                else
+                {
+                    const SuccRow<decltype(st)> nx{st, e};
+                    const u64 h = hash_words([&](u32 q) { return nx.word(q); }, S.W);
+                    insert(S, nx, h, g0 + k, static_cast<u32>(i), k);
+                }
+                ++k;
+                return true;
+            });
+        }
+    }
+}
+
+__global__ void k_seed_root(Store S, u32* state_g)
+{
+    const GlobalRow r{S.rows, S.W};
+    const u64 h = hash_words([&](u32 q) { return r.word(q); }, S.W);
+    S.hash[0] = h;
+    S.par[0] = 0xFFFFFFFFu;
+    S.kid[0] = 0;
+    state_g[0] = 0;
+    u64 j = h & S.mask;
+    for (u32 probe = 0; probe < S.max_probe && S.table[j] != kEmpty; ++probe)
+        j = (j + 1) & S.mask;
+    if (S.table[j] == kEmpty)
+        S.table[j] = (h & 0xFFFFFFFF00000000ull);
+    else
+        atomicOr(S.status, kStatusProbeLimit);
+}
+
+__global__ void k_rehash(u64* __restrict__ table, u64 mask, u32 max_probe, const u32* __restrict__ state_g, u64 n,
+                         const u64* __restrict__ hash, u32* status)
+{
+    for (u64 id = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; id < n; id += static_cast<u64>(gridDim.x) * blockDim.x)
+    {
+        const u64 g = state_g[id];
+        const u64 h = hash[g];
+        const u64 mine = (h & 0xFFFFFFFF00000000ull) | g;
+        u64 j = h & mask;
+        u32 probe = 0;
+        for (; probe < max_probe; ++probe, j = (j + 1) & mask)
+            if (atomicCAS(reinterpret_cast<unsigned long long*>(table + j), kEmpty, mine) == kEmpty)
+                break;
+        if (probe == max_probe)
+            atomicOr(status, kStatusProbeLimit);
+    }
+}
+
+struct WinIn
+{
+    const u8* claimed;
+    const u8* lost;
+    __device__ __forceinline__ u32 operator()(u64 c) const { return claimed[c] & (lost[c] ^ 1u); }
+};
+struct WinOut
+{
+    u32* state_g;  // + id of the layer's first new state
+    u64 cand_begin;
+    __device__ __forceinline__ void operator()(u64 c, u64 rank, u32 v) const
+    {
+        if (v)
+            state_g[rank] = static_cast<u32>(cand_begin + c);
+    }
+};
+struct CountIn
+{
+    const u32* c;
+    __device__ __forceinline__ u32 operator()(u64 i) const { return c[i]; }
+};
+struct BaseOut
+{
+    u64* base;
+    __device__ __forceinline__ void operator()(u64 i, u64 e, u32) const { base[i] = e; }
+};
+
+__global__ void k_fingerprint(const u32* __restrict__ state_g, u64 first_id, u64 n, const u64* __restrict__ rows,
+                              u32 W, u64* acc)
+{
+    u64 x = 0;
+    for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < n; i += static_cast<u64>(gridDim.x) * blockDim.x)
+    {
+        const u64 g = state_g[first_id + i];
+        const GlobalRow r{rows + g * W, W};
+        x ^= fingerprint_term(first_id + i, canonical_hash(r, W));
+    }
+    for (int o = 16; o > 0; o >>= 1)
+        x ^= __shfl_xor_sync(0xFFFFFFFFu, x, o);
+    if ((threadIdx.x & 31) == 0 && x)
+        atomicXor(reinterpret_cast<unsigned long long*>(acc), x);
+}
+
+__global__ void k_gather_rows(const u32* __restrict__ state_g, u64 first, u64 n, const u64* __restrict__ rows, u32 W,
+                              u64* __restrict__ out, u32 out_words)
+{
+    for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < n; i += static_cast<u64>(gridDim.x) * blockDim.x)
+    {
+        const u64 g = state_g[first + i];
+        for (u32 w = 0; w < out_words; ++w)
+            out[i * out_words + w] = w < W ? rows[g * W + w] : 0;
+    }
+}
+
+__global__ void k_gather_hash(const u32* __restrict__ state_g, u64 first, u64 n, const u64* __restrict__ hash,
+                              u64* __restrict__ out)
+{
+    for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < n; i += static_cast<u64>(gridDim.x) * blockDim.x)
+        out[i] = hash[state_g[first + i]];
+}
+
+__global__ void k_gather_nodes(const u32* __restrict__ state_g, u64 first, u64 n, const u32* __restrict__ par,
+                               const u32* __restrict__ kid, const u64* __restrict__ layer_begin, u32 nlayers,
+                               u32* __restrict__ out_parent, u32* __restrict__ out_index)
+{
+    for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < n; i += static_cast<u64>(gridDim.x) * blockDim.x)
+    {
+        const u64 id = first + i;
+        const u64 g = state_g[id];
+        if (id == 0)
+        {
+            out_parent[i] = 0xFFFFFFFFu;
+            out_index[i] = 0;
+            continue;
+        }
+        // layer L of id: layer_begin[L] <= id < layer_begin[L + 1]; its parents are in layer L - 1
+        u32 lo = 0, hi = nlayers;
+        while (hi - lo > 1)
+        {
+            const u32 mid = (lo + hi) / 2;
+            if (layer_begin[mid] <= id)
+                lo = mid;
+            else
+                hi = mid;
+        }
+        out_parent[i] = static_cast<u32>(layer_begin[lo - 1] + par[g]);
+        out_index[i] = kid[g];
+    }
+}
+}  // namespace
+}  // namespace b2
+
+using namespace b2;
+
+struct b2_brfs
+{
+    b2_task* task = nullptr;
+    b2_brfs_options opt{};
+    cudaStream_t stream = nullptr;
+    u32 W = 1;
+    // per candidate
+    DeviceBuffer rows, hash, par, kid;
+    u64 cap_cand = 0;
+    // per state
+    DeviceBuffer state_g;
+    u64 cap_states = 0;
+    // hash set
+    DeviceBuffer table;
+    u64 table_slots = 0;
+    u32 rehashes = 0;
+    // per layer scratch
+    DeviceBuffer counts, cand_base, flags, sums, misc;
+    u64 cap_layer = 0, cap_flags = 0;
+    // results
+    std::vector<u64> layer_begin;  // id of each layer's first state (+ the end)
+    u64 n_states = 0;
+    u64 launches = 0;
+    bool ran = false;
+    bool own_stream = false;
+};
+
+namespace
+{
+void ensure_cand(b2_brfs& B, u64 need, u64 used)
+{
+    if (need <= B.cap_cand)
+        return;
+    const u64 cap = std::max<u64>(need, B.cap_cand + B.cap_cand / 2);
+    B.rows.grow(cap * B.W * 8, used * B.W * 8, B.stream);
+    B.hash.grow(cap * 8, used * 8, B.stream);
+    B.par.grow(cap * 4, used * 4, B.stream);
+    B.kid.grow(cap * 4, used * 4, B.stream);
+    B.cap_cand = cap;
+}
+
+void ensure_states(b2_brfs& B, u64 need)
+{
+    if (need <= B.cap_states)
+        return;
+    const u64 cap = std::max<u64>(need, B.cap_states + B.cap_states / 2);
+    B.state_g.grow(cap * 4, B.n_states * 4, B.stream);
+    B.cap_states = cap;
+}
+
+void ensure_layer(b2_brfs& B, u64 E, u64 G)
+{
+    if (E > B.cap_layer)
+    {
+        const u64 cap = std::max<u64>(E, B.cap_layer * 2);
+        B.counts.alloc(cap * 4);
+        B.cand_base.alloc((cap + 1) * 8);
+        B.sums.alloc(std::max(scan_scratch_bytes(cap), B.sums.bytes));
+        B.cap_layer = cap;
+    }
+    if (G > B.cap_flags)
+    {
+        const u64 cap = std::max<u64>(G, B.cap_flags * 2);
+        B.flags.alloc(cap * 2 + 16);
+        if (B.sums.bytes < scan_scratch_bytes(cap))
+            B.sums.alloc(scan_scratch_bytes(cap));
+        B.cap_flags = cap;
+    }
+}
+
+u32 max_probe(u64 slots) { return static_cast<u32>(std::min<u64>(slots, u64{1} << 20)); }
+
+/// Grows the hash set so that `states` entries keep it at most half full, and reinserts the stored states.
+void ensure_table(b2_brfs& B, u64 states)
+{
+    if (states * 2 <= B.table_slots)
+        return;
+    u64 slots = B.table_slots ? B.table_slots : 1024;
+    while (states * 2 > slots)
+        slots *= 2;
+    B.table.alloc(slots * 8);
+    B.table_slots = slots;
+    B2_CUDA(cudaMemsetAsync(B.table.p, 0xFF, slots * 8, B.stream));
+    if (B.n_states)
+    {
+        LayerMisc* misc = B.misc.as<LayerMisc>();
+        k_rehash<<<grid_for(B.n_states, 256), 256, 0, B.stream>>>(B.table.as<u64>(), slots - 1, max_probe(slots),
+                                                                    B.state_g.as<u32>(), B.n_states, B.hash.as<u64>(),
+                                                                    &misc->status);
+        B2_CUDA(cudaGetLastError());
+        ++B.rehashes;
+        ++B.launches;
+    }
+}
+
+Store make_store(b2_brfs& B, u64 layer_cand_begin)
+{
+    Store S;
+    S.rows = B.rows.as<u64>();
+    S.hash = B.hash.as<u64>();
+    S.par = B.par.as<u32>();
+    S.kid = B.kid.as<u32>();
+    S.table = B.table.as<u64>();
+    S.mask = B.table_slots - 1;
+    S.W = B.W;
+    S.max_probe = max_probe(B.table_slots);
+    S.claimed = B.flags.as<u8>();
+    S.lost = B.flags.as<u8>() + B.cap_flags;
+    S.layer_cand_begin = layer_cand_begin;
+    S.status = &B.misc.as<LayerMisc>()->status;
+    return S;
+}
+
+LayerMisc read_misc(b2_brfs& B)
+{
+    LayerMisc m;
+    B2_CUDA(cudaMemcpyAsync(&m, B.misc.p, sizeof m, cudaMemcpyDeviceToHost, B.stream));
+    B2_CUDA(cudaStreamSynchronize(B.stream));
+    if (m.status & kStatusProbeLimit)
+        throw Error(B2_DEVICE_FAULT, "b2_brfs: a hash-set probe ran past its bound");
+    if (m.status)
+        throw Error(B2_DEVICE_FAULT, "b2_brfs: device status " + std::to_string(m.status));
+    return m;
+}
+
+void run_search(b2_brfs& B, b2_brfs_result& R)
+{
+    const auto t0 = std::chrono::steady_clock::now();
+    const Program& P = B.task->prog;
+    const DevTask& T = B.task->dev;
+    const b2_brfs_options& o = B.opt;
+    const u32 pi = o.witness_pruning ? 0 : 1;
+    const u32 W = B.W;
+    cudaStream_t s = B.stream;
+    cudaEvent_t ev[5];
+    for (auto& e : ev)
+        B2_CUDA(cudaEventCreate(&e));
+    struct EvGuard
+    {
+        cudaEvent_t* e;
+        ~EvGuard()
+        {
+            for (int i = 0; i < 5; ++i)
+                cudaEventDestroy(e[i]);
+        }
+    } guard{ev};
+
+    R.states = 1;
+    R.words = W;
+    if (o.stop_at_goal && P.goal_unsat)
+    {
+        R.status = B2_SEARCH_UNSOLVABLE;
+        B.n_states = 1;
+        return;
+    }
+    // root
+    const u64 expect = std::max<u64>(o.expected_states, 1024);
+    ensure_cand(B, expect * 2, 0);
+    ensure_states(B, expect);
+    B.misc.alloc(sizeof(LayerMisc));
+    B2_CUDA(cudaMemsetAsync(B.misc.p, 0, sizeof(LayerMisc), s));
+    ensure_table(B, expect);
+    B2_CUDA(cudaMemcpyAsync(B.rows.p, P.initial.data(), W * 8, cudaMemcpyHostToDevice, s));
+    k_seed_root<<<1, 1, 0, s>>>(make_store(B, 0), B.state_g.as<u32>());
+    B2_CUDA(cudaGetLastError());
+    ++B.launches;
+    B.n_states = 1;
+    u64 cand_next = 1;  // candidate 0 is the root
+    u64 layer_begin = 0, layer_end = 1;
+    B.layer_begin.assign(1, 0);
+    u32 layers = 0;
+    bool exhausted = false, solved = false;
+    u64 expanded = 0, generated = 0, goals = 0, goal_id = 0, fingerprint = 0;
+    double count_ms = 0, gen_ms = 0, dedup_ms = 0;
+    std::vector<std::array<u64, 3>> counts;
+    for (;;)
+    {
+        const u64 E = layer_end - layer_begin;
+        if (E == 0)
+        {
+            exhausted = true;
+            break;
+        }
+        if (layers == o.max_depth)
+            break;
+        ++layers;
+        ensure_layer(B, E, 0);
+        LayerMisc* misc = B.misc.as<LayerMisc>();
+        const LayerMisc init{0, 0, 0, 0, 0xFFFFFFFFu, 0, 0};
+        B2_CUDA(cudaMemcpyAsync(misc, &init, sizeof init, cudaMemcpyHostToDevice, s));
+        const u32* frontier = B.state_g.as<u32>() + layer_begin;
+        const unsigned grid = grid_for(E, 128, static_cast<unsigned>(B.task->ctx->sms) * 64);
+        if (o.timings)
+            B2_CUDA(cudaEventRecord(ev[0], s));
+        dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
+            k_count<OW, WR><<<grid, 128, 0, s>>>(T, pi, B.rows.as<u64>(), W, frontier, E, B.counts.as<u32>(), misc);
+        });
+        device_scan(CountIn{B.counts.as<u32>()}, BaseOut{B.cand_base.as<u64>()}, E, &misc->total_cand, B.sums.as<u64>(), s);
+        B.launches += 4;
+        if (o.timings)
+            B2_CUDA(cudaEventRecord(ev[1], s));
+        LayerMisc m = read_misc(B);
+        u64 E_exp = E, G = m.total_cand;
+        bool stop = false;
+        if (m.goals)
+        {
+            if (!solved)
+            {
+                solved = true;
+                goal_id = layer_begin + m.first_goal;
+            }
+            if (o.stop_at_goal)
+            {
+                E_exp = m.first_goal;
+                if (E_exp < E)
+                    B2_CUDA(cudaMemcpyAsync(&G, B.cand_base.as<u64>() + E_exp, 8, cudaMemcpyDeviceToHost, s));
+                B2_CUDA(cudaStreamSynchronize(s));
+                goals += 1;
+                stop = true;
+            }
+            else
+                goals += m.goals;
+        }
+        if (G >= (u64{1} << 32) - 1 - cand_next)
+            throw Error(B2_CAPACITY, "b2_brfs: more than 2^32 - 2 candidates");
+        ensure_layer(B, E, G);
+        ensure_cand(B, cand_next + G, cand_next);
+        ensure_states(B, B.n_states + G);
+        ensure_table(B, B.n_states + G);
+        u64 N = 0;
+        if (E_exp > 0 && G > 0)
+        {
+            B2_CUDA(cudaMemsetAsync(B.flags.p, 0, G, s));
+            B2_CUDA(cudaMemsetAsync(B.flags.as<u8>() + B.cap_flags, 0, G, s));
+            if (o.timings)
+                B2_CUDA(cudaEventRecord(ev[2], s));
+            const Store S = make_store(B, cand_next);
+            frontier = B.state_g.as<u32>() + layer_begin;
+            const unsigned grid_e = grid_for(E_exp, 128, static_cast<unsigned>(B.task->ctx->sms) * 64);
+            dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
+                k_expand<OW, WR><<<grid_e, 128, 0, s>>>(T, pi, frontier, E_exp, B.cand_base.as<u64>(), S);
+            });
+            B2_CUDA(cudaGetLastError());
+            if (o.timings)
+                B2_CUDA(cudaEventRecord(ev[3], s));
+            device_scan(WinIn{S.claimed, S.lost}, WinOut{B.state_g.as<u32>() + B.n_states, cand_next}, G,
+                        &misc->total_new, B.sums.as<u64>(), s);
+            B.launches += 4;
+            if (o.timings)
+                B2_CUDA(cudaEventRecord(ev[4], s));
+            m = read_misc(B);
+            N = m.total_new;
+            if (o.timings)
+            {
+                float a = 0, b = 0, c = 0;
+                B2_CUDA(cudaEventElapsedTime(&a, ev[0], ev[1]));
+                B2_CUDA(cudaEventElapsedTime(&b, ev[2], ev[3]));
+                B2_CUDA(cudaEventElapsedTime(&c, ev[3], ev[4]));
+                count_ms += a;
+                gen_ms += b;
+                dedup_ms += c;
+            }
+        }
+        expanded += E_exp;
+        generated += G;
+        counts.push_back({E_exp, G, N});
+        cand_next += G;
+        B.n_states += N;
+        layer_begin = layer_end;
+        layer_end = B.n_states;
+        B.layer_begin.push_back(layer_begin);
+        if (stop)
+            break;
+    }
+    B.layer_begin.push_back(B.n_states);
+    if (o.fingerprint)
+    {
+        u64* acc = &B.misc.as<LayerMisc>()->fingerprint;
+        B2_CUDA(cudaMemsetAsync(acc, 0, 8, s));
+        k_fingerprint<<<grid_for(B.n_states, 256, static_cast<unsigned>(B.task->ctx->sms) * 8), 256, 0, s>>>(
+            B.state_g.as<u32>(), 0, B.n_states, B.rows.as<u64>(), W, acc);
+        B2_CUDA(cudaGetLastError());
+        ++B.launches;
+        fingerprint = read_misc(B).fingerprint;
+    }
+    B2_CUDA(cudaStreamSynchronize(s));
+    R.states = B.n_states;
+    R.expanded = expanded;
+    R.generated = generated;
+    R.num_goal_states = goals;
+    R.layers = layers;
+    R.exhausted = exhausted ? 1 : 0;
+    R.solved = solved ? 1 : 0;
+    R.goal_id = solved ? goal_id : 0;
+    R.fingerprint = fingerprint;
+    R.count_ms = count_ms;
+    R.gen_ms = gen_ms;
+    R.dedup_ms = dedup_ms;
+    R.kernel_launches = B.launches;
+    R.status = solved ? B2_SEARCH_SOLVED
+                      : (exhausted || layers >= o.max_depth ? B2_SEARCH_EXHAUSTED : B2_SEARCH_OUT_OF_STATES);
+    R.rehashes = B.rehashes;
+    u32 lg = 0;
+    while ((u64{1} << lg) < B.table_slots)
+        ++lg;
+    R.table_log2 = lg;
+    if (R.layer_counts)
+        for (u32 i = 0; i < counts.size() && i < R.layer_capacity; ++i)
+            for (int k = 0; k < 3; ++k)
+                R.layer_counts[3 * i + k] = counts[i][k];
+    R.search_s = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+}
+}  // namespace
+
+extern "C" {
+
+void b2_brfs_options_default(b2_brfs_options* o)
+{
+    if (!o)
+        return;
+    *o = b2_brfs_options{};
+    o->witness_pruning = 1;
+    o->stop_at_goal = 1;
+    o->fingerprint = 0;
+    o->max_depth = 0xFFFFFFFFu;
+    o->max_states = ~uint64_t{0};
+    o->expected_states = 0;
+    o->timings = 0;
+    o->world_rank = 0;
+    o->world_size = 1;
+}
+
+b2_status b2_brfs_create(b2_task* task, const b2_brfs_options* options, b2_brfs** out)
+{
+    return guarded([&] {
+        if (!task || !options || !out)
+            throw std::invalid_argument("b2_brfs_create: null argument");
+        if (!task->ctx)
+            throw std::invalid_argument("a host-only task (created without a context) cannot run on the device");
+        if (options->max_states != ~uint64_t{0})
+            throw Error(B2_UNSUPPORTED, "b2_brfs: max_states is not supported by the device BrFS yet");
+        if (options->world_size != 1)
+            throw Error(B2_UNSUPPORTED, "b2_brfs: use the multi-GPU driver for world_size > 1");
+        if (options->witness_pruning && task->witness_refused)
+            throw Error(B2_UNSUPPORTED, "witness pruning with a witness parameter before an effect parameter");
+        B2_CUDA(cudaSetDevice(task->ctx->device));
+        auto b = std::make_unique<b2_brfs>();
+        b->task = task;
+        b->opt = *options;
+        b->W = task->prog.words;
+        if (options->stream)
+            b->stream = static_cast<cudaStream_t>(options->stream);
+        else
+        {
+            B2_CUDA(cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking));
+            b->own_stream = true;
+        }
+        *out = b.release();
+    });
+}
+
+b2_status b2_brfs_run(b2_brfs* search, b2_brfs_result* result)
+{
+    return guarded([&] {
+        if (!search || !result)
+            throw std::invalid_argument("b2_brfs_run: null argument");
+        if (search->ran)
+            throw std::invalid_argument("b2_brfs_run: the search ran already");
+        search->ran = true;
+        B2_CUDA(cudaSetDevice(search->task->ctx->device));
+        uint64_t* lc = result->layer_counts;
+        const uint32_t cap = result->layer_capacity;
+        *result = b2_brfs_result{};
+        result->layer_counts = lc;
+        result->layer_capacity = cap;
+        run_search(*search, *result);
+    });
+}
+
+b2_status b2_brfs_states(b2_brfs* B, uint64_t first, uint64_t count, uint64_t* rows, uint32_t words)
+{
+    return guarded([&] {
+        if (!B || (count && !rows) || !B->ran)
+            throw std::invalid_argument("b2_brfs_states: bad argument");
+        if (first + count > B->n_states || words < B->W)
+            throw std::invalid_argument("b2_brfs_states: range or width out of bounds");
+        if (!count)
+            return;
+        DeviceBuffer tmp;
+        tmp.alloc(count * words * 8);
+        k_gather_rows<<<grid_for(count, 256), 256, 0, B->stream>>>(B->state_g.as<u32>(), first, count, B->rows.as<u64>(),
+                                                                   B->W, tmp.as<u64>(), words);
+        B2_CUDA(cudaGetLastError());
+        B2_CUDA(cudaMemcpyAsync(rows, tmp.p, count * words * 8, cudaMemcpyDeviceToHost, B->stream));
+        B2_CUDA(cudaStreamSynchronize(B->stream));
+    });
+}
+
+b2_status b2_brfs_state_hashes(b2_brfs* B, uint64_t first, uint64_t count, uint64_t* hashes)
+{
+    return guarded([&] {
+        if (!B || (count && !hashes) || !B->ran || first + count > B->n_states)
+            throw std::invalid_argument("b2_brfs_state_hashes: bad argument");
+        if (!count)
+            return;
+        DeviceBuffer tmp;
+        tmp.alloc(count * 8);
+        k_gather_hash<<<grid_for(count, 256), 256, 0, B->stream>>>(B->state_g.as<u32>(), first, count,
+                                                                   B->hash.as<u64>(), tmp.as<u64>());
+        B2_CUDA(cudaGetLastError());
+        B2_CUDA(cudaMemcpyAsync(hashes, tmp.p, count * 8, cudaMemcpyDeviceToHost, B->stream));
+        B2_CUDA(cudaStreamSynchronize(B->stream));
+    });
+}
+
+b2_status b2_brfs_nodes(b2_brfs* B, uint64_t first, uint64_t count, uint32_t* parent, uint32_t* index)
+{
+    return guarded([&] {
+        if (!B || (count && (!parent || !index)) || !B->ran || first + count > B->n_states)
+            throw std::invalid_argument("b2_brfs_nodes: bad argument");
+        if (!count)
+            return;
+        DeviceBuffer tmp, lb;
+        tmp.alloc(count * 8);
+        lb.alloc(B->layer_begin.size() * 8);
+        B2_CUDA(cudaMemcpyAsync(lb.p, B->layer_begin.data(), B->layer_begin.size() * 8, cudaMemcpyHostToDevice, B->stream));
+        u32* tp = tmp.as<u32>();
+        k_gather_nodes<<<grid_for(count, 256), 256, 0, B->stream>>>(B->state_g.as<u32>(), first, count, B->par.as<u32>(),
+                                                                    B->kid.as<u32>(), lb.as<u64>(),
+                                                                    static_cast<u32>(B->layer_begin.size()), tp, tp + count);
+        B2_CUDA(cudaGetLastError());
+        B2_CUDA(cudaMemcpyAsync(parent, tp, count * 4, cudaMemcpyDeviceToHost, B->stream));
+        B2_CUDA(cudaMemcpyAsync(index, tp + count, count * 4, cudaMemcpyDeviceToHost, B->stream));
+        B2_CUDA(cudaStreamSynchronize(B->stream));
+    });
+}
+
+void b2_brfs_destroy(b2_brfs* search)
+{
+    if (!search)
+        return;
+    if (search->stream)
+    {
+        cudaStreamSynchronize(search->stream);
+        if (search->own_stream)
+            cudaStreamDestroy(search->stream);
+    }
+    delete search;
+}
+
+}  // extern "C"

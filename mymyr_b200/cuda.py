@@ -1,0 +1,164 @@
+"""Device searches: ``brfs`` mirrors mymyr.cuda.brfs (python/src/cuda_bindings.cpp:2715-2745 in maichmueller/mymyr) and
+returns a result with the fields of BrfsResult and DeviceBrfsStats; ``hash_rows`` mirrors mymyr.hash_rows
+(python/src/module.cpp:187)."""
+
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from . import _lib
+from ._lib import check, lib
+from .task import Context, Task
+
+STATUS = {0: "solved", 1: "exhausted", 2: "out_of_states", 3: "unsolvable"}
+
+
+@dataclass
+class DeviceBrfsStats:
+    """Per-phase device times (with timings=True) and table facts (cuda::DeviceBrfsStats)."""
+
+    count_ms: float = 0.0
+    gen_ms: float = 0.0
+    dedup_ms: float = 0.0
+    rehashes: int = 0
+    table_slots: int = 0
+    kernel_launches: int = 0
+
+
+@dataclass
+class BrfsResult:
+    status: str
+    states: int
+    expanded: int
+    generated: int
+    num_goal_states: int
+    layers: int
+    layer_counts: list
+    exhausted: bool
+    solved: bool
+    goal_id: int
+    fingerprint: int
+    search_s: float
+    words: int
+    stats: DeviceBrfsStats = field(default_factory=DeviceBrfsStats)
+    store: str = "device"
+    _search: object = None
+
+    def state_rows(self, first: int = 0, count: int | None = None) -> np.ndarray:
+        """State rows in id order (DeviceBrfs::states), [count, words] uint64."""
+        return self._search.states(first, count)
+
+    def nodes(self, first: int = 0, count: int | None = None):
+        """Node records (parent id, successor index) of states [first, first + count) (DeviceBrfs::nodes)."""
+        return self._search.nodes(first, count)
+
+    def state_hashes(self, first: int = 0, count: int | None = None) -> np.ndarray:
+        """hash::state of every stored state, in id order."""
+        return self._search.hashes(first, count)
+
+
+class _Search:
+    def __init__(self, task: Task, opts: _lib.BrfsOptions):
+        self.task = task
+        h = C.c_void_p()
+        check(lib().b2_brfs_create(task.handle, C.byref(opts), C.byref(h)))
+        self._h = h
+        self.n = 0
+
+    def run(self, layer_cap: int = 4096) -> _lib.BrfsResult:
+        lc = np.zeros((layer_cap, 3), np.uint64)
+        r = _lib.BrfsResult()
+        r.layer_counts = lc.ctypes.data_as(C.POINTER(C.c_uint64))
+        r.layer_capacity = layer_cap
+        check(lib().b2_brfs_run(self._h, C.byref(r)))
+        self.n = r.states
+        self.lc = lc[: min(r.layers, layer_cap)]
+        return r
+
+    def _range(self, first, count):
+        if count is None:
+            count = self.n - first
+        return first, count
+
+    def states(self, first=0, count=None):
+        first, count = self._range(first, count)
+        out = np.zeros((count, self.task.words), np.uint64)
+        check(lib().b2_brfs_states(self._h, first, count, out.ctypes.data, self.task.words))
+        return out
+
+    def nodes(self, first=0, count=None):
+        first, count = self._range(first, count)
+        p = np.zeros(count, np.uint32)
+        k = np.zeros(count, np.uint32)
+        check(lib().b2_brfs_nodes(self._h, first, count, p.ctypes.data, k.ctypes.data))
+        return p, k
+
+    def hashes(self, first=0, count=None):
+        first, count = self._range(first, count)
+        out = np.zeros(count, np.uint64)
+        check(lib().b2_brfs_state_hashes(self._h, first, count, out.ctypes.data))
+        return out
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value and _lib._lib is not None:
+            _lib._lib.b2_brfs_destroy(h)
+            self._h = None
+
+
+def brfs(task: Task, ctx: Context | None = None, witness_pruning: bool = True, canonical_order: bool = True,
+         max_states: int | None = None, stop_at_goal: bool = True, fingerprint: bool = False,
+         chunk_states: int | None = None, expected_states: int | None = None, max_depth: int | None = None,
+         timings: bool = False, stream=None) -> BrfsResult:
+    """The device BrFS (cuda::brfs). Ids, per-layer counts and the fingerprint equal the reference CPU BrFS with
+    deterministic ids. ``chunk_states`` is accepted for signature compatibility: layers are never chunked here, and
+    ids do not depend on it."""
+    if not canonical_order:
+        raise ValueError("mymyr_b200 brfs: canonical_order=False is not supported (ids are defined in canonical order)")
+    if ctx is not None and task.ctx is not None and ctx.device != task.ctx.device:
+        raise ValueError("mymyr_b200 brfs: the task lives on another device than ctx")
+    o = _lib.BrfsOptions()
+    lib().b2_brfs_options_default(C.byref(o))
+    o.witness_pruning = int(bool(witness_pruning))
+    o.stop_at_goal = int(bool(stop_at_goal))
+    o.fingerprint = int(bool(fingerprint))
+    o.timings = int(bool(timings))
+    if max_depth is not None:
+        o.max_depth = int(max_depth)
+    if max_states is not None:
+        o.max_states = int(max_states)
+    if expected_states is not None:
+        o.expected_states = int(expected_states)
+    if stream is not None:
+        o.stream = stream
+    s = _Search(task, o)
+    r = s.run()
+    res = BrfsResult(status=STATUS.get(r.status, str(r.status)), states=r.states, expanded=r.expanded,
+                     generated=r.generated, num_goal_states=r.num_goal_states, layers=r.layers,
+                     layer_counts=[tuple(int(x) for x in row) for row in s.lc], exhausted=bool(r.exhausted),
+                     solved=bool(r.solved), goal_id=r.goal_id, fingerprint=r.fingerprint, search_s=r.search_s,
+                     words=r.words,
+                     stats=DeviceBrfsStats(r.count_ms, r.gen_ms, r.dedup_ms, r.rehashes, 1 << r.table_log2,
+                                           r.kernel_launches), _search=s)
+    return res
+
+
+def hash_rows(states, *, numeric_words: int = 0, stream=None, ctx: Context | None = None):
+    """hash::state of each row of a CUDA uint64/int64 tensor [N, W] -> [N] (same dtype)."""
+    import torch
+
+    from .task import default_context
+
+    if numeric_words:
+        raise ValueError("mymyr_b200 hash_rows: numeric words are not supported")
+    if not states.is_cuda or states.dim() != 2 or states.element_size() != 8:
+        raise ValueError("hash_rows: states must be a CUDA [N, W] tensor of 64-bit words")
+    states = states.contiguous()
+    ctx = ctx or default_context(states.device.index)
+    out = torch.empty(states.shape[0], dtype=states.dtype, device=states.device)
+    st = stream if stream is not None else torch.cuda.current_stream(states.device).cuda_stream
+    check(lib().b2_hash_rows(ctx.handle, states.data_ptr(), states.shape[0], states.shape[1], out.data_ptr(), st))
+    return out

@@ -1,0 +1,132 @@
+"""CPU tests (no GPU): the C-ABI library loads and exports every declared entry point; the host task compiler's atom
+layout equals the reference's dense layout; the oracle reproduces the reference's golden vectors; generators are
+deterministic."""
+
+import hashlib
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from mymyr_b200 import _lib, tasks
+from mymyr_b200.task import Task
+
+ROOT = Path(__file__).resolve().parent.parent
+REF_TASKS = Path("/root/reference/tests/data/tasks")
+
+
+def declared_symbols():
+    text = (ROOT / "include" / "mymyr_b200.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(b2_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    L = _lib.lib()
+    names = declared_symbols()
+    assert len(names) >= 20
+    for n in names:
+        assert hasattr(L, n), n
+    assert set(names) == set(_lib.SIGNATURES), set(names) ^ set(_lib.SIGNATURES)
+    assert b"sm_100a" in L.b2_version()
+
+
+def test_errors_cross_the_abi_as_status_codes():
+    with pytest.raises(RuntimeError, match="task text"):
+        Task.from_text("O 2\nP 1\nF 1 p\nSI 0\nFI 1\n0 5\n", host_only=True)  # object out of range
+    with pytest.raises(ValueError, match="does not support|does not run"):
+        Task.from_text("O 1\nP 1\nD 1 p\nSI 0\nFI 0\nG 0\nA 0\n", host_only=True)
+
+
+GENERATED = {
+    "tower7": lambda: tasks.tower(7, 0),
+    "tower5_s3": lambda: tasks.tower(5, 3),
+    "transport": lambda: tasks.transport(2, 40, 2, 0),
+    "transport_3_4_1": lambda: tasks.transport(3, 4, 1, 2),
+    "tile4x4": lambda: tasks.sliding_tile(4, 4, 60, 0),
+    "tile3x3": lambda: tasks.sliding_tile(3, 3, 40, 5),
+    "random0": lambda: tasks.random_domain(0),
+    "random1": lambda: tasks.random_domain(1),
+}
+
+
+def test_generators_are_deterministic_and_pinned():
+    digests = {k: hashlib.sha256(f().encode()).hexdigest()[:16] for k, f in GENERATED.items()}
+    again = {k: hashlib.sha256(f().encode()).hexdigest()[:16] for k, f in GENERATED.items()}
+    assert digests == again
+    pinned = (ROOT / "tests" / "golden" / "task_digests.txt")
+    want = dict(line.split() for line in pinned.read_text().splitlines() if line.strip())
+    assert digests == want
+
+
+def test_bench_config_shapes():
+    t = Task.from_text(tasks.sliding_tile(4, 4, 60, 0), host_only=True)
+    assert (t.words, t.fluent_slots, t.num_objects) == (4, 256, 31)
+    t = Task.from_text(tasks.tower(7, 0), host_only=True)
+    assert (t.words, t.fluent_slots) == (2, 71)
+    t = Task.from_text(tasks.transport(2, 40, 2, 0), host_only=True)
+    assert (t.words, t.fluent_slots) == (3, 164)
+
+
+@pytest.mark.parametrize("name", sorted(GENERATED))
+def test_layout_matches_reference_dense(ref, name):
+    text = GENERATED[name]()
+    rt = ref.RefTask(text, atoms="dense")
+    t = Task.from_text(text, host_only=True)
+    assert (t.words, t.fluent_slots) == (rt.words, rt.fluent_slots)
+    assert np.array_equal(t.initial_state(), rt.initial_state())
+
+
+def _suite_texts():
+    if not REF_TASKS.exists():
+        return []
+    return sorted(REF_TASKS.glob("*.txt"))
+
+
+@pytest.mark.parametrize("path", _suite_texts(), ids=lambda p: p.stem)
+def test_layout_matches_reference_on_suite(ref, path):
+    """The reference's own task fixtures (read in place; not copied): dense layouts agree wherever the device path
+    accepts the task."""
+    text = path.read_text()
+    try:
+        t = Task.from_text(text, host_only=True)
+    except ValueError as e:
+        pytest.skip(f"unsupported on the device path: {e}")
+    rt = ref.RefTask(text, atoms="dense")
+    assert (t.words, t.fluent_slots) == (rt.words, rt.fluent_slots)
+    assert np.array_equal(t.initial_state(), rt.initial_state())
+
+
+# golden counts of exhaustive BrFS (witness pruning on), tests/cpp/support/suite.hpp:31-54 of the reference
+SUITE_GOLDEN = {
+    "gripper__prob05": (376832, 2031616, 2),
+    "depot__p02": (40320, 376560, 9),
+    "pegsol-08-strips__p22": (99457, 189967, 2),
+    "philosophers__p03-phil4": (47938, 121820, 1),
+    "organic-synthesis-opt18-strips__p20": (41311, 52548, 24),
+    "openstacks-opt08-adl__p03": (97953, 548161, 6),
+}
+
+
+@pytest.mark.parametrize("name", sorted(SUITE_GOLDEN))
+def test_oracle_reproduces_suite_golden_counts(ref, name):
+    path = REF_TASKS / f"{name}.txt"
+    if not path.exists():
+        pytest.skip("reference fixtures absent")
+    r = ref.RefTask(path.read_text(), atoms="auto").brfs(threads=1, stop_at_goal=False)
+    assert (r["states"], r["generated"], r["num_goal_states"]) == SUITE_GOLDEN[name]
+
+
+def test_oracle_philox_known_answers(ref):
+    """Random123 philox4x32-10 known answers (tests/cpp/rl/test_env.cpp:167-194 of the reference)."""
+    import ctypes as C
+
+    kats = [((0, 0, 0, 0), (0, 0), (0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8)),
+            ((0xFFFFFFFF,) * 4, (0xFFFFFFFF,) * 2, (0x408F276D, 0x41C83B0E, 0xA20BC7C6, 0x6D5451FD)),
+            ((0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344), (0xA4093822, 0x299F31D0),
+             (0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1))]
+    out = np.zeros(4, np.uint32)
+    for ctr, key, want in kats:
+        ref.lib().ref_philox_block(*ctr, *key, out.ctypes.data)
+        assert tuple(int(x) for x in out) == want

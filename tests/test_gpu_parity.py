@@ -1,0 +1,250 @@
+"""Device path vs the reference's CPU path (oracle/_ref), bit for bit: BrFS states, ids, node records, per-layer
+counts and fingerprints; batched expand CSR (labels and successor hashes); env trajectories; row hashes.
+
+Mirrors the reference's device-vs-host tests (tests/cuda/test_device_brfs.cpp:131-360,
+tests/cuda/test_device_env.cpp:254-460 in maichmueller/mymyr)."""
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+from mymyr_b200 import cuda as b2cuda  # noqa: E402
+from mymyr_b200 import rl as b2rl  # noqa: E402
+from mymyr_b200 import tasks  # noqa: E402
+from mymyr_b200.task import Task  # noqa: E402
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _need_cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+
+
+def random_states(task_words: int, slots: int, n: int, density: float, seed: int) -> np.ndarray:
+    rng = np.random.default_rng(seed)
+    bits = rng.random((n, task_words * 64)) < density
+    bits[:, slots:] = False
+    out = np.zeros((n, task_words), np.uint64)
+    for w in range(task_words):
+        chunk = bits[:, w * 64:(w + 1) * 64].astype(np.uint64)
+        out[:, w] = (chunk << np.arange(64, dtype=np.uint64)).sum(axis=1, dtype=np.uint64)
+    return out
+
+
+def to_dev(a: np.ndarray):
+    return torch.from_numpy(a.view(np.int64)).cuda()
+
+
+def as_u64(t):
+    return t.cpu().numpy().view(np.uint64)
+
+
+# ------------------------------------------------------------------------------------------------ hashing
+
+def test_hash_rows_match_reference(ref):
+    for W in (1, 2, 3, 4, 7, 13):
+        rows = np.random.default_rng(W).integers(0, 2**63, (257, W), dtype=np.int64).view(np.uint64)
+        rows[::3, W // 2:] = 0  # trimmed widths
+        rows[5] = 0
+        got = as_u64(b2cuda.hash_rows(to_dev(rows)))
+        want = np.array([ref.hash_state(r) for r in rows], np.uint64)
+        assert np.array_equal(got, want)
+
+
+# ------------------------------------------------------------------------------------------------ BrFS
+
+BRFS_CASES = [
+    ("tower7", lambda: tasks.tower(7, 0), None),
+    ("tower5_seed3", lambda: tasks.tower(5, 3), None),
+    ("transport_2_6_2", lambda: tasks.transport(2, 6, 2, 1), None),
+    ("transport_3_4_1", lambda: tasks.transport(3, 4, 1, 2), None),
+    ("tile3x3", lambda: tasks.sliding_tile(3, 3, 40, 5), None),
+    ("tile4x4_d12", lambda: tasks.sliding_tile(4, 4, 60, 0), 12),
+]
+
+
+@pytest.mark.parametrize("name,make,depth", BRFS_CASES, ids=[c[0] for c in BRFS_CASES])
+@pytest.mark.parametrize("witness", [True, False])
+def test_brfs_matches_reference(ref, name, make, depth, witness):
+    text = make()
+    rt = ref.RefTask(text)
+    t = Task.from_text(text)
+    want = rt.brfs(threads=1, max_depth=depth, stop_at_goal=False, witness_pruning=witness, fingerprint=True)
+    got = b2cuda.brfs(t, max_depth=depth, stop_at_goal=False, witness_pruning=witness, fingerprint=True)
+    assert got.states == want["states"]
+    assert got.expanded == want["expanded"]
+    assert got.generated == want["generated"]
+    assert got.num_goal_states == want["num_goal_states"]
+    assert got.layers == want["layers"]
+    assert got.layer_counts == want["layer_counts"]
+    assert got.exhausted == bool(want["exhausted"])
+    assert got.solved == bool(want["solved"])
+    assert got.fingerprint == want["fingerprint"]
+    # the stored states, ids and node records, in id order
+    rows, par, idx = rt.brfs_states(max_depth=depth, witness_pruning=witness)
+    assert np.array_equal(got.state_rows(), rows)
+    p, k = got.nodes()
+    assert np.array_equal(p, par)
+    assert np.array_equal(k, idx)
+    hs = got.state_hashes()
+    assert len(hs) == len(rows)
+    assert np.array_equal(hs[:500], np.array([ref.hash_state(r) for r in rows[:500]], np.uint64))
+
+
+@pytest.mark.parametrize("make", [lambda: tasks.tower(7, 0), lambda: tasks.sliding_tile(3, 3, 30, 1),
+                                  lambda: tasks.transport(2, 5, 2, 4)])
+def test_brfs_stop_at_goal_matches_reference(ref, make):
+    text = make()
+    rt = ref.RefTask(text)
+    want = rt.brfs(threads=1, stop_at_goal=True, fingerprint=True)
+    got = b2cuda.brfs(Task.from_text(text), stop_at_goal=True, fingerprint=True)
+    for key in ("states", "expanded", "generated", "num_goal_states", "layers", "fingerprint"):
+        assert getattr(got, key) == want[key], key
+    assert got.solved == bool(want["solved"])
+    assert got.layer_counts == want["layer_counts"]
+
+
+def test_brfs_deterministic_across_runs():
+    t = Task.from_text(tasks.sliding_tile(4, 4, 60, 7))
+    a = b2cuda.brfs(t, max_depth=13, stop_at_goal=False, fingerprint=True)
+    b = b2cuda.brfs(t, max_depth=13, stop_at_goal=False, fingerprint=True, expected_states=1 << 20)
+    assert a.fingerprint == b.fingerprint and a.layer_counts == b.layer_counts
+    assert b.stats.rehashes == 0 and a.stats.rehashes > 0  # growth does not change ids
+
+
+@pytest.mark.slow
+def test_brfs_tile_depth22_full_config(ref):
+    """BASELINE config [3] at full size: per-layer counts and fingerprint against the reference's multi-threaded BrFS
+    (deterministic ids)."""
+    import os
+
+    text = tasks.sliding_tile(4, 4, 60, 0)
+    want = ref.RefTask(text).brfs(threads=os.cpu_count() or 8, max_depth=22, stop_at_goal=False, fingerprint=True,
+                                  store="concurrent")
+    got = b2cuda.brfs(Task.from_text(text), max_depth=22, stop_at_goal=False, fingerprint=True)
+    assert got.layer_counts == want["layer_counts"]
+    assert got.states == want["states"] and got.generated == want["generated"]
+    assert got.fingerprint == want["fingerprint"]
+
+
+# ------------------------------------------------------------------------------------------------ expand
+
+EXPAND_CASES = [
+    ("random", lambda: tasks.random_domain(0), 1024, 0.05),
+    ("random_seed1", lambda: tasks.random_domain(1), 512, 0.08),
+    ("tower7", lambda: tasks.tower(7, 0), 2048, 0.2),
+    ("transport", lambda: tasks.transport(2, 40, 2, 0), 2048, 0.3),
+    ("tile4x4", lambda: tasks.sliding_tile(4, 4, 60, 0), 2048, 0.1),
+]
+
+
+@pytest.mark.parametrize("name,make,n,density", EXPAND_CASES, ids=[c[0] for c in EXPAND_CASES])
+@pytest.mark.parametrize("witness", [False, True])
+def test_expand_matches_reference(ref, name, make, n, density, witness):
+    text = make()
+    rt = ref.RefTask(text)
+    t = Task.from_text(text)
+    states = random_states(t.words, t.fluent_slots, n, density, seed=hash(name) & 0xFFFF)
+    states[0] = t.initial_state()
+    want = rt.expand(states, witness_pruning=witness, succ=True)
+    got = b2rl.expand(t, to_dev(states), witness_pruning=witness, succ=True)
+    assert got.generated == want["generated"]
+    assert np.array_equal(got.offsets.cpu().numpy(), want["offsets"])
+    assert np.array_equal(got.parent.cpu().numpy(), want["parent"])
+    assert np.array_equal(got.schema.cpu().numpy(), want["schema"])
+    lw = want["binding"].shape[1]
+    assert np.array_equal(got.binding.cpu().numpy()[:, :lw], want["binding"])
+    assert np.array_equal(as_u64(got.succ_hash), want["succ_hash"])
+    assert np.array_equal(as_u64(got.succ), want["succ"])
+
+
+def test_expand_empty_batch():
+    t = Task.from_text(tasks.tower(4, 0))
+    e = b2rl.expand(t, torch.zeros((0, t.words), dtype=torch.int64, device="cuda"))
+    assert e.generated == 0 and e.offsets.tolist() == [0]
+
+
+# ------------------------------------------------------------------------------------------------ env
+
+def _compare_env(env, renv):
+    assert np.array_equal(as_u64(env.states), renv.states)
+    assert np.array_equal(env.steps.cpu().numpy(), renv.steps)
+    assert np.array_equal(as_u64(env.draws), renv.draws)
+    assert np.array_equal(env.at_goal.cpu().numpy(), renv.at_goal)
+    assert np.array_equal(env.count.cpu().numpy(), renv.count)
+
+
+ENV_CASES = [
+    ("transport", lambda: tasks.transport(2, 40, 2, 0), dict()),
+    ("transport_small_trunc", lambda: tasks.transport(2, 3, 2, 1), dict(max_steps=17, step_reward=-0.5)),
+    ("tower5", lambda: tasks.tower(5, 2), dict(goal_reward=2.5)),
+    ("tile3x3", lambda: tasks.sliding_tile(3, 3, 10, 3), dict(max_steps=40)),
+]
+
+
+@pytest.mark.parametrize("name,make,cfg", ENV_CASES, ids=[c[0] for c in ENV_CASES])
+def test_env_trajectories_match_reference(ref, name, make, cfg):
+    text = make()
+    rt = ref.RefTask(text)
+    t = Task.from_text(text)
+    n, steps = 512, 120
+    env = b2rl.BatchedEnv(t, n, seed=1234, first_env=7, **cfg)
+    renv = ref.RefEnv(rt, n, seed=1234, first_env=7, **cfg)
+    env.reset()
+    renv.reset()
+    _compare_env(env, renv)
+    lw = renv.lw
+    for s in range(steps):
+        env.step()
+        renv.step()
+        torch.cuda.synchronize()
+        _compare_env(env, renv)
+        assert np.array_equal(env.reward.cpu().numpy(), renv.reward), s
+        assert np.array_equal(env.terminated.cpu().numpy(), renv.terminated), s
+        assert np.array_equal(env.truncated.cpu().numpy(), renv.truncated), s
+        assert np.array_equal(env.goal.cpu().numpy(), renv.goal), s
+        assert np.array_equal(env.invalid.cpu().numpy(), renv.invalid), s
+        assert np.array_equal(env.schema.cpu().numpy(), renv.schema), s
+        assert np.array_equal(env.binding.cpu().numpy()[:, :lw], renv.binding), s
+        assert np.array_equal(as_u64(env.final_states), renv.final_states), s
+
+
+def test_env_given_actions_match_reference(ref):
+    text = tasks.transport(2, 4, 2, 3)
+    rt = ref.RefTask(text)
+    t = Task.from_text(text)
+    n = 300
+    env = b2rl.BatchedEnv(t, n, seed=5)
+    renv = ref.RefEnv(rt, n, seed=5)
+    env.reset()
+    renv.reset()
+    rng = np.random.default_rng(0)
+    for s in range(60):
+        a = rng.integers(-2, 12, n).astype(np.int64)  # out-of-range indices are invalid moves
+        env.step(torch.from_numpy(a).cuda())
+        renv.step(a)
+        _compare_env(env, renv)
+        assert np.array_equal(env.invalid.cpu().numpy(), renv.invalid)
+        assert np.array_equal(env.reward.cpu().numpy(), renv.reward)
+
+
+@pytest.mark.slow
+def test_env_full_config_digest(ref):
+    """BASELINE config [2] at its batch size (65,536 envs): states and counters after 50 steps, compared in full."""
+    import os
+
+    text = tasks.transport(2, 40, 2, 0)
+    rt = ref.RefTask(text)
+    t = Task.from_text(text)
+    n = 65536
+    env = b2rl.BatchedEnv(t, n, seed=0)
+    renv = ref.RefEnv(rt, n, seed=0, threads=os.cpu_count() or 8)
+    env.reset()
+    renv.reset()
+    for _ in range(50):
+        env.step()
+        renv.step()
+    _compare_env(env, renv)
