@@ -40,6 +40,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--env-steps", type=int, default=200)
     ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--depth", type=int, default=DEPTH, help="BrFS depth (profiling runs use a smaller case)")
+    ap.add_argument("--quick", action="store_true", help="timed BrFS only: no e2e, CPU baseline or env leg")
     return ap.parse_args()
 
 
@@ -223,7 +225,7 @@ def main():
     sp = stream.cuda_stream
 
     def one(expected=None):
-        return b2cuda.brfs(task, max_depth=DEPTH, stop_at_goal=False, timings=True, expected_states=expected,
+        return b2cuda.brfs(task, max_depth=args.depth, stop_at_goal=False, timings=True, expected_states=expected,
                            stream=sp)
 
     r = one()
@@ -264,6 +266,14 @@ def main():
     achieved = bytes_run / (kern_ms / 1000.0) / 1e9
     launches = sum(r.stats.kernel_launches for r in results)
 
+    if args.quick:
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                              "depth": args.depth, "ms_per_step": ms / args.steps, "roofline_achieved": achieved,
+                              "frac": achieved / peak, "quick": True}), flush=True)
+        if pg is not None:
+            pg.destroy_process_group()
+        return
     # ---------------------------------------------------------------- end to end through the public API
     barrier()
     e2e_times = []
@@ -272,7 +282,7 @@ def main():
     for _ in range(args.steps):
         t0 = time.perf_counter()
         t2 = Task.from_text(text, ctx)
-        rr = b2cuda.brfs(t2, max_depth=DEPTH, stop_at_goal=False, expected_states=expected, stream=sp)
+        rr = b2cuda.brfs(t2, max_depth=args.depth, stop_at_goal=False, expected_states=expected, stream=sp)
         hashes = rr.state_hashes()
         e2e_times.append(time.perf_counter() - t0)
         d2h = hashes.nbytes + 24 * rr.layers

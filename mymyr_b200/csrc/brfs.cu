@@ -18,7 +18,8 @@
 // index) discoverer keys (src/mymyr/search/brfs.cpp:1657-1778).
 //
 // Per layer: k_count (goal test + successor counts per parent) -> scan (candidate offsets) -> host reads the layer's
-// candidate count -> k_expand (regenerate, hash, insert) -> scan of winners (ids) -> host reads the new-state count.
+// candidate count -> k_expand (regenerate, hash, optimistic insert) -> k_resolve (deferred inserts) -> scan of winners
+// (ids) -> host reads the new-state count.
 
 #include "scan.cuh"
 
@@ -38,15 +39,8 @@ struct LayerMisc
     u32 goals;       // goal states among the layer's parents
     u32 first_goal;  // smallest parent index that is a goal (0xFFFFFFFF: none)
     u32 status;
-    u32 pad;
+    u32 ndeferred;   // inserts left to the resolve pass
 };
-
-__device__ __forceinline__ u64 ld_acquire(const u64* p)
-{
-    u64 v;
-    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
 
 struct Store
 {
@@ -62,36 +56,36 @@ struct Store
     u8* lost;
     u64 layer_cand_begin;
     u32* status;
+    uint2* deferred;  // (candidate g, slot) of inserts left to the resolve pass
+    u32* ndeferred;
 };
 
-/// Inserts candidate g (row `s`, hash h) of parent i, successor index k.
+/// Phase A of an insert, with no fence and no acquire: the candidate's row is read by other threads only in the
+/// resolve pass (a later kernel), so plain stores suffice. A slot holding a state of an earlier layer is compared in
+/// place (its row was written by an earlier kernel); an empty slot is claimed by CAS; a slot holding a candidate of
+/// this layer with the same tag defers the insert (row, hash and node record written first) to the resolve pass.
 template<class Row>
 __device__ __forceinline__ void insert(const Store& S, const Row& s, u64 h, u64 g, u32 i, u32 k)
 {
     const u64 mine = (h & 0xFFFFFFFF00000000ull) | g;
     u64 j = h & S.mask;
-    bool written = false;
     auto write_row = [&]() {
-        if (written)
-            return;
         u64* r = S.rows + g * S.W;
         for (u32 w = 0; w < S.W; ++w)
             r[w] = s.word(w);
         S.hash[g] = h;
         S.par[g] = i;
         S.kid[g] = k;
-        __threadfence();
-        written = true;
     };
     for (u32 probe = 0; probe < S.max_probe; ++probe, j = (j + 1) & S.mask)
     {
-        u64 cur = ld_acquire(S.table + j);
+        u64 cur = __ldcg(S.table + j);
         if (cur == kEmpty)
         {
-            write_row();
             const u64 prev = atomicCAS(reinterpret_cast<unsigned long long*>(S.table + j), kEmpty, mine);
             if (prev == kEmpty)
             {
+                write_row();
                 S.claimed[g - S.layer_cand_begin] = 1;
                 return;
             }
@@ -100,24 +94,74 @@ __device__ __forceinline__ void insert(const Store& S, const Row& s, u64 h, u64 
         if ((cur >> 32) != (mine >> 32))
             continue;
         const u64 og = cur & 0xFFFFFFFFull;
+        if (og >= S.layer_cand_begin)
+        {
+            write_row();
+            const u32 q = atomicAdd(S.ndeferred, 1u);
+            S.deferred[q] = make_uint2(static_cast<u32>(g), static_cast<u32>(j));
+            return;
+        }
         const u64* r = S.rows + og * S.W;
         bool eq = true;
         for (u32 w = 0; w < S.W && eq; ++w)
             eq = __ldcg(r + w) == s.word(w);
-        if (!eq)
-            continue;
-        if (og < g)
-            return;  // an earlier discovery of the same state
-        write_row();
-        const u64 prev = atomicMin(reinterpret_cast<unsigned long long*>(S.table + j), mine);
-        if (prev > mine)
-        {
-            S.claimed[g - S.layer_cand_begin] = 1;
-            S.lost[(prev & 0xFFFFFFFFull) - S.layer_cand_begin] = 1;
-        }
-        return;
+        if (eq)
+            return;  // a state of an earlier layer
     }
     atomicOr(S.status, kStatusProbeLimit);
+}
+
+/// Phase B: the deferred inserts, resumed at their slots. Every row they can meet was written by the expansion
+/// kernel (or an earlier one), so the comparisons need no ordering within this kernel. Among equal candidates of the
+/// layer the smallest g takes the slot by atomicMin (the tag sits above g); a displaced one is marked lost.
+__global__ void k_resolve(Store S)
+{
+    const u32 n = *S.ndeferred;
+    for (u32 q = blockIdx.x * blockDim.x + threadIdx.x; q < n; q += gridDim.x * blockDim.x)
+    {
+        const uint2 d = S.deferred[q];
+        const u64 g = d.x;
+        const u64 h = S.hash[g];
+        const u64 mine = (h & 0xFFFFFFFF00000000ull) | g;
+        const u64* row = S.rows + g * S.W;
+        u64 j = d.y;
+        bool done = false;
+        for (u32 probe = 0; probe < S.max_probe && !done; ++probe, j = (j + 1) & S.mask)
+        {
+            u64 cur = __ldcg(S.table + j);
+            if (cur == kEmpty)
+            {
+                const u64 prev = atomicCAS(reinterpret_cast<unsigned long long*>(S.table + j), kEmpty, mine);
+                if (prev == kEmpty)
+                {
+                    S.claimed[g - S.layer_cand_begin] = 1;
+                    done = true;
+                    break;
+                }
+                cur = prev;
+            }
+            if ((cur >> 32) != (mine >> 32))
+                continue;
+            const u64 og = cur & 0xFFFFFFFFull;
+            const u64* r = S.rows + og * S.W;
+            bool eq = true;
+            for (u32 w = 0; w < S.W && eq; ++w)
+                eq = __ldcg(r + w) == __ldcg(row + w);
+            if (!eq)
+                continue;
+            done = true;
+            if (og < g)
+                break;  // an earlier discovery of the same state
+            const u64 prev = atomicMin(reinterpret_cast<unsigned long long*>(S.table + j), mine);
+            if (prev > mine)
+            {
+                S.claimed[g - S.layer_cand_begin] = 1;
+                S.lost[(prev & 0xFFFFFFFFull) - S.layer_cand_begin] = 1;
+            }
+        }
+        if (!done)
+            atomicOr(S.status, kStatusProbeLimit);
+    }
 }
 
 template<int OW, int WR>
@@ -160,19 +204,24 @@ __global__ void __launch_bounds__(128) k_expand(DevTask T, u32 pi, const u32* __
         {
             const DSchema& sc = T.schemas[s];
             enumerate<OW>(T, sc.prog[pi], st, bind, [&](const u32* b) {
-                Effects e;
-                collect_effects(T, sc, b, e);
                 if constexpr (WR > 0)
                 {
-                    RegRow<WR> nx;
-#pragma unroll
-                    for (int q = 0; q < WR; ++q)
-                        nx.w[q] = succ_word(st, e, q);
+                    RegRow<WR> nx = st;
+                    for (u32 q = sc.del_begin; q < sc.del_end; ++q)
+                    {
+                        const u64 key = pattern_key(T, T.lits[q], b);
+                        if (key < T.fluent_count)
+                            nx.clear(static_cast<u32>(key));
+                    }
+                    for (u32 q = sc.add_begin; q < sc.add_end; ++q)
+                        nx.set(static_cast<u32>(pattern_key(T, T.lits[q], b)));
                     const u64 h = hash_words([&](u32 q) { return nx.word(q); }, S.W);
                     insert(S, nx, h, g0 + k, static_cast<u32>(i), k);
                 }
                 else
                 {
+                    Effects e;
+                    collect_effects(T, sc, b, e);
                     const SuccRow<decltype(st)> nx{st, e};
                     const u64 h = hash_words([&](u32 q) { return nx.word(q); }, S.W);
                     insert(S, nx, h, g0 + k, static_cast<u32>(i), k);
@@ -330,7 +379,7 @@ struct b2_brfs
     u64 table_slots = 0;
     u32 rehashes = 0;
     // per layer scratch
-    DeviceBuffer counts, cand_base, flags, sums, misc;
+    DeviceBuffer counts, cand_base, flags, deferred, sums, misc;
     u64 cap_layer = 0, cap_flags = 0;
     // results
     std::vector<u64> layer_begin;  // id of each layer's first state (+ the end)
@@ -377,6 +426,7 @@ void ensure_layer(b2_brfs& B, u64 E, u64 G)
     {
         const u64 cap = std::max<u64>(G, B.cap_flags * 2);
         B.flags.alloc(cap * 2 + 16);
+        B.deferred.alloc(cap * sizeof(uint2));
         if (B.sums.bytes < scan_scratch_bytes(cap))
             B.sums.alloc(scan_scratch_bytes(cap));
         B.cap_flags = cap;
@@ -423,6 +473,8 @@ Store make_store(b2_brfs& B, u64 layer_cand_begin)
     S.lost = B.flags.as<u8>() + B.cap_flags;
     S.layer_cand_begin = layer_cand_begin;
     S.status = &B.misc.as<LayerMisc>()->status;
+    S.deferred = B.deferred.as<uint2>();
+    S.ndeferred = &B.misc.as<LayerMisc>()->ndeferred;
     return S;
 }
 
@@ -555,7 +607,9 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
             dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
                 k_expand<OW, WR><<<grid_e, 128, 0, s>>>(T, pi, frontier, E_exp, B.cand_base.as<u64>(), S);
             });
+            k_resolve<<<static_cast<unsigned>(B.task->ctx->sms) * 8, 256, 0, s>>>(S);
             B2_CUDA(cudaGetLastError());
+            ++B.launches;
             if (o.timings)
                 B2_CUDA(cudaEventRecord(ev[3], s));
             device_scan(WinIn{S.claimed, S.lost}, WinOut{B.state_g.as<u32>() + B.n_states, cand_next}, G,

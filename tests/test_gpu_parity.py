@@ -15,6 +15,7 @@ from mymyr_b200 import cuda as b2cuda  # noqa: E402
 from mymyr_b200 import rl as b2rl  # noqa: E402
 from mymyr_b200 import tasks  # noqa: E402
 from mymyr_b200.task import Task  # noqa: E402
+from mymyr_b200 import UnsupportedTask  # noqa: E402
 
 
 @pytest.fixture(scope="module", autouse=True)
@@ -150,6 +151,12 @@ def test_expand_matches_reference(ref, name, make, n, density, witness):
     states = random_states(t.words, t.fluent_slots, n, density, seed=hash(name) & 0xFFFF)
     states[0] = t.initial_state()
     want = rt.expand(states, witness_pruning=witness, succ=True)
+    if witness and name.startswith("random"):
+        # these schemas bind witness-only parameters before effect parameters; the device path refuses them under
+        # witness pruning rather than emit them out of canonical order
+        with pytest.raises(UnsupportedTask):
+            b2rl.expand(t, to_dev(states), witness_pruning=witness, succ=True)
+        return
     got = b2rl.expand(t, to_dev(states), witness_pruning=witness, succ=True)
     assert got.generated == want["generated"]
     assert np.array_equal(got.offsets.cpu().numpy(), want["offsets"])
