@@ -108,6 +108,23 @@ void b2_task_desc_free(b2_task_desc* desc);
 b2_status b2_task_create(b2_ctx* ctx, const b2_task_desc* desc, b2_task** out);
 void b2_task_destroy(b2_task* task);
 
+/* How the kernels match schema preconditions. COMPILED (the default): the task's matchers are generated as CUDA with
+ * every layout constant folded in and compiled for sm_100a at task creation (NVRTC, cached per process by program);
+ * INTERPRETED: generic kernels walk the task's matcher tables. Both enumerate the same bindings in the same order. */
+enum { B2_MATCHER_AUTO = 0, B2_MATCHER_INTERPRETED = 1, B2_MATCHER_COMPILED = 2 };
+
+typedef struct b2_task_options {
+    int32_t matcher; /* B2_MATCHER_* */
+} b2_task_options;
+
+/* b2_task_create with options (NULL: the defaults). */
+b2_status b2_task_create_ex(b2_ctx* ctx, const b2_task_desc* desc, const b2_task_options* options, b2_task** out);
+
+/* Compiles the task's kernels for sm_100a into the process cache without a device (a host-only task works). The
+ * generated source is copied into src (NUL-terminated, truncated to src_cap; src may be NULL) and its full length
+ * returned in *src_len (may be NULL). */
+b2_status b2_task_compile(const b2_task* task, char* src, size_t src_cap, size_t* src_len);
+
 typedef struct b2_task_info {
     uint32_t words;        /* Task::words(): u64 words of a state row */
     uint32_t fluent_slots; /* AtomIndex::fluent_slots() */

@@ -53,6 +53,13 @@ class TaskDesc(C.Structure):
                 ("goal_begin", C.c_uint32), ("goal_count", C.c_uint32), ("unsupported", C.c_uint32)]
 
 
+class TaskOptions(C.Structure):
+    _fields_ = [("matcher", C.c_int32)]
+
+
+MATCHER = {"auto": 0, "interpreted": 1, "compiled": 2}
+
+
 class TaskInfo(C.Structure):
     _fields_ = [("words", C.c_uint32), ("fluent_slots", C.c_uint32), ("num_schemas", C.c_uint32),
                 ("num_objects", C.c_uint32), ("label_width", C.c_uint32), ("object_words", C.c_uint32)]
@@ -112,6 +119,8 @@ SIGNATURES = {
     "b2_task_desc_free": (None, [C.POINTER(TaskDesc)]),
     "b2_task_create": (C.c_int, [P, C.POINTER(TaskDesc), PP]),
     "b2_task_destroy": (None, [P]),
+    "b2_task_create_ex": (C.c_int, [P, C.POINTER(TaskDesc), C.POINTER(TaskOptions), PP]),
+    "b2_task_compile": (C.c_int, [P, C.c_char_p, C.c_size_t, C.POINTER(C.c_size_t)]),
     "b2_task_info_get": (C.c_int, [P, C.POINTER(TaskInfo)]),
     "b2_task_initial_state": (C.c_int, [P, P, U32]),
     "b2_task_slot_atom": (C.c_int, [P, U32, P, U32]),

@@ -22,8 +22,12 @@ LIB_DIR = ROOT / "lib"
 LIB = LIB_DIR / "libmymyr_b200.so"
 OBJ_DIR = REPO / "_build" / "mymyr_b200"
 
-CU_SOURCES = ["api.cu", "scan.cu", "expand.cu", "brfs.cu", "env.cu"]
-CPP_SOURCES = ["compile.cpp"]
+CU_SOURCES = ["api.cu", "scan.cu", "expand.cu", "brfs.cu", "env.cu", "jit.cu"]
+CPP_SOURCES = ["compile.cpp", "codegen.cpp"]
+# device sources compiled at run time (NVRTC), embedded into the library as strings
+EMBEDDED = {"b2_jit_core_source": "core.cuh", "b2_jit_kernels_source": "jit_kernels.cuh"}
+CUDA_LIB = "/usr/local/cuda/lib64"
+# NVRTC is loaded with dlopen at the first compile (jit.cu); the library links only the static CUDA runtime
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -71,11 +75,22 @@ def build(verbose: bool = False, ptxas_verbose: bool = False) -> Path:
         objs.append(o)
         if _stale(o, [s] + headers):
             jobs.append(["g++", "-std=c++20", "-O2", "-fPIC", "-Wall", *inc, "-c", str(s), "-o", str(o)])
+    emb_src = OBJ_DIR / "jit_sources.cpp"
+    emb_obj = OBJ_DIR / "jit_sources.cpp.o"
+    objs.append(emb_obj)
+    if _stale(emb_obj, [CSRC / f for f in EMBEDDED.values()]):
+        parts = []
+        for sym, f in EMBEDDED.items():
+            text = (CSRC / f).read_text()
+            assert ")B2SRC" not in text
+            parts.append(f'extern "C" const char {sym}[] = R"B2SRC({text})B2SRC";\n')
+        emb_src.write_text("".join(parts))
+        jobs.append(["g++", "-std=c++20", "-O1", "-fPIC", "-c", str(emb_src), "-o", str(emb_obj)])
     with cf.ThreadPoolExecutor(max_workers=max(1, min(8, os.cpu_count() or 1))) as ex:
         list(ex.map(_run, jobs))
     if jobs or not LIB.exists():
         tmp = LIB.with_suffix(".so.tmp")
-        _run([nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", str(tmp), *map(str, objs)])
+        _run([nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", str(tmp), *map(str, objs), "-ldl"])
         tmp.replace(LIB)
     if verbose:
         print(f"built {LIB}")

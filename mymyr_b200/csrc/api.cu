@@ -1,6 +1,7 @@
 // C ABI: errors, contexts, task descriptions and upload, row hashing.
 
 #include "common.cuh"
+#include "jit.hpp"
 
 #include <cstring>
 #include <mutex>
@@ -293,9 +294,17 @@ void b2_task_desc_free(b2_task_desc* desc) { delete reinterpret_cast<DescHolder*
 
 b2_status b2_task_create(b2_ctx* ctx, const b2_task_desc* desc, b2_task** out)
 {
+    return b2_task_create_ex(ctx, desc, nullptr, out);
+}
+
+b2_status b2_task_create_ex(b2_ctx* ctx, const b2_task_desc* desc, const b2_task_options* options, b2_task** out)
+{
     return guarded([&] {
         if (!desc || !out)
             throw std::invalid_argument("b2_task_create: null argument");
+        const int32_t matcher = options ? options->matcher : B2_MATCHER_AUTO;
+        if (matcher < B2_MATCHER_AUTO || matcher > B2_MATCHER_COMPILED)
+            throw std::invalid_argument("b2_task_create: bad matcher option");
         if (ctx)
             B2_CUDA(cudaSetDevice(ctx->device));
         auto t = std::make_unique<b2_task>();
@@ -316,8 +325,30 @@ b2_status b2_task_create(b2_ctx* ctx, const b2_task_desc* desc, b2_task** out)
             if (s.add_end - s.add_begin > 16 || s.del_end - s.del_begin > 16)
                 throw Error(B2_UNSUPPORTED, "an action schema with more than 16 add or delete effects");
         if (ctx)
+        {
             upload(*t);  // a host-only task (ctx NULL) is compiled but cannot run kernels
+            if (matcher != B2_MATCHER_INTERPRETED)
+                t->jit = jit_module(ctx->device, t->prog);
+        }
         *out = t.release();
+    });
+}
+
+b2_status b2_task_compile(const b2_task* task, char* src, size_t src_cap, size_t* src_len)
+{
+    return guarded([&] {
+        if (!task)
+            throw std::invalid_argument("b2_task_compile: null task");
+        const std::string text = generate_matcher_source(task->prog);
+        jit_cubin(task->prog);
+        if (src && src_cap)
+        {
+            const size_t n = text.size() < src_cap - 1 ? text.size() : src_cap - 1;
+            std::memcpy(src, text.data(), n);
+            src[n] = 0;
+        }
+        if (src_len)
+            *src_len = text.size();
     });
 }
 

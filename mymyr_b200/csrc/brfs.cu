@@ -29,87 +29,10 @@ namespace b2
 {
 namespace
 {
-constexpr u64 kEmpty = ~u64{0};
-
-struct LayerMisc
-{
-    u64 total_cand;  // candidates of the layer (scan total)
-    u64 total_new;   // new states of the layer (scan total)
-    u64 fingerprint;
-    u32 goals;       // goal states among the layer's parents
-    u32 first_goal;  // smallest parent index that is a goal (0xFFFFFFFF: none)
-    u32 status;
-    u32 ndeferred;   // inserts left to the resolve pass
-};
-
-struct Store
-{
-    u64* rows;
-    u64* hash;
-    u32* par;
-    u32* kid;
-    u64* table;
-    u64 mask;
-    u32 W;
-    u32 max_probe;
-    u8* claimed;  // per layer candidate
-    u8* lost;
-    u64 layer_cand_begin;
-    u32* status;
-    uint2* deferred;  // (candidate g, slot) of inserts left to the resolve pass
-    u32* ndeferred;
-};
-
-/// Phase A of an insert, with no fence and no acquire: the candidate's row is read by other threads only in the
-/// resolve pass (a later kernel), so plain stores suffice. A slot holding a state of an earlier layer is compared in
-/// place (its row was written by an earlier kernel); an empty slot is claimed by CAS; a slot holding a candidate of
-/// this layer with the same tag defers the insert (row, hash and node record written first) to the resolve pass.
-template<class Row>
-__device__ __forceinline__ void insert(const Store& S, const Row& s, u64 h, u64 g, u32 i, u32 k)
-{
-    const u64 mine = (h & 0xFFFFFFFF00000000ull) | g;
-    u64 j = h & S.mask;
-    auto write_row = [&]() {
-        u64* r = S.rows + g * S.W;
-        for (u32 w = 0; w < S.W; ++w)
-            r[w] = s.word(w);
-        S.hash[g] = h;
-        S.par[g] = i;
-        S.kid[g] = k;
-    };
-    for (u32 probe = 0; probe < S.max_probe; ++probe, j = (j + 1) & S.mask)
-    {
-        u64 cur = __ldcg(S.table + j);
-        if (cur == kEmpty)
-        {
-            const u64 prev = atomicCAS(reinterpret_cast<unsigned long long*>(S.table + j), kEmpty, mine);
-            if (prev == kEmpty)
-            {
-                write_row();
-                S.claimed[g - S.layer_cand_begin] = 1;
-                return;
-            }
-            cur = prev;
-        }
-        if ((cur >> 32) != (mine >> 32))
-            continue;
-        const u64 og = cur & 0xFFFFFFFFull;
-        if (og >= S.layer_cand_begin)
-        {
-            write_row();
-            const u32 q = atomicAdd(S.ndeferred, 1u);
-            S.deferred[q] = make_uint2(static_cast<u32>(g), static_cast<u32>(j));
-            return;
-        }
-        const u64* r = S.rows + og * S.W;
-        bool eq = true;
-        for (u32 w = 0; w < S.W && eq; ++w)
-            eq = __ldcg(r + w) == s.word(w);
-        if (eq)
-            return;  // a state of an earlier layer
-    }
-    atomicOr(S.status, kStatusProbeLimit);
-}
+using dev::insert;
+using dev::kEmpty;
+using dev::LayerMisc;
+using dev::Store;
 
 /// Phase B: the deferred inserts, resumed at their slots. Every row they can meet was written by the expansion
 /// kernel (or an earlier one), so the comparisons need no ordering within this kernel. Among equal candidates of the
@@ -119,12 +42,12 @@ __global__ void k_resolve(Store S)
     const u32 n = *S.ndeferred;
     for (u32 q = blockIdx.x * blockDim.x + threadIdx.x; q < n; q += gridDim.x * blockDim.x)
     {
-        const uint2 d = S.deferred[q];
-        const u64 g = d.x;
+        const u64 d = S.deferred[q];
+        const u64 g = d & 0xFFFFFFFFull;
         const u64 h = S.hash[g];
         const u64 mine = (h & 0xFFFFFFFF00000000ull) | g;
         const u64* row = S.rows + g * S.W;
-        u64 j = d.y;
+        u64 j = d >> 32;
         bool done = false;
         for (u32 probe = 0; probe < S.max_probe && !done; ++probe, j = (j + 1) & S.mask)
         {
@@ -426,7 +349,7 @@ void ensure_layer(b2_brfs& B, u64 E, u64 G)
     {
         const u64 cap = std::max<u64>(G, B.cap_flags * 2);
         B.flags.alloc(cap * 2 + 16);
-        B.deferred.alloc(cap * sizeof(uint2));
+        B.deferred.alloc(cap * sizeof(u64));
         if (B.sums.bytes < scan_scratch_bytes(cap))
             B.sums.alloc(scan_scratch_bytes(cap));
         B.cap_flags = cap;
@@ -473,7 +396,7 @@ Store make_store(b2_brfs& B, u64 layer_cand_begin)
     S.lost = B.flags.as<u8>() + B.cap_flags;
     S.layer_cand_begin = layer_cand_begin;
     S.status = &B.misc.as<LayerMisc>()->status;
-    S.deferred = B.deferred.as<uint2>();
+    S.deferred = B.deferred.as<u64>();
     S.ndeferred = &B.misc.as<LayerMisc>()->ndeferred;
     return S;
 }
@@ -559,9 +482,21 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
         const unsigned grid = grid_for(E, 128, static_cast<unsigned>(B.task->ctx->sms) * 64);
         if (o.timings)
             B2_CUDA(cudaEventRecord(ev[0], s));
-        dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
-            k_count<OW, WR><<<grid, 128, 0, s>>>(T, pi, B.rows.as<u64>(), W, frontier, E, B.counts.as<u32>(), misc);
-        });
+        if (B.task->jit)
+        {
+            dev::BrfsArgs a{};
+            a.frontier = frontier;
+            a.E = E;
+            a.counts = B.counts.as<u32>();
+            a.misc = misc;
+            a.S = make_store(B, cand_next);
+            a.pi = pi;
+            jit_launch(B.task->jit->brfs_count[pi], grid, 128, &a, s);
+        }
+        else
+            dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
+                k_count<OW, WR><<<grid, 128, 0, s>>>(T, pi, B.rows.as<u64>(), W, frontier, E, B.counts.as<u32>(), misc);
+            });
         device_scan(CountIn{B.counts.as<u32>()}, BaseOut{B.cand_base.as<u64>()}, E, &misc->total_cand, B.sums.as<u64>(), s);
         B.launches += 4;
         if (o.timings)
@@ -604,9 +539,21 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
             const Store S = make_store(B, cand_next);
             frontier = B.state_g.as<u32>() + layer_begin;
             const unsigned grid_e = grid_for(E_exp, 128, static_cast<unsigned>(B.task->ctx->sms) * 64);
-            dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
-                k_expand<OW, WR><<<grid_e, 128, 0, s>>>(T, pi, frontier, E_exp, B.cand_base.as<u64>(), S);
-            });
+            if (B.task->jit)
+            {
+                dev::BrfsArgs a{};
+                a.frontier = frontier;
+                a.E = E_exp;
+                a.cand_base = B.cand_base.as<u64>();
+                a.misc = misc;
+                a.S = S;
+                a.pi = pi;
+                jit_launch(B.task->jit->brfs_expand[pi], grid_e, 128, &a, s);
+            }
+            else
+                dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
+                    k_expand<OW, WR><<<grid_e, 128, 0, s>>>(T, pi, frontier, E_exp, B.cand_base.as<u64>(), S);
+                });
             k_resolve<<<static_cast<unsigned>(B.task->ctx->sms) * 8, 256, 0, s>>>(S);
             B2_CUDA(cudaGetLastError());
             ++B.launches;

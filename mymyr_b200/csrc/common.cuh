@@ -5,6 +5,7 @@
 #pragma once
 
 #include "device.cuh"
+#include "jit.hpp"
 #include "mymyr_b200.h"
 
 #include <cuda_runtime.h>
@@ -147,6 +148,7 @@ struct b2_task
     b2::DeviceBuffer blob;
     b2::DevTask dev{};
     bool witness_refused = false;  // some schema cannot keep canonical order under witness pruning
+    std::shared_ptr<b2::JitModule> jit;  // the compiled kernels (null: the interpreted ones)
 };
 
 namespace b2

@@ -1,0 +1,350 @@
+// Device primitives shared by the nvcc-compiled kernels and the per-task kernels compiled at run time (NVRTC): scalar
+// types, the reference's state hash and Philox RNG (bit-exact restatements), register rows, bit extraction, the
+// hash-set insert protocol of the BrFS, and the kernel argument blocks. Self-contained: no standard headers, so that
+// NVRTC compiles it as is.
+
+#pragma once
+
+#if defined(__CUDACC_RTC__)
+typedef unsigned char u8_t;
+typedef unsigned int u32_t;
+typedef unsigned long long u64_t;
+typedef int i32_t;
+typedef long long i64_t;
+#else
+#include <cstdint>
+typedef std::uint8_t u8_t;
+typedef std::uint32_t u32_t;
+typedef std::uint64_t u64_t;
+typedef std::int32_t i32_t;
+typedef std::int64_t i64_t;
+#endif
+
+namespace b2
+{
+namespace dev
+{
+using u8 = u8_t;
+using u32 = u32_t;
+using u64 = u64_t;
+using i32 = i32_t;
+using i64 = i64_t;
+
+#define B2_DI __device__ __forceinline__
+
+// ------------------------------------------------------------------------------------------------ hash
+// hash::mix64 / mulfold / words / state_words (include/mymyr/core/hash.hpp:12-55 of maichmueller/mymyr).
+constexpr u64 kHashSeed = 0x2d358dccaa6c78a5ULL;
+constexpr u64 kHashP1 = 0x8bb84b93962eacc9ULL;
+constexpr u64 kHashP2 = 0x4b33a62ed433d4a3ULL;
+
+B2_DI u64 mix64(u64 x)
+{
+    x ^= x >> 30;
+    x *= 0xbf58476d1ce4e5b9ULL;
+    x ^= x >> 27;
+    x *= 0x94d049bb133111ebULL;
+    x ^= x >> 31;
+    return x;
+}
+
+B2_DI u64 mulfold(u64 a, u64 b) { return (a * b) ^ __umul64hi(a, b); }
+
+/// hash::state_words over words w(0..W-1) of a zero-padded row (trailing zero words ignored).
+template<class Get>
+B2_DI u64 hash_words(Get&& w, u32 W)
+{
+    u32 n = W;
+    while (n > 0 && w(n - 1) == 0)
+        --n;
+    u64 h = kHashSeed ^ (static_cast<u64>(n) * kHashP1);
+    u32 i = 0;
+    for (; i + 1 < n; i += 2)
+        h = mulfold(h ^ w(i) ^ kHashP1, w(i + 1) ^ kHashP2);
+    if (i < n)
+        h = mulfold(h ^ w(i) ^ kHashP1, kHashP2);
+    return mix64(h);
+}
+
+/// brfs_fingerprint_term (src/mymyr/search/brfs.cpp:34-37).
+B2_DI u64 fingerprint_term(u64 id, u64 canonical) { return mix64(id * 0x9E3779B97F4A7C15ULL ^ canonical); }
+
+// ------------------------------------------------------------------------------------------------ Philox
+// rl::rng (include/mymyr/rl/rng.hpp:45-84): Philox-4x32-10 of (seed; draw lo, draw hi, env, purpose).
+B2_DI u64 philox_bits64(u64 seed, u64 env, u64 draw, u32 purpose)
+{
+    u32 c0 = static_cast<u32>(draw), c1 = static_cast<u32>(draw >> 32), c2 = static_cast<u32>(env), c3 = purpose;
+    u32 k0 = static_cast<u32>(seed), k1 = static_cast<u32>(seed >> 32);
+#pragma unroll
+    for (int r = 0; r < 10; ++r)
+    {
+        const u32 hi0 = __umulhi(0xD2511F53u, c0), lo0 = 0xD2511F53u * c0;
+        const u32 hi1 = __umulhi(0xCD9E8D57u, c2), lo1 = 0xCD9E8D57u * c2;
+        const u32 n0 = hi1 ^ c1 ^ k0, n2 = hi0 ^ c3 ^ k1;
+        c0 = n0;
+        c1 = lo1;
+        c2 = n2;
+        c3 = lo0;
+        k0 += 0x9E3779B9u;
+        k1 += 0xBB67AE85u;
+    }
+    return static_cast<u64>(c0) | (static_cast<u64>(c1) << 32);
+}
+
+/// high64(x * n) (rng::below).
+B2_DI u32 below(u64 x, u32 n)
+{
+    const u64 hi = (x >> 32) * n, lo = (x & 0xFFFFFFFFull) * n;
+    return static_cast<u32>((hi + (lo >> 32)) >> 32);
+}
+
+// ------------------------------------------------------------------------------------------------ rows
+/// A state row of up to WR words in registers; word(i) for i >= WR reads zero.
+template<int WR>
+struct RegRow
+{
+    u64 w[WR];
+    B2_DI u64 word(u32 i) const
+    {
+        u64 r = 0;
+#pragma unroll
+        for (int k = 0; k < WR; ++k)
+            r = (static_cast<u32>(k) == i) ? w[k] : r;
+        return r;
+    }
+    B2_DI void set(u32 bit)
+    {
+#pragma unroll
+        for (int k = 0; k < WR; ++k)
+            w[k] |= (static_cast<u32>(k) == (bit >> 6)) ? (u64{1} << (bit & 63)) : 0;
+    }
+    B2_DI void clear(u32 bit)
+    {
+#pragma unroll
+        for (int k = 0; k < WR; ++k)
+            w[k] &= (static_cast<u32>(k) == (bit >> 6)) ? ~(u64{1} << (bit & 63)) : ~u64{0};
+    }
+};
+
+/// A state row read from global memory (rows wider than the register classes).
+struct GlobalRow
+{
+    const u64* p;
+    u32 W;
+    B2_DI u64 word(u32 i) const { return i < W ? __ldg(p + i) : 0; }
+};
+
+template<int WR>
+B2_DI RegRow<WR> load_reg_row(const u64* p, u32 W)
+{
+    RegRow<WR> r;
+#pragma unroll
+    for (int k = 0; k < WR; ++k)
+        r.w[k] = static_cast<u32>(k) < W ? p[k] : 0;
+    return r;
+}
+
+template<class St>
+B2_DI bool bit_of(const St& st, u64 bit)
+{
+    return (st.word(static_cast<u32>(bit >> 6)) >> (bit & 63)) & 1;
+}
+
+/// 64 bits of the row from bit `pos` (bits past the row read as zero).
+template<class St>
+B2_DI u64 extract64(const St& st, u64 pos)
+{
+    const u32 w = static_cast<u32>(pos >> 6), sh = static_cast<u32>(pos & 63);
+    const u64 lo = st.word(w) >> sh;
+    return sh ? lo | (st.word(w + 1) << (64 - sh)) : lo;
+}
+
+/// The successor word i of a parent under delete-then-add effect slots.
+template<class St>
+B2_DI u64 succ_word(const St& st, const u32* del, u32 nd, const u32* add, u32 na, u32 i)
+{
+    u64 w = st.word(i);
+    for (u32 j = 0; j < nd; ++j)
+        if ((del[j] >> 6) == i)
+            w &= ~(u64{1} << (del[j] & 63));
+    for (u32 j = 0; j < na; ++j)
+        if ((add[j] >> 6) == i)
+            w |= u64{1} << (add[j] & 63);
+    return w;
+}
+
+/// canonical_hash of a dense-slot state (src/mymyr/task/task.cpp:387-403).
+template<class St>
+B2_DI u64 canonical_hash(const St& st, u32 W)
+{
+    u64 x = 0;
+    for (u32 i = 0; i < W; ++i)
+    {
+        u64 w = st.word(i);
+        while (w)
+        {
+            const u32 b = __ffsll(static_cast<long long>(w)) - 1;
+            w &= w - 1;
+            x ^= mix64(static_cast<u64>(i) * 64 + b + 0x1234567ULL);
+        }
+    }
+    return x;
+}
+
+// ------------------------------------------------------------------------------------------------ status words
+constexpr u32 kStatusProbeLimit = 1u;
+constexpr u32 kStatusEffectOverflow = 2u;
+constexpr u32 kStatusCapacity = 4u;
+
+// ------------------------------------------------------------------------------------------------ BrFS hash set
+constexpr u64 kEmpty = ~u64{0};
+
+/// The device side of a BrFS layer: per-candidate arenas (row, hash, parent index, successor index), the
+/// open-addressing set of u64 slots (hash >> 32) << 32 | g, and the layer's claim/loss flags and deferred inserts.
+struct Store
+{
+    u64* rows;
+    u64* hash;
+    u32* par;
+    u32* kid;
+    u64* table;
+    u64 mask;
+    u32 W;
+    u32 max_probe;
+    u8* claimed;  // per candidate of the layer
+    u8* lost;
+    u64 layer_cand_begin;
+    u32* status;
+    u64* deferred;  // (slot << 32 | candidate g) of inserts left to the resolve pass
+    u32* ndeferred;
+};
+
+/// Phase A of an insert, with no fence and no acquire: other threads read this candidate's row only in the resolve
+/// pass (a later kernel), so plain stores suffice. A slot holding a state of an earlier layer is compared in place
+/// (its row was written by an earlier kernel); an empty slot is claimed by CAS; a slot holding a candidate of this
+/// layer with the same tag defers the insert (row, hash and node record written first) to the resolve pass.
+template<class Row>
+B2_DI void insert(const Store& S, const Row& s, u64 h, u64 g, u32 i, u32 k)
+{
+    const u64 mine = (h & 0xFFFFFFFF00000000ull) | g;
+    u64 j = h & S.mask;
+    for (u32 probe = 0; probe < S.max_probe; ++probe, j = (j + 1) & S.mask)
+    {
+        u64 cur = __ldcg(S.table + j);
+        if (cur == kEmpty)
+        {
+            const u64 prev = atomicCAS(reinterpret_cast<unsigned long long*>(S.table + j), kEmpty, mine);
+            if (prev == kEmpty)
+            {
+                u64* r = S.rows + g * S.W;
+                for (u32 w = 0; w < S.W; ++w)
+                    r[w] = s.word(w);
+                S.hash[g] = h;
+                S.par[g] = i;
+                S.kid[g] = k;
+                S.claimed[g - S.layer_cand_begin] = 1;
+                return;
+            }
+            cur = prev;
+        }
+        if ((cur >> 32) != (mine >> 32))
+            continue;
+        const u64 og = cur & 0xFFFFFFFFull;
+        if (og >= S.layer_cand_begin)
+        {
+            u64* r = S.rows + g * S.W;
+            for (u32 w = 0; w < S.W; ++w)
+                r[w] = s.word(w);
+            S.hash[g] = h;
+            S.par[g] = i;
+            S.kid[g] = k;
+            const u32 q = atomicAdd(S.ndeferred, 1u);
+            S.deferred[q] = (j << 32) | g;
+            return;
+        }
+        const u64* r = S.rows + og * S.W;
+        bool eq = true;
+        for (u32 w = 0; w < S.W && eq; ++w)
+            eq = __ldcg(r + w) == s.word(w);
+        if (eq)
+            return;  // a state of an earlier layer
+    }
+    atomicOr(S.status, kStatusProbeLimit);
+}
+
+// ------------------------------------------------------------------------------------------------ kernel arguments
+struct LayerMisc
+{
+    u64 total_cand;  // candidates of the layer (scan total)
+    u64 total_new;   // new states of the layer (scan total)
+    u64 fingerprint;
+    u32 goals;       // goal states among the layer's parents
+    u32 first_goal;  // smallest parent index that is a goal (0xFFFFFFFF: none)
+    u32 status;
+    u32 ndeferred;   // inserts left to the resolve pass
+};
+
+/// Arguments of the BrFS count / expand kernels.
+struct BrfsArgs
+{
+    const u32* frontier;  // candidate index of each parent
+    u64 E;                // parents
+    u32* counts;          // [E] successor counts (count pass)
+    const u64* cand_base; // [E] candidate offsets (expand pass)
+    LayerMisc* misc;
+    Store S;
+    u32 pi;               // 0: witness pruning, 1: off
+};
+
+/// Arguments of the env kernels (b2_env_batch and b2_step_out, flattened).
+struct EnvArgs
+{
+    u64* states;
+    u64 rows;
+    u32 words;
+    u32 label_width;
+    i32* steps;
+    u64* draws;
+    u8* at_goal;
+    u32* counts;
+    u64 first_env;
+    float* reward;
+    u8* terminated;
+    u8* truncated;
+    i32* count;
+    u64* final_states;
+    i32* schema;
+    i32* binding;
+    u8* invalid;
+    u8* goal;
+    const i64* actions;
+    const u64* init;       // the initial row
+    const u32* init_info;  // goal, total, per-schema counts of the initial state
+    u32* status;
+    u64 seed;
+    u32 max_steps;
+    float step_reward, goal_reward, dead_end_reward;
+    u32 dead_end_none, dead_end_terminal, autoreset, pi;
+};
+
+/// Arguments of the batched-expand kernels.
+struct ExpandArgs
+{
+    const u64* states;
+    u64 rows;
+    u32 W;
+    u32 pi;
+    u32* counts;          // [rows * schemas]
+    const u64* seg_off;   // [rows * schemas]
+    u64 capacity;
+    u32 out_words;
+    u32 label_width;
+    u64* succ;
+    i32* parent;
+    i32* schema;
+    i32* binding;
+    u64* succ_hash;
+    u32* status;
+};
+}  // namespace dev
+}  // namespace b2

@@ -10,6 +10,7 @@
 
 #pragma once
 
+#include "core.cuh"
 #include "task.hpp"
 
 #include <cstdint>
@@ -19,86 +20,22 @@ namespace b2
 {
 #define B2_HD __host__ __device__ __forceinline__
 
-// ------------------------------------------------------------------------------------------------ hash
-// hash::mix64 / mulfold / words / state_words of the reference (include/mymyr/core/hash.hpp:12-55).
-constexpr u64 kHashSeed = 0x2d358dccaa6c78a5ULL;
-constexpr u64 kHashP1 = 0x8bb84b93962eacc9ULL;
-constexpr u64 kHashP2 = 0x4b33a62ed433d4a3ULL;
+// Hash, Philox, rows and bit extraction come from core.cuh (shared with the run-time compiled kernels).
+using dev::below;
+using dev::bit_of;
+using dev::canonical_hash;
+using dev::extract64;
+using dev::fingerprint_term;
+using dev::GlobalRow;
+using dev::hash_words;
+using dev::mix64;
+using dev::philox_bits64;
+using dev::RegRow;
 
-B2_HD u64 mix64(u64 x)
+template<class St>
+__device__ __forceinline__ bool test_bit(const St& st, u64 bit)
 {
-    x ^= x >> 30;
-    x *= 0xbf58476d1ce4e5b9ULL;
-    x ^= x >> 27;
-    x *= 0x94d049bb133111ebULL;
-    x ^= x >> 31;
-    return x;
-}
-
-B2_HD u64 mulfold(u64 a, u64 b)
-{
-#if defined(__CUDA_ARCH__)
-    return (a * b) ^ __umul64hi(a, b);
-#else
-    const unsigned __int128 r = static_cast<unsigned __int128>(a) * b;
-    return static_cast<u64>(r) ^ static_cast<u64>(r >> 64);
-#endif
-}
-
-/// hash::state_words over words w(0..W-1) (trailing zero words ignored); W is the padded width.
-template<class Get>
-B2_HD u64 hash_words(Get&& w, u32 W)
-{
-    u32 n = W;
-    while (n > 0 && w(n - 1) == 0)
-        --n;
-    u64 h = kHashSeed ^ (static_cast<u64>(n) * kHashP1);
-    u32 i = 0;
-    for (; i + 1 < n; i += 2)
-        h = mulfold(h ^ w(i) ^ kHashP1, w(i + 1) ^ kHashP2);
-    if (i < n)
-        h = mulfold(h ^ w(i) ^ kHashP1, kHashP2);
-    return mix64(h);
-}
-
-/// brfs_fingerprint_term (src/mymyr/search/brfs.cpp:34-37).
-B2_HD u64 fingerprint_term(u64 id, u64 canonical) { return mix64(id * 0x9E3779B97F4A7C15ULL ^ canonical); }
-
-// ------------------------------------------------------------------------------------------------ Philox
-// rl::rng (include/mymyr/rl/rng.hpp:45-84): Philox-4x32-10 of (seed; draw lo, draw hi, env, purpose), a uniform
-// index as the high word of the 64-bit draw times n.
-struct Block4
-{
-    u32 v[4];
-};
-
-B2_HD u32 mulhi32(u32 a, u32 b) { return static_cast<u32>((static_cast<u64>(a) * b) >> 32); }
-
-B2_HD Block4 philox(Block4 c, u32 k0, u32 k1)
-{
-#pragma unroll
-    for (int r = 0; r < 10; ++r)
-    {
-        const u32 hi0 = mulhi32(0xD2511F53u, c.v[0]), lo0 = 0xD2511F53u * c.v[0];
-        const u32 hi1 = mulhi32(0xCD9E8D57u, c.v[2]), lo1 = 0xCD9E8D57u * c.v[2];
-        c = Block4{{hi1 ^ c.v[1] ^ k0, lo1, hi0 ^ c.v[3] ^ k1, lo0}};
-        k0 += 0x9E3779B9u;
-        k1 += 0xBB67AE85u;
-    }
-    return c;
-}
-
-B2_HD u64 philox_bits64(u64 seed, u64 env, u64 draw, u32 purpose)
-{
-    const Block4 b = philox(Block4{{static_cast<u32>(draw), static_cast<u32>(draw >> 32), static_cast<u32>(env), purpose}},
-                            static_cast<u32>(seed), static_cast<u32>(seed >> 32));
-    return static_cast<u64>(b.v[0]) | (static_cast<u64>(b.v[1]) << 32);
-}
-
-B2_HD u32 below(u64 x, u32 n)
-{
-    const u64 hi = (x >> 32) * n, lo = (x & 0xFFFFFFFFull) * n;
-    return static_cast<u32>((hi + (lo >> 32)) >> 32);
+    return bit_of(st, bit);
 }
 
 // ------------------------------------------------------------------------------------------------ task view
@@ -121,59 +58,6 @@ struct DevTask
     const u64* goal_pos;
     const u64* goal_neg;
 };
-
-// ------------------------------------------------------------------------------------------------ state access
-/// A state row of W words held in registers (W <= 8): word(i) for i >= W reads zero.
-template<int W>
-struct RegRow
-{
-    u64 w[W];
-    __device__ __forceinline__ u64 word(u32 i) const
-    {
-        u64 r = 0;
-#pragma unroll
-        for (int k = 0; k < W; ++k)
-            r = (static_cast<u32>(k) == i) ? w[k] : r;
-        return r;
-    }
-    __device__ __forceinline__ void set(u32 bit)
-    {
-#pragma unroll
-        for (int k = 0; k < W; ++k)
-            if (static_cast<u32>(k) == (bit >> 6))
-                w[k] |= u64{1} << (bit & 63);
-    }
-    __device__ __forceinline__ void clear(u32 bit)
-    {
-#pragma unroll
-        for (int k = 0; k < W; ++k)
-            if (static_cast<u32>(k) == (bit >> 6))
-                w[k] &= ~(u64{1} << (bit & 63));
-    }
-};
-
-/// A state row read from global memory (wide rows).
-struct GlobalRow
-{
-    const u64* p;
-    u32 W;
-    __device__ __forceinline__ u64 word(u32 i) const { return i < W ? __ldg(p + i) : 0; }
-};
-
-template<class St>
-__device__ __forceinline__ bool test_bit(const St& st, u64 bit)
-{
-    return (st.word(static_cast<u32>(bit >> 6)) >> (bit & 63)) & 1;
-}
-
-/// 64 bits of the row starting at bit `pos` (bits past the row read as zero).
-template<class St>
-__device__ __forceinline__ u64 extract64(const St& st, u64 pos)
-{
-    const u32 w = static_cast<u32>(pos >> 6), sh = static_cast<u32>(pos & 63);
-    const u64 lo = st.word(w) >> sh;
-    return sh ? lo | (st.word(w + 1) << (64 - sh)) : lo;
-}
 
 // ------------------------------------------------------------------------------------------------ matcher
 template<int OW>
@@ -414,22 +298,4 @@ __device__ __forceinline__ u64 succ_word(const St& st, const Effects& e, u32 i)
     return w;
 }
 
-/// canonical_hash of a dense-slot state (src/mymyr/task/task.cpp:387-403): xor of mix64(cid + 0x1234567) over its
-/// true atoms.
-template<class St>
-__device__ __forceinline__ u64 canonical_hash(const St& st, u32 W)
-{
-    u64 x = 0;
-    for (u32 i = 0; i < W; ++i)
-    {
-        u64 w = st.word(i);
-        while (w)
-        {
-            const u32 b = __ffsll(static_cast<long long>(w)) - 1;
-            w &= w - 1;
-            x ^= mix64(static_cast<u64>(i) * 64 + b + 0x1234567ULL);
-        }
-    }
-    return x;
-}
 }  // namespace b2

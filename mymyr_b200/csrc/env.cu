@@ -282,9 +282,17 @@ b2_status b2_env_create(b2_task* task, const b2_env_config* config, b2_env** out
         e->status.alloc(4);
         B2_CUDA(cudaMemset(e->status.p, 0, 4));
         const u32 pi = config->witness_pruning ? 0 : 1;
-        dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
-            k_env_init<OW, WR><<<1, 1>>>(task->dev, e->init.as<u64>(), P.words, pi, e->init_info.as<u32>());
-        });
+        if (task->jit)
+        {
+            dev::EnvArgs a{};
+            a.init = e->init.as<u64>();
+            a.status = e->init_info.as<u32>();  // the init kernel writes goal, total and per-schema counts here
+            jit_launch(task->jit->env_init[pi], 1, 1, &a, nullptr);
+        }
+        else
+            dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
+                k_env_init<OW, WR><<<1, 1>>>(task->dev, e->init.as<u64>(), P.words, pi, e->init_info.as<u32>());
+            });
         B2_CUDA(cudaGetLastError());
         B2_CUDA(cudaDeviceSynchronize());
         *out = e.release();
@@ -349,10 +357,47 @@ b2_status b2_env_step(b2_env* env, const b2_env_batch* batch, const b2_step_out*
         p.autoreset = env->cfg.autoreset ? 1 : 0;
         p.pi = env->cfg.witness_pruning ? 0 : 1;
         const unsigned grid = grid_for(batch->rows, 128, static_cast<unsigned>(env->task->ctx->sms) * 64);
-        dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
-            k_env_step<OW, WR><<<grid, 128, 0, s>>>(env->task->dev, p, *batch, *out, actions, env->init.as<u64>(),
-                                                    env->init_info.as<u32>(), env->status.as<u32>());
-        });
+        if (env->task->jit)
+        {
+            dev::EnvArgs a{};
+            a.states = batch->states;
+            a.rows = batch->rows;
+            a.words = batch->words;
+            a.label_width = out->label_width;
+            a.steps = batch->steps;
+            a.draws = batch->draws;
+            a.at_goal = batch->at_goal;
+            a.counts = batch->counts;
+            a.first_env = batch->first_env;
+            a.reward = out->reward;
+            a.terminated = out->terminated;
+            a.truncated = out->truncated;
+            a.count = out->count;
+            a.final_states = out->final_states;
+            a.schema = out->schema;
+            a.binding = out->binding;
+            a.invalid = out->invalid;
+            a.goal = out->goal;
+            a.actions = actions;
+            a.init = env->init.as<u64>();
+            a.init_info = env->init_info.as<u32>();
+            a.status = env->status.as<u32>();
+            a.seed = p.seed;
+            a.max_steps = p.max_steps;
+            a.step_reward = p.step_reward;
+            a.goal_reward = p.goal_reward;
+            a.dead_end_reward = p.dead_end_reward;
+            a.dead_end_none = p.dead_end_none;
+            a.dead_end_terminal = p.dead_end_terminal;
+            a.autoreset = p.autoreset;
+            a.pi = p.pi;
+            jit_launch(env->task->jit->env_step[p.pi], grid, 128, &a, s);
+        }
+        else
+            dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
+                k_env_step<OW, WR><<<grid, 128, 0, s>>>(env->task->dev, p, *batch, *out, actions, env->init.as<u64>(),
+                                                        env->init_info.as<u32>(), env->status.as<u32>());
+            });
         B2_CUDA(cudaGetLastError());
     });
 }

@@ -134,12 +134,32 @@ extern "C" b2_status b2_expand(b2_task* task, const uint64_t* states, uint64_t r
         B2_CUDA(cudaMemsetAsync(status, 0, 4, s));
         const u32 pi = witness_pruning ? 0 : 1;
         const unsigned grid = grid_for(nseg, 128, static_cast<unsigned>(ctx->sms) * 64);
-        if (nseg)
+        dev::ExpandArgs a{};
+        a.states = states;
+        a.rows = rows;
+        a.W = words;
+        a.pi = pi;
+        a.counts = counts;
+        a.seg_off = seg_off;
+        a.capacity = out->capacity;
+        a.out_words = out->words;
+        a.label_width = out->label_width;
+        a.succ = out->succ;
+        a.parent = out->parent;
+        a.schema = out->schema;
+        a.binding = out->binding;
+        a.succ_hash = out->succ_hash;
+        a.status = status;
+        if (nseg && task->jit)
+            jit_launch(task->jit->expand_count[pi], grid, 128, &a, s);
+        else if (nseg)
             dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
                 k_expand_count<OW, WR><<<grid, 128, 0, s>>>(task->dev, states, rows, words, pi, counts);
             });
         device_scan(SegCountIn{counts}, SegCountOut{seg_off}, nseg, total, sums, s);
-        if (nseg)
+        if (nseg && task->jit)
+            jit_launch(task->jit->expand_write[pi], grid, 128, &a, s);
+        else if (nseg)
             dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
                 k_expand_write<OW, WR><<<grid, 128, 0, s>>>(task->dev, states, rows, words, pi, seg_off, *out, status);
             });

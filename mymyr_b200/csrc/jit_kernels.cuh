@@ -1,0 +1,345 @@
+// The kernels of the device path over a generated matcher (namespace b2::gen, see codegen.cpp), compiled at run time
+// by NVRTC for sm_100a together with the task's matcher: the BrFS count and expand passes, the env step, and the
+// batched expand. Their logic is the one of the nvcc-compiled kernels (brfs.cu, env.cu, expand.cu); only the matcher
+// calls differ.
+
+#pragma once
+
+namespace b2
+{
+namespace gen
+{
+using namespace b2::dev;
+
+template<int N>
+struct RowSel
+{
+    using type = RegRow<N>;
+    B2_DI static type load(const u64* p) { return load_reg_row<N>(p, W); }
+};
+template<>
+struct RowSel<0>
+{
+    using type = GlobalRow;
+    B2_DI static type load(const u64* p) { return GlobalRow{p, W}; }
+};
+using Row = typename RowSel<WR>::type;
+
+/// The successor of `st` under the effect keys, as a word accessor (wide rows).
+struct SuccView
+{
+    const Row& st;
+    const u32* del;
+    u32 nd;
+    const u32* add;
+    u32 na;
+    B2_DI u64 word(u32 i) const { return succ_word(st, del, nd, add, na, i); }
+};
+
+/// Calls f(successor accessor, hash) for the successor of `st` under schema S's binding b.
+template<int S, class F>
+B2_DI void with_successor(const Row& st, const u32* b, F&& f)
+{
+    u32 del[Eff<S>::ND ? Eff<S>::ND : 1], add[Eff<S>::NA ? Eff<S>::NA : 1];
+    u32 nd = 0, na = 0;
+    Eff<S>::keys(b, del, nd, add, na);
+    if constexpr (WR > 0)
+    {
+        Row nx = st;
+        for (u32 j = 0; j < nd; ++j)
+            nx.clear(del[j]);
+        for (u32 j = 0; j < na; ++j)
+            nx.set(add[j]);
+        const u64 h = hash_words([&](u32 q) { return nx.word(q); }, W);
+        f(nx, h);
+    }
+    else
+    {
+        const SuccView nx{st, del, nd, add, na};
+        const u64 h = hash_words([&](u32 q) { return nx.word(q); }, W);
+        f(nx, h);
+    }
+}
+
+template<int PI>
+B2_DI u32 count_all(const Row& st)
+{
+    u32 c = 0;
+    for_each_schema([&]<int S>() {
+        Run<S, PI>::go(st, [&](const u32*) {
+            ++c;
+            return true;
+        });
+    });
+    return c;
+}
+
+// ------------------------------------------------------------------------------------------------ BrFS
+template<int PI>
+B2_DI void brfs_count(const BrfsArgs& a)
+{
+    for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < a.E; i += static_cast<u64>(gridDim.x) * blockDim.x)
+    {
+        const u64 g = a.frontier[i];
+        const Row st = RowSel<WR>::load(a.S.rows + g * W);
+        if (goal(st))
+        {
+            atomicAdd(&a.misc->goals, 1u);
+            atomicMin(&a.misc->first_goal, static_cast<u32>(i));
+        }
+        a.counts[i] = count_all<PI>(st);
+    }
+}
+
+template<int PI>
+B2_DI void brfs_expand(const BrfsArgs& a)
+{
+    for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < a.E; i += static_cast<u64>(gridDim.x) * blockDim.x)
+    {
+        const u64 pg = a.frontier[i];
+        const Row st = RowSel<WR>::load(a.S.rows + pg * W);
+        const u64 g0 = a.S.layer_cand_begin + a.cand_base[i];
+        u32 k = 0;
+        for_each_schema([&]<int S>() {
+            Run<S, PI>::go(st, [&](const u32* b) {
+                with_successor<S>(st, b, [&](const auto& nx, u64 h) { insert(a.S, nx, h, g0 + k, static_cast<u32>(i), k); });
+                ++k;
+                return true;
+            });
+        });
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ env
+template<int PI>
+B2_DI void env_init(const EnvArgs& a)
+{
+    const Row st = RowSel<WR>::load(a.init);
+    u32* out = a.status;  // [2 + NS]: goal, total, per-schema counts
+    u32 total = 0;
+    for_each_schema([&]<int S>() {
+        u32 c = 0;
+        Run<S, PI>::go(st, [&](const u32*) {
+            ++c;
+            return true;
+        });
+        out[2 + S] = c;
+        total += c;
+    });
+    out[0] = goal(st) ? 1 : 0;
+    out[1] = total;
+}
+
+template<int PI>
+B2_DI void env_step(const EnvArgs& a)
+{
+    for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < a.rows; i += static_cast<u64>(gridDim.x) * blockDim.x)
+    {
+        u64* row = a.states + i * W;
+        u32* cache = a.counts + i * NS;
+        const Row st = RowSel<WR>::load(row);
+        const bool already_goal = a.at_goal[i] != 0;
+        u32 c = 0;
+        for (u32 s = 0; s < NS; ++s)
+            c += cache[s];
+        enum : u32
+        {
+            kOk,
+            kGoal,
+            kStuck,
+            kInvalid
+        };
+        u32 stt = already_goal ? kGoal : kOk;
+        u64 act = 0;
+        if (!already_goal && c == 0)
+            stt = kStuck;
+        else if (!already_goal && a.actions)
+        {
+            const i64 x = a.actions[i];
+            if (x < 0 || static_cast<u64>(x) >= c)
+                stt = kInvalid;
+            else
+                act = static_cast<u64>(x);
+        }
+        else if (!already_goal)
+            act = below(philox_bits64(a.seed, a.first_env + i, a.draws[i], 0u), c);
+        a.draws[i] += 1;
+        u32 schema = 0;
+        u64 r = act;
+        if (stt == kOk)
+            while (schema < NS && r >= cache[schema])
+                r -= cache[schema++];
+        bool g = already_goal;
+        u32 c2 = c;
+        bool moved = false;
+        u32 newc[NS ? NS : 1];
+        if (stt == kOk)
+        {
+            bool found = false;
+            with_schema(schema, [&]<int S>() {
+                u64 seen = 0;
+                Run<S, PI>::go(st, [&](const u32* b) {
+                    if (seen++ != r)
+                        return true;
+                    found = true;
+                    if (a.schema)
+                        a.schema[i] = static_cast<i32>(S);
+                    if (a.binding)
+                        for (u32 k = 0; k < a.label_width; ++k)
+                            a.binding[i * a.label_width + k] = k < ARITY[S] ? static_cast<i32>(b[k]) : -1;
+                    with_successor<S>(st, b, [&](const auto& nx, u64) {
+                        for (u32 q = 0; q < W; ++q)
+                        {
+                            const u64 x = nx.word(q);
+                            if (a.final_states)
+                                a.final_states[i * W + q] = x;
+                            row[q] = x;  // provisional: an autoreset overwrites it (wide rows: reads stay ahead)
+                        }
+                    });
+                    return false;
+                });
+            });
+            if (!found)
+            {
+                atomicOr(a.status, kStatusCapacity);  // the count cache disagreed with the state
+                stt = kStuck;
+            }
+            else
+            {
+                moved = true;
+                const Row nx = RowSel<WR>::load(row);
+                g = goal(nx);
+                c2 = 0;
+                for_each_schema([&]<int S>() {
+                    u32 cs = 0;
+                    Run<S, PI>::go(nx, [&](const u32*) {
+                        ++cs;
+                        return true;
+                    });
+                    newc[S] = cs;
+                    c2 += cs;
+                });
+            }
+        }
+        if (stt != kOk)
+        {
+            if (a.schema)
+                a.schema[i] = -1;
+            if (a.binding)
+                for (u32 k = 0; k < a.label_width; ++k)
+                    a.binding[i * a.label_width + k] = -1;
+            if (a.final_states)
+                for (u32 q = 0; q < W; ++q)
+                    a.final_states[i * W + q] = st.word(q);
+        }
+        if (a.invalid)
+            a.invalid[i] = stt == kInvalid ? 1 : 0;
+        const bool dead = !a.dead_end_none && !g && ((moved && c2 == 0) || stt == kStuck);
+        const bool term = g || (dead && a.dead_end_terminal);
+        const bool absorbed = already_goal || (stt == kStuck && dead && a.dead_end_terminal);
+        const i32 t2 = a.steps ? a.steps[i] + (absorbed ? 0 : 1) : 0;
+        const bool trunc = !term && a.max_steps && t2 >= static_cast<i32>(a.max_steps);
+        if (a.reward)
+            a.reward[i] = absorbed ? 0.0f : a.step_reward + (g ? a.goal_reward : 0.0f) + (dead ? a.dead_end_reward : 0.0f);
+        if (a.terminated)
+            a.terminated[i] = term ? 1 : 0;
+        if (a.truncated)
+            a.truncated[i] = trunc ? 1 : 0;
+        if (a.goal)
+            a.goal[i] = g ? 1 : 0;
+        if (a.autoreset && (term || trunc))
+        {
+            for (u32 q = 0; q < W; ++q)
+                row[q] = a.init[q];
+            if (a.steps)
+                a.steps[i] = 0;
+            for (u32 s = 0; s < NS; ++s)
+                cache[s] = a.init_info[2 + s];
+            a.at_goal[i] = static_cast<u8>(a.init_info[0]);
+            if (a.count)
+                a.count[i] = static_cast<i32>(a.init_info[1]);
+            continue;
+        }
+        a.at_goal[i] = g ? 1 : 0;
+        if (moved)
+            for (u32 s = 0; s < NS; ++s)
+                cache[s] = newc[s];
+        if (a.steps)
+            a.steps[i] = t2;
+        if (a.count)
+            a.count[i] = static_cast<i32>(c2);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ batched expand
+template<int PI>
+B2_DI void expand_count(const ExpandArgs& a)
+{
+    const u64 nseg = a.rows * NS;
+    for (u64 q = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; q < nseg; q += static_cast<u64>(gridDim.x) * blockDim.x)
+    {
+        const u64 r = q / NS;
+        const u32 s = static_cast<u32>(q - r * NS);
+        const Row st = RowSel<WR>::load(a.states + r * W);
+        u32 c = 0;
+        with_schema(s, [&]<int S>() {
+            Run<S, PI>::go(st, [&](const u32*) {
+                ++c;
+                return true;
+            });
+        });
+        a.counts[q] = c;
+    }
+}
+
+template<int PI>
+B2_DI void expand_write(const ExpandArgs& a)
+{
+    const u64 nseg = a.rows * NS;
+    for (u64 q = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; q < nseg; q += static_cast<u64>(gridDim.x) * blockDim.x)
+    {
+        const u64 r = q / NS;
+        const u32 s = static_cast<u32>(q - r * NS);
+        const Row st = RowSel<WR>::load(a.states + r * W);
+        u64 idx = a.seg_off[q];
+        with_schema(s, [&]<int S>() {
+            Run<S, PI>::go(st, [&](const u32* b) {
+                if (idx < a.capacity)
+                {
+                    if (a.parent)
+                        a.parent[idx] = static_cast<i32>(r);
+                    if (a.schema)
+                        a.schema[idx] = static_cast<i32>(S);
+                    if (a.binding)
+                        for (u32 k = 0; k < a.label_width; ++k)
+                            a.binding[idx * a.label_width + k] = k < ARITY[S] ? static_cast<i32>(b[k]) : -1;
+                    if (a.succ_hash || a.succ)
+                        with_successor<S>(st, b, [&](const auto& nx, u64 h) {
+                            if (a.succ_hash)
+                                a.succ_hash[idx] = h;
+                            if (a.succ)
+                                for (u32 w = 0; w < a.out_words; ++w)
+                                    a.succ[idx * a.out_words + w] = w < W ? nx.word(w) : 0;
+                        });
+                }
+                ++idx;
+                return true;
+            });
+        });
+    }
+}
+}  // namespace gen
+}  // namespace b2
+
+extern "C" __global__ void __launch_bounds__(128) b2j_brfs_count_w(b2::dev::BrfsArgs a) { b2::gen::brfs_count<0>(a); }
+extern "C" __global__ void __launch_bounds__(128) b2j_brfs_count_nw(b2::dev::BrfsArgs a) { b2::gen::brfs_count<1>(a); }
+extern "C" __global__ void __launch_bounds__(128) b2j_brfs_expand_w(b2::dev::BrfsArgs a) { b2::gen::brfs_expand<0>(a); }
+extern "C" __global__ void __launch_bounds__(128) b2j_brfs_expand_nw(b2::dev::BrfsArgs a) { b2::gen::brfs_expand<1>(a); }
+extern "C" __global__ void b2j_env_init_w(b2::dev::EnvArgs a) { b2::gen::env_init<0>(a); }
+extern "C" __global__ void b2j_env_init_nw(b2::dev::EnvArgs a) { b2::gen::env_init<1>(a); }
+extern "C" __global__ void __launch_bounds__(128) b2j_env_step_w(b2::dev::EnvArgs a) { b2::gen::env_step<0>(a); }
+extern "C" __global__ void __launch_bounds__(128) b2j_env_step_nw(b2::dev::EnvArgs a) { b2::gen::env_step<1>(a); }
+extern "C" __global__ void __launch_bounds__(128) b2j_expand_count_w(b2::dev::ExpandArgs a) { b2::gen::expand_count<0>(a); }
+extern "C" __global__ void __launch_bounds__(128) b2j_expand_count_nw(b2::dev::ExpandArgs a) { b2::gen::expand_count<1>(a); }
+extern "C" __global__ void __launch_bounds__(128) b2j_expand_write_w(b2::dev::ExpandArgs a) { b2::gen::expand_write<0>(a); }
+extern "C" __global__ void __launch_bounds__(128) b2j_expand_write_nw(b2::dev::ExpandArgs a) { b2::gen::expand_write<1>(a); }

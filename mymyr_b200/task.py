@@ -56,7 +56,7 @@ class Task:
     """A compiled task. On a device context (``ctx``) it can run kernels; with ``host_only=True`` it is compiled on
     the host only (layout, initial state, slot records; no GPU needed)."""
 
-    def __init__(self, text: str, ctx: Context | None = None, host_only: bool = False):
+    def __init__(self, text: str, ctx: Context | None = None, host_only: bool = False, matcher: str = "auto"):
         L = lib()
         desc = C.POINTER(_lib.TaskDesc)()
         raw = text.encode()
@@ -64,8 +64,10 @@ class Task:
         try:
             self.ctx = None if host_only else (ctx or default_context())
             h = C.c_void_p()
-            check(L.b2_task_create(self.ctx.handle if self.ctx else None, desc, C.byref(h)))
+            opts = _lib.TaskOptions(_lib.MATCHER[matcher])
+            check(L.b2_task_create_ex(self.ctx.handle if self.ctx else None, desc, C.byref(opts), C.byref(h)))
             self._h = h
+            self.matcher = "interpreted" if matcher == "interpreted" or host_only else "compiled"
         finally:
             L.b2_task_desc_free(desc)
         info = _lib.TaskInfo()
@@ -79,13 +81,23 @@ class Task:
         self.text = text
 
     @classmethod
-    def from_text(cls, text: str, ctx: Context | None = None, host_only: bool = False) -> "Task":
-        return cls(text, ctx, host_only)
+    def from_text(cls, text: str, ctx: Context | None = None, host_only: bool = False,
+                  matcher: str = "auto") -> "Task":
+        return cls(text, ctx, host_only, matcher)
 
     @classmethod
-    def from_text_file(cls, path, ctx: Context | None = None, host_only: bool = False) -> "Task":
+    def from_text_file(cls, path, ctx: Context | None = None, host_only: bool = False,
+                       matcher: str = "auto") -> "Task":
         with open(path) as f:
-            return cls(f.read(), ctx, host_only)
+            return cls(f.read(), ctx, host_only, matcher)
+
+    def compile(self) -> str:
+        """Compiles the task's kernels for sm_100a (no device needed) and returns the generated source."""
+        n = C.c_size_t()
+        check(lib().b2_task_compile(self._h, None, 0, C.byref(n)))
+        buf = C.create_string_buffer(n.value + 1)
+        check(lib().b2_task_compile(self._h, buf, n.value + 1, None))
+        return buf.value.decode()
 
     @property
     def handle(self) -> C.c_void_p:

@@ -18,6 +18,9 @@ from mymyr_b200.task import Task  # noqa: E402
 from mymyr_b200 import UnsupportedTask  # noqa: E402
 
 
+MATCHERS = ["compiled", "interpreted"]
+
+
 @pytest.fixture(scope="module", autouse=True)
 def _need_cuda():
     if not torch.cuda.is_available():
@@ -69,10 +72,11 @@ BRFS_CASES = [
 
 @pytest.mark.parametrize("name,make,depth", BRFS_CASES, ids=[c[0] for c in BRFS_CASES])
 @pytest.mark.parametrize("witness", [True, False])
-def test_brfs_matches_reference(ref, name, make, depth, witness):
+@pytest.mark.parametrize("matcher", MATCHERS)
+def test_brfs_matches_reference(ref, name, make, depth, witness, matcher):
     text = make()
     rt = ref.RefTask(text)
-    t = Task.from_text(text)
+    t = Task.from_text(text, matcher=matcher)
     want = rt.brfs(threads=1, max_depth=depth, stop_at_goal=False, witness_pruning=witness, fingerprint=True)
     got = b2cuda.brfs(t, max_depth=depth, stop_at_goal=False, witness_pruning=witness, fingerprint=True)
     assert got.states == want["states"]
@@ -97,11 +101,12 @@ def test_brfs_matches_reference(ref, name, make, depth, witness):
 
 @pytest.mark.parametrize("make", [lambda: tasks.tower(7, 0), lambda: tasks.sliding_tile(3, 3, 30, 1),
                                   lambda: tasks.transport(2, 5, 2, 4)])
-def test_brfs_stop_at_goal_matches_reference(ref, make):
+@pytest.mark.parametrize("matcher", MATCHERS)
+def test_brfs_stop_at_goal_matches_reference(ref, make, matcher):
     text = make()
     rt = ref.RefTask(text)
     want = rt.brfs(threads=1, stop_at_goal=True, fingerprint=True)
-    got = b2cuda.brfs(Task.from_text(text), stop_at_goal=True, fingerprint=True)
+    got = b2cuda.brfs(Task.from_text(text, matcher=matcher), stop_at_goal=True, fingerprint=True)
     for key in ("states", "expanded", "generated", "num_goal_states", "layers", "fingerprint"):
         assert getattr(got, key) == want[key], key
     assert got.solved == bool(want["solved"])
@@ -144,10 +149,11 @@ EXPAND_CASES = [
 
 @pytest.mark.parametrize("name,make,n,density", EXPAND_CASES, ids=[c[0] for c in EXPAND_CASES])
 @pytest.mark.parametrize("witness", [False, True])
-def test_expand_matches_reference(ref, name, make, n, density, witness):
+@pytest.mark.parametrize("matcher", MATCHERS)
+def test_expand_matches_reference(ref, name, make, n, density, witness, matcher):
     text = make()
     rt = ref.RefTask(text)
-    t = Task.from_text(text)
+    t = Task.from_text(text, matcher=matcher)
     states = random_states(t.words, t.fluent_slots, n, density, seed=hash(name) & 0xFFFF)
     states[0] = t.initial_state()
     want = rt.expand(states, witness_pruning=witness, succ=True)
@@ -193,10 +199,11 @@ ENV_CASES = [
 
 
 @pytest.mark.parametrize("name,make,cfg", ENV_CASES, ids=[c[0] for c in ENV_CASES])
-def test_env_trajectories_match_reference(ref, name, make, cfg):
+@pytest.mark.parametrize("matcher", MATCHERS)
+def test_env_trajectories_match_reference(ref, name, make, cfg, matcher):
     text = make()
     rt = ref.RefTask(text)
-    t = Task.from_text(text)
+    t = Task.from_text(text, matcher=matcher)
     n, steps = 512, 120
     env = b2rl.BatchedEnv(t, n, seed=1234, first_env=7, **cfg)
     renv = ref.RefEnv(rt, n, seed=1234, first_env=7, **cfg)
@@ -219,10 +226,11 @@ def test_env_trajectories_match_reference(ref, name, make, cfg):
         assert np.array_equal(as_u64(env.final_states), renv.final_states), s
 
 
-def test_env_given_actions_match_reference(ref):
+@pytest.mark.parametrize("matcher", MATCHERS)
+def test_env_given_actions_match_reference(ref, matcher):
     text = tasks.transport(2, 4, 2, 3)
     rt = ref.RefTask(text)
-    t = Task.from_text(text)
+    t = Task.from_text(text, matcher=matcher)
     n = 300
     env = b2rl.BatchedEnv(t, n, seed=5)
     renv = ref.RefEnv(rt, n, seed=5)
