@@ -225,8 +225,10 @@ def main():
     sp = stream.cuda_stream
 
     def one(expected=None):
-        return b2cuda.brfs(task, max_depth=args.depth, stop_at_goal=False, timings=True, expected_states=expected,
-                           stream=sp)
+        r = b2cuda.brfs(task, max_depth=args.depth, stop_at_goal=False, timings=True, expected_states=expected,
+                        stream=sp)
+        r.close()  # free the search's device buffers now (back to the pool for the next step)
+        return r
 
     r = one()
     expected = r.states
@@ -284,6 +286,7 @@ def main():
         t2 = Task.from_text(text, ctx)
         rr = b2cuda.brfs(t2, max_depth=args.depth, stop_at_goal=False, expected_states=expected, stream=sp)
         hashes = rr.state_hashes()
+        rr.close()
         e2e_times.append(time.perf_counter() - t0)
         d2h = hashes.nbytes + 24 * rr.layers
     e2e_s = sum(e2e_times)
@@ -313,7 +316,8 @@ def main():
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches,
             "clocks": clocks,
-            "phases_ms_per_run": {"count": statistics.mean(r.stats.count_ms for r in results),
+            "phases_ms_per_run": {"rehashes": results[-1].stats.rehashes,
+                                  "count": statistics.mean(r.stats.count_ms for r in results),
                                   "expand": statistics.mean(r.stats.gen_ms for r in results),
                                   "rank": statistics.mean(r.stats.dedup_ms for r in results),
                                   "wall": statistics.mean(r.search_s * 1000 for r in results)},

@@ -272,6 +272,11 @@ b2_status b2_ctx_create(int device, b2_ctx** out)
             throw Error(B2_UNSUPPORTED, "mymyr_b200 is built for sm_100a (B200); device " + std::to_string(device) +
                                             " is sm_" + std::to_string(c->prop.major * 10 + c->prop.minor));
         c->sms = c->prop.multiProcessorCount;
+        // keep the device pool's memory between stream-ordered frees (searches allocate and free gigabytes)
+        cudaMemPool_t pool;
+        B2_CUDA(cudaDeviceGetDefaultMemPool(&pool, device));
+        uint64_t keep = ~uint64_t{0};
+        B2_CUDA(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep));
         *out = c.release();
     });
 }

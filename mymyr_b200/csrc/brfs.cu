@@ -304,6 +304,7 @@ struct b2_brfs
     // per layer scratch
     DeviceBuffer counts, cand_base, flags, deferred, sums, misc;
     u64 cap_layer = 0, cap_flags = 0;
+    dev::LayerMisc* misc_host = nullptr;  // pinned mirror of `misc`
     // results
     std::vector<u64> layer_begin;  // id of each layer's first state (+ the end)
     u64 n_states = 0;
@@ -340,18 +341,18 @@ void ensure_layer(b2_brfs& B, u64 E, u64 G)
     if (E > B.cap_layer)
     {
         const u64 cap = std::max<u64>(E, B.cap_layer * 2);
-        B.counts.alloc(cap * 4);
-        B.cand_base.alloc((cap + 1) * 8);
-        B.sums.alloc(std::max(scan_scratch_bytes(cap), B.sums.bytes));
+        B.counts.alloc(cap * 4, B.stream);
+        B.cand_base.alloc((cap + 1) * 8, B.stream);
+        B.sums.alloc(std::max(scan_scratch_bytes(cap), B.sums.bytes), B.stream);
         B.cap_layer = cap;
     }
     if (G > B.cap_flags)
     {
         const u64 cap = std::max<u64>(G, B.cap_flags * 2);
-        B.flags.alloc(cap * 2 + 16);
-        B.deferred.alloc(cap * sizeof(u64));
+        B.flags.alloc(cap * 2 + 16, B.stream);
+        B.deferred.alloc(cap * sizeof(u64), B.stream);
         if (B.sums.bytes < scan_scratch_bytes(cap))
-            B.sums.alloc(scan_scratch_bytes(cap));
+            B.sums.alloc(scan_scratch_bytes(cap), B.stream);
         B.cap_flags = cap;
     }
 }
@@ -361,12 +362,13 @@ u32 max_probe(u64 slots) { return static_cast<u32>(std::min<u64>(slots, u64{1} <
 /// Grows the hash set so that `states` entries keep it at most half full, and reinserts the stored states.
 void ensure_table(b2_brfs& B, u64 states)
 {
-    if (states * 2 <= B.table_slots)
+    // `states` is an upper bound (stored states + this layer's candidates): grow past 3/4 of it, to 1/2 load
+    if (states * 4 <= B.table_slots * 3)
         return;
     u64 slots = B.table_slots ? B.table_slots : 1024;
     while (states * 2 > slots)
         slots *= 2;
-    B.table.alloc(slots * 8);
+    B.table.alloc(slots * 8, B.stream);
     B.table_slots = slots;
     B2_CUDA(cudaMemsetAsync(B.table.p, 0xFF, slots * 8, B.stream));
     if (B.n_states)
@@ -403,9 +405,9 @@ Store make_store(b2_brfs& B, u64 layer_cand_begin)
 
 LayerMisc read_misc(b2_brfs& B)
 {
-    LayerMisc m;
-    B2_CUDA(cudaMemcpyAsync(&m, B.misc.p, sizeof m, cudaMemcpyDeviceToHost, B.stream));
+    B2_CUDA(cudaMemcpyAsync(B.misc_host, B.misc.p, sizeof(LayerMisc), cudaMemcpyDeviceToHost, B.stream));
     B2_CUDA(cudaStreamSynchronize(B.stream));
+    const LayerMisc m = *B.misc_host;
     if (m.status & kStatusProbeLimit)
         throw Error(B2_DEVICE_FAULT, "b2_brfs: a hash-set probe ran past its bound");
     if (m.status)
@@ -447,7 +449,11 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
     const u64 expect = std::max<u64>(o.expected_states, 1024);
     ensure_cand(B, expect * 2, 0);
     ensure_states(B, expect);
-    B.misc.alloc(sizeof(LayerMisc));
+    if (o.expected_states)
+        ensure_layer(B, expect / 2, expect);  // a layer holds at most the states, and about twice as many candidates
+    B.misc.alloc(sizeof(LayerMisc), s);
+    if (!B.misc_host)
+        B2_CUDA(cudaMallocHost(&B.misc_host, sizeof(LayerMisc)));
     B2_CUDA(cudaMemsetAsync(B.misc.p, 0, sizeof(LayerMisc), s));
     ensure_table(B, expect);
     B2_CUDA(cudaMemcpyAsync(B.rows.p, P.initial.data(), W * 8, cudaMemcpyHostToDevice, s));
@@ -476,8 +482,8 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
         ++layers;
         ensure_layer(B, E, 0);
         LayerMisc* misc = B.misc.as<LayerMisc>();
-        const LayerMisc init{0, 0, 0, 0, 0xFFFFFFFFu, 0, 0};
-        B2_CUDA(cudaMemcpyAsync(misc, &init, sizeof init, cudaMemcpyHostToDevice, s));
+        *B.misc_host = LayerMisc{0, 0, 0, 0, 0xFFFFFFFFu, 0, 0};
+        B2_CUDA(cudaMemcpyAsync(misc, B.misc_host, sizeof(LayerMisc), cudaMemcpyHostToDevice, s));
         const u32* frontier = B.state_g.as<u32>() + layer_begin;
         const unsigned grid = grid_for(E, 128, static_cast<unsigned>(B.task->ctx->sms) * 64);
         if (o.timings)
@@ -758,9 +764,17 @@ void b2_brfs_destroy(b2_brfs* search)
     if (search->stream)
     {
         cudaStreamSynchronize(search->stream);
+        // stream-ordered frees go on the search's stream, before a stream of its own is destroyed
+        for (DeviceBuffer* b : {&search->rows, &search->hash, &search->par, &search->kid, &search->state_g,
+                                &search->table, &search->counts, &search->cand_base, &search->flags, &search->deferred,
+                                &search->sums, &search->misc})
+            b->reset();
+        cudaStreamSynchronize(search->stream);
         if (search->own_stream)
             cudaStreamDestroy(search->stream);
     }
+    if (search->misc_host)
+        cudaFreeHost(search->misc_host);
     delete search;
 }
 

@@ -84,11 +84,15 @@ enum : u32
     kStatusCapacity = 4u,        // a write past a buffer's capacity was dropped
 };
 
-/// A device allocation owned by the library.
+/// A device allocation owned by the library. Plain buffers use cudaMalloc; stream-ordered ones (a stream given to
+/// alloc/grow) come from the device's memory pool, which the context keeps from releasing memory between calls, so a
+/// search that allocates and frees gigabytes does not pay for page mapping every time.
 struct DeviceBuffer
 {
     void* p = nullptr;
     size_t bytes = 0;
+    cudaStream_t stream = nullptr;
+    bool pooled = false;
     DeviceBuffer() = default;
     DeviceBuffer(const DeviceBuffer&) = delete;
     DeviceBuffer& operator=(const DeviceBuffer&) = delete;
@@ -96,29 +100,45 @@ struct DeviceBuffer
     void reset()
     {
         if (p)
-            cudaFree(p);
+        {
+            if (pooled)
+                cudaFreeAsync(p, stream);
+            else
+                cudaFree(p);
+        }
         p = nullptr;
         bytes = 0;
     }
     void alloc(size_t n)
     {
         reset();
+        pooled = false;
         if (n)
             B2_CUDA(cudaMalloc(&p, n));
         bytes = n;
     }
-    /// Grows to at least n bytes, keeping the first `keep` bytes.
+    /// Stream-ordered allocation from the device's pool (contents undefined).
+    void alloc(size_t n, cudaStream_t s)
+    {
+        reset();
+        stream = s;
+        pooled = true;
+        if (n)
+            B2_CUDA(cudaMallocAsync(&p, n, s));
+        bytes = n;
+    }
+    /// Grows to at least n bytes (stream-ordered), keeping the first `keep` bytes.
     void grow(size_t n, size_t keep, cudaStream_t s)
     {
         if (n <= bytes)
             return;
         void* q = nullptr;
-        B2_CUDA(cudaMalloc(&q, n));
+        B2_CUDA(cudaMallocAsync(&q, n, s));
         if (p && keep)
             B2_CUDA(cudaMemcpyAsync(q, p, keep, cudaMemcpyDeviceToDevice, s));
-        B2_CUDA(cudaStreamSynchronize(s));
-        if (p)
-            cudaFree(p);
+        reset();
+        stream = s;
+        pooled = true;
         p = q;
         bytes = n;
     }

@@ -66,6 +66,28 @@ B2_DI u64 hash_words(Get&& w, u32 W)
     return mix64(h);
 }
 
+/// hash_words for a compile-time width NW (every loop unrolled, so register rows are indexed by constants); the
+/// trimmed length stays a run-time value: pair i is folded iff i + 1 < n, the odd tail iff i == n - 1.
+template<int NW, class Get>
+B2_DI u64 hash_words_fixed(Get&& w)
+{
+    u32 n = 0;
+#pragma unroll
+    for (int i = 0; i < NW; ++i)
+        n = w(i) != 0 ? static_cast<u32>(i + 1) : n;
+    u64 h = kHashSeed ^ (static_cast<u64>(n) * kHashP1);
+#pragma unroll
+    for (int i = 0; i < NW; i += 2)
+    {
+        const u64 a = w(i), b = i + 1 < NW ? w(i + 1) : 0;
+        if (static_cast<u32>(i) + 1 < n)
+            h = mulfold(h ^ a ^ kHashP1, b ^ kHashP2);
+        else if (static_cast<u32>(i) < n)
+            h = mulfold(h ^ a ^ kHashP1, kHashP2);
+    }
+    return mix64(h);
+}
+
 /// brfs_fingerprint_term (src/mymyr/search/brfs.cpp:34-37).
 B2_DI u64 fingerprint_term(u64 id, u64 canonical) { return mix64(id * 0x9E3779B97F4A7C15ULL ^ canonical); }
 
@@ -223,7 +245,33 @@ struct Store
 /// pass (a later kernel), so plain stores suffice. A slot holding a state of an earlier layer is compared in place
 /// (its row was written by an earlier kernel); an empty slot is claimed by CAS; a slot holding a candidate of this
 /// layer with the same tag defers the insert (row, hash and node record written first) to the resolve pass.
-template<class Row>
+/// Calls f(q) for q < NW (unrolled) or, with NW == 0, for q < W.
+template<int NW, class F>
+B2_DI void for_words(u32 W, F&& f)
+{
+    if constexpr (NW > 0)
+    {
+#pragma unroll
+        for (int q = 0; q < NW; ++q)
+            f(static_cast<u32>(q));
+    }
+    else
+        for (u32 q = 0; q < W; ++q)
+            f(q);
+}
+
+template<int NW, class Row>
+B2_DI void write_candidate(const Store& S, const Row& s, u64 h, u64 g, u32 i, u32 k)
+{
+    u64* r = S.rows + g * S.W;
+    for_words<NW>(S.W, [&](u32 q) { r[q] = s.word(q); });
+    S.hash[g] = h;
+    S.par[g] = i;
+    S.kid[g] = k;
+}
+
+/// NW: the row width when it is a compile-time constant (0: S.W at run time).
+template<int NW = 0, class Row>
 B2_DI void insert(const Store& S, const Row& s, u64 h, u64 g, u32 i, u32 k)
 {
     const u64 mine = (h & 0xFFFFFFFF00000000ull) | g;
@@ -236,12 +284,7 @@ B2_DI void insert(const Store& S, const Row& s, u64 h, u64 g, u32 i, u32 k)
             const u64 prev = atomicCAS(reinterpret_cast<unsigned long long*>(S.table + j), kEmpty, mine);
             if (prev == kEmpty)
             {
-                u64* r = S.rows + g * S.W;
-                for (u32 w = 0; w < S.W; ++w)
-                    r[w] = s.word(w);
-                S.hash[g] = h;
-                S.par[g] = i;
-                S.kid[g] = k;
+                write_candidate<NW>(S, s, h, g, i, k);
                 S.claimed[g - S.layer_cand_begin] = 1;
                 return;
             }
@@ -252,20 +295,14 @@ B2_DI void insert(const Store& S, const Row& s, u64 h, u64 g, u32 i, u32 k)
         const u64 og = cur & 0xFFFFFFFFull;
         if (og >= S.layer_cand_begin)
         {
-            u64* r = S.rows + g * S.W;
-            for (u32 w = 0; w < S.W; ++w)
-                r[w] = s.word(w);
-            S.hash[g] = h;
-            S.par[g] = i;
-            S.kid[g] = k;
+            write_candidate<NW>(S, s, h, g, i, k);
             const u32 q = atomicAdd(S.ndeferred, 1u);
             S.deferred[q] = (j << 32) | g;
             return;
         }
         const u64* r = S.rows + og * S.W;
         bool eq = true;
-        for (u32 w = 0; w < S.W && eq; ++w)
-            eq = __ldcg(r + w) == s.word(w);
+        for_words<NW>(S.W, [&](u32 q) { eq = eq && __ldcg(r + q) == s.word(q); });
         if (eq)
             return;  // a state of an earlier layer
     }

@@ -46,11 +46,15 @@ B2_DI void with_successor(const Row& st, const u32* b, F&& f)
     if constexpr (WR > 0)
     {
         Row nx = st;
-        for (u32 j = 0; j < nd; ++j)
-            nx.clear(del[j]);
-        for (u32 j = 0; j < na; ++j)
-            nx.set(add[j]);
-        const u64 h = hash_words([&](u32 q) { return nx.word(q); }, W);
+#pragma unroll
+        for (int j = 0; j < Eff<S>::ND; ++j)
+            if (static_cast<u32>(j) < nd)
+                nx.clear(del[j]);
+#pragma unroll
+        for (int j = 0; j < Eff<S>::NA; ++j)
+            if (static_cast<u32>(j) < na)
+                nx.set(add[j]);
+        const u64 h = hash_words_fixed<W>([&](u32 q) { return nx.word(q); });
         f(nx, h);
     }
     else
@@ -102,7 +106,9 @@ B2_DI void brfs_expand(const BrfsArgs& a)
         u32 k = 0;
         for_each_schema([&]<int S>() {
             Run<S, PI>::go(st, [&](const u32* b) {
-                with_successor<S>(st, b, [&](const auto& nx, u64 h) { insert(a.S, nx, h, g0 + k, static_cast<u32>(i), k); });
+                with_successor<S>(st, b, [&](const auto& nx, u64 h) {
+                    insert<(WR > 0 ? static_cast<int>(W) : 0)>(a.S, nx, h, g0 + k, static_cast<u32>(i), k);
+                });
                 ++k;
                 return true;
             });

@@ -59,6 +59,12 @@ class BrfsResult:
         """hash::state of every stored state, in id order."""
         return self._search.hashes(first, count)
 
+    def close(self) -> None:
+        """Releases the device state space (state_rows, nodes and state_hashes are unavailable afterwards)."""
+        if self._search is not None:
+            self._search.close()
+            self._search = None
+
 
 class _Search:
     def __init__(self, task: Task, opts: _lib.BrfsOptions):
@@ -102,11 +108,14 @@ class _Search:
         check(lib().b2_brfs_state_hashes(self._h, first, count, out.ctypes.data))
         return out
 
-    def __del__(self):
+    def close(self):
         h = getattr(self, "_h", None)
         if h is not None and h.value and _lib._lib is not None:
             _lib._lib.b2_brfs_destroy(h)
-            self._h = None
+        self._h = None
+
+    def __del__(self):
+        self.close()
 
 
 def brfs(task: Task, ctx: Context | None = None, witness_pruning: bool = True, canonical_order: bool = True,
