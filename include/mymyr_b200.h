@@ -164,6 +164,18 @@ typedef struct b2_expansion {
 b2_status b2_expand(b2_task* task, const uint64_t* states, uint64_t rows, uint32_t words, int witness_pruning,
                     b2_expansion* out, void* stream);
 
+/* b2_expand for callers that cannot allocate device memory while they run: processes that reserve the GPU's memory up
+ * front through their own allocator (a framework's caching allocator, a fixed per-process budget) and forbid other
+ * allocations, and latency-bound callers that cannot take the device-wide synchronization of cudaMalloc/cudaFree. It
+ * has no counterpart in the reference. Same arguments, results and errors as b2_expand; it calls no cudaMalloc,
+ * cudaFree or other allocating routine. Its scratch is a fixed array in the library's device memory (about 3 MB, held
+ * by every GPU that loads the library until the process exits), so a call takes at most 2^18 (state, schema) segments
+ * (rows x schemas) and refuses larger batches with B2_CAPACITY. The first call on a device looks up the array's
+ * device address (once per device), so make that first call before any stream capture. All calls share the array:
+ * calls that overlap on the GPU (other streams, other threads) race and must be serialized by the caller. */
+b2_status b2_expand_noalloc(b2_task* task, const uint64_t* states, uint64_t rows, uint32_t words, int witness_pruning,
+                            b2_expansion* out, void* stream);
+
 /* ------------------------------------------------------------------------------------------------ BrFS
  * The layer-synchronous breadth-first search of cuda::DeviceBrfs (include/mymyr/cuda/brfs.hpp:96-123) and mymyr::brfs
  * (include/mymyr/search/brfs.hpp:140): same states, ids, per-layer counts and fingerprint as the reference CPU BrFS

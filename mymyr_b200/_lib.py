@@ -126,6 +126,7 @@ SIGNATURES = {
     "b2_task_slot_atom": (C.c_int, [P, U32, P, U32]),
     "b2_hash_rows": (C.c_int, [P, P, U64, U32, P, P]),
     "b2_expand": (C.c_int, [P, P, U64, U32, C.c_int, C.POINTER(Expansion), P]),
+    "b2_expand_noalloc": (C.c_int, [P, P, U64, U32, C.c_int, C.POINTER(Expansion), P]),
     "b2_brfs_options_default": (None, [C.POINTER(BrfsOptions)]),
     "b2_brfs_create": (C.c_int, [P, C.POINTER(BrfsOptions), PP]),
     "b2_brfs_run": (C.c_int, [P, C.POINTER(BrfsResult)]),

@@ -5,6 +5,8 @@
 
 #include "scan.cuh"
 
+#include <mutex>
+
 namespace b2
 {
 namespace
@@ -176,5 +178,132 @@ extern "C" b2_status b2_expand(b2_task* task, const uint64_t* states, uint64_t r
                                          std::to_string(out->capacity));
         if (gen > (u64{1} << 31) - 1)
             throw Error(B2_CAPACITY, "b2_expand: more than 2^31 - 1 successors");
+    });
+}
+
+// ------------------------------------------------------------------------------------------------ b2_expand_noalloc
+// The batched expand without any allocation, for callers that cannot allocate device memory while they run: a
+// process that reserves the GPU's memory up front through its own allocator (a training or serving framework's caching
+// allocator, or a fixed per-process budget) and forbids other allocations, or a latency-bound caller for which the
+// device-wide synchronization of cudaMalloc/cudaFree is unacceptable. Its scratch (per-segment counts and offsets, the
+// scan's block sums, the total and a status word) lives in a file-scope __device__ array of kNoAllocScratchBytes
+// that every GPU loading this library holds until the process exits.
+
+namespace b2
+{
+namespace
+{
+/// Segments ((state, schema) pairs) a b2_expand_noalloc call may have.
+constexpr u64 kNoAllocMaxSegments = u64{1} << 18;
+constexpr size_t kNoAllocCounts = kNoAllocMaxSegments * 4;
+constexpr size_t kNoAllocOffsets = kNoAllocMaxSegments * 8;
+constexpr size_t kNoAllocSums = ((kNoAllocMaxSegments + kScanTile - 1) / kScanTile + 1) * 8;
+constexpr size_t kNoAllocScratchBytes = kNoAllocCounts + kNoAllocOffsets + 256 + kNoAllocSums;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[256] = {};  // per device: the device address of g_noalloc_scratch
+
+/// The device address of the scratch array on `device` (which must be current). The host-side name of the array is
+/// not a device address; its address on each device comes from cudaGetSymbolAddress, once per device.
+void* noalloc_scratch(int device)
+{
+    if (device < 0 || device >= 256)
+        throw std::invalid_argument("b2_expand_noalloc: device index out of range");
+    std::lock_guard lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[device])
+    {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p)
+            throw Error(B2_CUDA_ERROR, std::string("b2_expand_noalloc: cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+        g_noalloc_ptr[device] = p;
+    }
+    return g_noalloc_ptr[device];
+}
+}  // namespace
+}  // namespace b2
+
+extern "C" b2_status b2_expand_noalloc(b2_task* task, const uint64_t* states, uint64_t rows, uint32_t words,
+                                       int witness_pruning, b2_expansion* out, void* stream)
+{
+    return guarded([&] {
+        if (!task || !out || (rows && !states))
+            throw std::invalid_argument("b2_expand_noalloc: null argument");
+        if (!task->ctx)
+            throw std::invalid_argument("a host-only task (created without a context) cannot run on the device");
+        const Program& P = task->prog;
+        if (words != P.words)
+            throw std::invalid_argument("b2_expand_noalloc: rows of " + std::to_string(words) + " words; the task has " +
+                                        std::to_string(P.words));
+        if (out->binding && out->label_width < P.label_width)
+            throw std::invalid_argument("b2_expand_noalloc: label width below the largest schema arity");
+        if (out->succ && out->words < P.words)
+            throw std::invalid_argument("b2_expand_noalloc: successor rows narrower than the task's words");
+        if (witness_pruning && task->witness_refused)
+            throw Error(B2_UNSUPPORTED, "witness pruning with a witness parameter before an effect parameter");
+        const u64 nseg = rows * P.nschemas;
+        if (P.nschemas && rows > kNoAllocMaxSegments / P.nschemas)
+            throw Error(B2_CAPACITY, "b2_expand_noalloc: " + std::to_string(rows) + " states x " +
+                                         std::to_string(P.nschemas) + " schemas exceed its fixed scratch of " +
+                                         std::to_string(kNoAllocMaxSegments) +
+                                         " (state, schema) segments; use b2_expand or smaller batches");
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        B2_CUDA(cudaSetDevice(task->ctx->device));
+        char* base = static_cast<char*>(noalloc_scratch(task->ctx->device));
+        u32* counts = reinterpret_cast<u32*>(base);
+        u64* seg_off = reinterpret_cast<u64*>(base + kNoAllocCounts);
+        u64* total = reinterpret_cast<u64*>(base + kNoAllocCounts + kNoAllocOffsets);
+        u32* status = reinterpret_cast<u32*>(base + kNoAllocCounts + kNoAllocOffsets + 8);
+        u64* sums = reinterpret_cast<u64*>(base + kNoAllocCounts + kNoAllocOffsets + 256);
+        B2_CUDA(cudaMemsetAsync(status, 0, 4, s));  // the array keeps the last call's contents
+        const u32 pi = witness_pruning ? 0 : 1;
+        const unsigned grid = grid_for(nseg, 128, static_cast<unsigned>(task->ctx->sms) * 64);
+        dev::ExpandArgs a{};
+        a.states = states;
+        a.rows = rows;
+        a.W = words;
+        a.pi = pi;
+        a.counts = counts;
+        a.seg_off = seg_off;
+        a.capacity = out->capacity;
+        a.out_words = out->words;
+        a.label_width = out->label_width;
+        a.succ = out->succ;
+        a.parent = out->parent;
+        a.schema = out->schema;
+        a.binding = out->binding;
+        a.succ_hash = out->succ_hash;
+        a.status = status;
+        if (nseg && task->jit)
+            jit_launch(task->jit->expand_count[pi], grid, 128, &a, s);
+        else if (nseg)
+            dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
+                k_expand_count<OW, WR><<<grid, 128, 0, s>>>(task->dev, states, rows, words, pi, counts);
+            });
+        device_scan(SegCountIn{counts}, SegCountOut{seg_off}, nseg, total, sums, s);
+        if (nseg && task->jit)
+            jit_launch(task->jit->expand_write[pi], grid, 128, &a, s);
+        else if (nseg)
+            dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
+                k_expand_write<OW, WR><<<grid, 128, 0, s>>>(task->dev, states, rows, words, pi, seg_off, *out, status);
+            });
+        if (out->offsets)
+            k_offsets<<<grid_for(rows + 1, 256), 256, 0, s>>>(seg_off, rows, P.nschemas, total, out->offsets);
+        B2_CUDA(cudaGetLastError());
+        u64 gen = 0;
+        u32 st = 0;
+        B2_CUDA(cudaMemcpyAsync(&gen, total, 8, cudaMemcpyDeviceToHost, s));
+        B2_CUDA(cudaMemcpyAsync(&st, status, 4, cudaMemcpyDeviceToHost, s));
+        B2_CUDA(cudaStreamSynchronize(s));
+        out->generated = gen;
+        if (st)
+            throw Error(B2_DEVICE_FAULT, "b2_expand_noalloc: device status " + std::to_string(st));
+        if (gen > out->capacity && (out->succ || out->parent || out->schema || out->binding || out->succ_hash))
+            throw Error(B2_CAPACITY, "b2_expand_noalloc: " + std::to_string(gen) +
+                                         " successors exceed the capacity of " + std::to_string(out->capacity));
+        if (gen > (u64{1} << 31) - 1)
+            throw Error(B2_CAPACITY, "b2_expand_noalloc: more than 2^31 - 1 successors");
     });
 }
