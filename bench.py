@@ -1,13 +1,16 @@
 """Benchmark of the device path (one JSON line on rank 0).
 
-Headline workload (BASELINE config [3]): BrFS of the 4x4 sliding-tile task (60 seeded random blank moves from the
-solved layout, seed 0) to depth 22, the whole reachable space below that depth, witness pruning and canonical order on
-(mymyr::brfs defaults), stop_at_goal off. One step = one complete BrFS (22 expanded layers). Metric: BrFS expanded
-states/s. Secondary: env steps/s of config [2] (65,536 envs of the two-room, 40-ball transport task).
+Headline workload: BrFS of the 4x4 sliding-tile task (60 seeded random blank moves from the solved layout, seed 0) to
+depth 22, the whole reachable space below that depth, witness pruning and canonical order on (mymyr::brfs defaults),
+stop_at_goal off. One step = one complete BrFS (22 expanded layers). Metric: BrFS expanded states/s. Secondary: env
+steps/s of 65,536 envs of the two-room, 40-ball transport task.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--depth D]
 
-N > 1 runs under torchrun, one process per GPU. --impl reference times the reference's own CPU BrFS
+N > 1 runs under torchrun, one process per GPU, and shards the search by state-hash owner (NCCL reductions, NVLink
+peer-memory exchange of successors). Without --depth, N GPUs search to depth 22 + log2(N) (weak scaling: each layer
+of this space holds about 2.1 times the states of the one before, so the states per GPU stay about constant); with
+--depth the search is the same at every N (strong scaling). --impl reference times the reference's own CPU BrFS
 (oracle/_ref, mymyr::brfs with deterministic ids, all host threads) on the same workload.
 """
 
@@ -15,6 +18,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -29,7 +33,17 @@ sys.path.insert(0, str(ROOT))
 METRIC = "BrFS expanded states/sec"
 UNIT = "states/s"
 DEPTH = 22
-WORKLOAD = "sliding-tile 4x4 BrFS to depth 22 (BASELINE configs[2], seed 0, 60 scramble moves)"
+
+
+def workload(depth: int) -> str:
+    return f"sliding-tile 4x4 BrFS to depth {depth} (seed 0, 60 scramble moves, whole space below the depth)"
+
+
+def bench_depth(args, world: int) -> tuple[int, str]:
+    """The search depth at `world` GPUs and the scaling it gives."""
+    if args.depth is not None:
+        return args.depth, "strong" if world > 1 else "weak"
+    return DEPTH + max(0, round(math.log2(world))), "weak"
 
 
 def parse():
@@ -40,7 +54,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--env-steps", type=int, default=200)
     ap.add_argument("--no-secondary", action="store_true")
-    ap.add_argument("--depth", type=int, default=DEPTH, help="BrFS depth (profiling runs use a smaller case)")
+    ap.add_argument("--depth", type=int, default=None,
+                    help="BrFS depth at every N (default: 22 + log2(N), weak scaling; profiling runs use a smaller case)")
     ap.add_argument("--quick", action="store_true", help="timed BrFS only: no e2e, CPU baseline or env leg")
     return ap.parse_args()
 
@@ -131,24 +146,30 @@ def run_reference(args, world, rank):
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref not built (make -C oracle)"}))
         return
     threads = os.cpu_count() or 1
+    depth, scaling = bench_depth(args, world)
+    # a step is one reference BrFS; past depth 23 it takes a bounded sample of the workload (the same space to depth
+    # 23, the first 23 of its layers), so that the whole run ends within minutes
+    sample_depth = min(depth, 23)
     rt = ref.RefTask(tasks.sliding_tile(4, 4, 60, 0))
     for _ in range(args.warmup):
-        rt.brfs(threads=threads, max_depth=DEPTH, stop_at_goal=False, store="concurrent")
+        rt.brfs(threads=threads, max_depth=sample_depth, stop_at_goal=False, store="concurrent")
     times, expanded = [], 0
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        r = rt.brfs(threads=threads, max_depth=DEPTH, stop_at_goal=False, store="concurrent")
+        r = rt.brfs(threads=threads, max_depth=sample_depth, stop_at_goal=False, store="concurrent")
         times.append(time.perf_counter() - t0)
         expanded = r["expanded"]
     total = sum(times)
     value = expanded * args.steps / total
+    sample = (f"the full workload x {args.steps} runs" if sample_depth == depth else
+              f"the workload's first {sample_depth} layers ({expanded} expanded) x {args.steps} runs")
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1000 * total / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "u64", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "threads": threads, "store": "concurrent", "deterministic_ids": True},
+            "scaling": scaling, "vs_baseline": None, "dtype": "u64", "data": "synthetic",
+            "config": {"workload": workload(depth), "threads": threads, "store": "concurrent",
+                       "deterministic_ids": True},
             "impl": "reference",
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference",
-                             "sample": f"full workload x {args.steps} runs"},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference", "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -163,7 +184,7 @@ def cpu_baseline(steps_hint=1):
     rt = ref.RefTask(tasks.sliding_tile(4, 4, 60, 0))
     t0 = time.perf_counter()
     r = rt.brfs(threads=threads, max_depth=DEPTH, stop_at_goal=False, store="concurrent")
-    dt = time.perf_counter() - t0
+    dt = time.perf_counter() - t0  # the headline depth: cpu_baseline is taken at N = 1 only
     return {"value": r["expanded"] / dt, "unit": UNIT, "cores": threads, "kind": "reference",
             "sample": f"one full BrFS to depth {DEPTH} ({r['expanded']} expanded, {dt:.2f} s, mymyr::brfs "
                       f"concurrent store, {threads} threads)"}
@@ -191,7 +212,7 @@ def env_secondary(args, device):
         b.record(stream)
     stream.synchronize()
     ms = a.elapsed_time(b)
-    return {"metric": "env steps/sec (BASELINE configs[1]: 65,536 envs, transport 2 rooms/40 balls/2 grippers)",
+    return {"metric": "env steps/sec (65,536 envs, transport 2 rooms/40 balls/2 grippers)",
             "value": n * args.env_steps / (ms / 1000.0), "unit": "steps/s", "steps_timed": args.env_steps,
             "ms_per_step": ms / args.env_steps}
 
@@ -219,14 +240,20 @@ def main():
     from mymyr_b200.task import Context, Task
 
     ctx = Context(local)
+    comm = None
+    if world > 1:
+        from mymyr_b200.dist import Communicator
+
+        comm = Communicator(ctx)
+    depth, scaling = bench_depth(args, world)
     text = tasks.sliding_tile(4, 4, 60, 0)
     task = Task.from_text(text, ctx)
     stream = torch.cuda.Stream(device)
     sp = stream.cuda_stream
 
     def one(expected=None):
-        r = b2cuda.brfs(task, max_depth=args.depth, stop_at_goal=False, timings=True, expected_states=expected,
-                        stream=sp)
+        r = b2cuda.brfs(task, max_depth=depth, stop_at_goal=False, timings=True, expected_states=expected,
+                        stream=sp, comm=comm)
         r.close()  # free the search's device buffers now (back to the pool for the next step)
         return r
 
@@ -259,11 +286,18 @@ def main():
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         ms = float(t.item())
     expanded = results[-1].expanded
-    value = world * expanded * args.steps / (ms / 1000.0)
-    # roofline of expansion + dedup (k_expand and the winners' scan), from its device events
+    # every rank's search is the same one (sharded): the whole job expands `expanded` states per step
+    value = expanded * args.steps / (ms / 1000.0)
+    # roofline of expansion + dedup from its device events (a rank's share of the algorithmic bytes at N > 1, and its
+    # expansion + exchange + insert + id phases, the slowest rank's)
     W = task.words
-    bytes_run = algorithmic_bytes(results[-1].layer_counts, W)
+    bytes_run = algorithmic_bytes(results[-1].layer_counts, W) / world
     kern_ms = statistics.mean(r.stats.gen_ms + r.stats.dedup_ms for r in results)
+    exchanged = statistics.mean(r.stats.exchanged for r in results)
+    if pg is not None:
+        t = torch.tensor([kern_ms, exchanged], dtype=torch.float64, device=device)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        kern_ms, exchanged = float(t[0]), float(t[1])
     peak, peak_kind = measured_peaks()
     achieved = bytes_run / (kern_ms / 1000.0) / 1e9
     launches = sum(r.stats.kernel_launches for r in results)
@@ -271,8 +305,10 @@ def main():
     if args.quick:
         if rank == 0:
             print(json.dumps({"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-                              "depth": args.depth, "ms_per_step": ms / args.steps, "roofline_achieved": achieved,
+                              "depth": depth, "ms_per_step": ms / args.steps, "roofline_achieved": achieved,
                               "frac": achieved / peak, "quick": True}), flush=True)
+        if comm is not None:
+            comm.close()
         if pg is not None:
             pg.destroy_process_group()
         return
@@ -284,32 +320,37 @@ def main():
     for _ in range(args.steps):
         t0 = time.perf_counter()
         t2 = Task.from_text(text, ctx)
-        rr = b2cuda.brfs(t2, max_depth=args.depth, stop_at_goal=False, expected_states=expected, stream=sp)
-        hashes = rr.state_hashes()
+        rr = b2cuda.brfs(t2, max_depth=depth, stop_at_goal=False, expected_states=expected, stream=sp, comm=comm)
+        hashes = rr.local(rows=False, nodes=False)["hashes"]  # this rank's part of the visited set
         rr.close()
         e2e_times.append(time.perf_counter() - t0)
-        d2h = hashes.nbytes + 24 * rr.layers
+        d2h = hashes.nbytes + 8 * len(hashes) + 24 * rr.layers
     e2e_s = sum(e2e_times)
     if pg is not None:
         t = torch.tensor([e2e_s], dtype=torch.float64, device=device)
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         e2e_s = float(t.item())
-    e2e_value = world * expanded * args.steps / e2e_s
+    e2e_value = expanded * args.steps / e2e_s
 
     secondary = None if args.no_secondary else env_secondary(args, device)
     base = cpu_baseline() if rank == 0 and world == 1 else None
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": scaling,
             "vs_baseline": None, "dtype": "u64", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "states": results[-1].states, "expanded": expanded,
-                       "generated": results[-1].generated, "layers": results[-1].layers, "words": W,
-                       "parallelism": "replicas" if world > 1 else "single",
+            "config": {"workload": workload(depth), "depth": depth, "states": results[-1].states,
+                       "expanded": expanded, "generated": results[-1].generated, "layers": results[-1].layers,
+                       "words": W,
+                       "parallelism": (f"hash-owner sharded over {world} GPUs (NCCL all-reduce of counts and flags, "
+                                       "NVLink peer-memory push of successors)") if world > 1 else "single",
+                       "exchanged_per_rank": exchanged,
                        "l2": "working set > L2 (rows, table and frontiers are several hundred MB)",
                        "expected_states": "presized from the warm-up run"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None, "kernel": "k_expand + winners scan",
+                         "frac": achieved / peak, "traffic": None,
+                         "kernel": "b2j_brfs_expand + k_resolve + winners scan" if world == 1 else
+                                   "b2j_dbrfs_expand + k_push + k_dinsert + id scan (per rank)",
                          "algorithmic_bytes_per_run": bytes_run, "kernel_ms_per_run": kern_ms,
                          "peak_source": peak_kind},
             "cpu_baseline": base,
@@ -324,6 +365,8 @@ def main():
             "secondary": secondary,
         }
         print(json.dumps(line), flush=True)
+    if comm is not None:
+        comm.close()
     if pg is not None:
         pg.barrier()
         pg.destroy_process_group()

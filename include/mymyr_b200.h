@@ -176,10 +176,32 @@ b2_status b2_expand(b2_task* task, const uint64_t* states, uint64_t rows, uint32
 b2_status b2_expand_noalloc(b2_task* task, const uint64_t* states, uint64_t rows, uint32_t words, int witness_pruning,
                             b2_expansion* out, void* stream);
 
+/* ------------------------------------------------------------------------------------------------ communicators
+ * Multi-GPU searches run one process (or host thread) per GPU. Their ranks share an NCCL communicator for the
+ * reductions of each layer and map each other's receive buffers (CUDA IPC) for the exchange of successors. The
+ * reference has no multi-GPU layer; these have no counterpart in it. NCCL (libnccl.so.2) is loaded on first use;
+ * in a process that already loaded it (PyTorch) that copy is used. */
+typedef struct b2_comm b2_comm;
+typedef struct b2_comm_id {
+    char bytes[128]; /* an ncclUniqueId: made once (b2_comm_id_new) and handed to every rank */
+} b2_comm_id;
+b2_status b2_comm_id_new(b2_comm_id* out);
+/* Collective: every rank of `world` calls it with the same id and its own rank, on its own GPU's context. */
+b2_status b2_comm_create(b2_ctx* ctx, const b2_comm_id* id, uint32_t rank, uint32_t world, b2_comm** out);
+/* Seconds a rank waits for the others' part of a collective before it aborts the communicator and fails the call
+ * with B2_CUDA_ERROR (default 600): a rank that stopped taking part ends the others' searches instead of hanging them. */
+b2_status b2_comm_set_timeout(b2_comm* comm, double seconds);
+void b2_comm_destroy(b2_comm* comm);
+
 /* ------------------------------------------------------------------------------------------------ BrFS
  * The layer-synchronous breadth-first search of cuda::DeviceBrfs (include/mymyr/cuda/brfs.hpp:96-123) and mymyr::brfs
  * (include/mymyr/search/brfs.hpp:140): same states, ids, per-layer counts and fingerprint as the reference CPU BrFS
- * with deterministic ids. The state space stays on the device until b2_brfs_destroy. */
+ * with deterministic ids. The state space stays on the device until b2_brfs_destroy.
+ *
+ * With a communicator the search is sharded over its ranks: every state lives on the rank its hash::state selects
+ * (owner = high 32 bits of the hash x ranks >> 32), each rank expands the states it owns, and the successors go to
+ * their owners. Every rank calls b2_brfs_create and b2_brfs_run together and gets the same result; the ids, layer
+ * counts and fingerprint are those of the one-GPU search. A rank reads its own states with b2_brfs_local. */
 typedef struct b2_brfs_options {
     int32_t witness_pruning;  /* default 1 */
     int32_t stop_at_goal;     /* default 1 */
@@ -188,9 +210,10 @@ typedef struct b2_brfs_options {
     uint64_t max_states;      /* 0xFFFF...: no limit */
     uint64_t expected_states; /* pre-sizes the table and arenas (0: grow as needed) */
     int32_t timings;          /* per-phase device times in b2_brfs_result */
-    int32_t world_rank;       /* multi-GPU: this rank (0 for one GPU) */
+    int32_t world_rank;       /* multi-GPU: this rank (0 for one GPU; the communicator's rank when `comm` is set) */
     int32_t world_size;       /* multi-GPU: ranks sharing the frontier by state-hash owner (1: one GPU) */
     void* stream;             /* the stream the search runs on (NULL: a stream of its own) */
+    b2_comm* comm;            /* multi-GPU: the ranks' communicator (NULL: one GPU) */
 } b2_brfs_options;
 
 void b2_brfs_options_default(b2_brfs_options* o);
@@ -218,6 +241,8 @@ typedef struct b2_brfs_result {
     uint32_t table_log2;       /* out: log2 of the hash-set slots at the end */
     uint32_t rehashes;         /* out: table growths */
     uint32_t words;
+    uint64_t local_states;     /* out: states this rank stores (all of them on one GPU) */
+    uint64_t exchanged;        /* out: successors this rank received from other ranks (sharded search) */
 } b2_brfs_result;
 
 b2_status b2_brfs_create(b2_task* task, const b2_brfs_options* options, b2_brfs** out);
@@ -228,6 +253,13 @@ b2_status b2_brfs_states(b2_brfs* search, uint64_t first, uint64_t count, uint64
 b2_status b2_brfs_nodes(b2_brfs* search, uint64_t first, uint64_t count, uint32_t* parent, uint32_t* index);
 /* hash::state of every stored state, in id order, into host memory (the visited-state hash set). */
 b2_status b2_brfs_state_hashes(b2_brfs* search, uint64_t first, uint64_t count, uint64_t* hashes);
+/* The states this rank stores (all of them on one GPU), in id order: their count, and for local states
+ * [first, first + count) their ids, rows (`words` words each), hashes and node records, into host memory (NULL arrays
+ * are skipped). The states, nodes and state_hashes calls above serve one-GPU searches only. No counterpart in the
+ * reference (it has no sharded search). */
+b2_status b2_brfs_local_count(b2_brfs* search, uint64_t* count);
+b2_status b2_brfs_local(b2_brfs* search, uint64_t first, uint64_t count, uint64_t* ids, uint64_t* rows, uint32_t words,
+                        uint64_t* hashes, uint32_t* parent, uint32_t* index);
 void b2_brfs_destroy(b2_brfs* search);
 
 /* ------------------------------------------------------------------------------------------------ env step

@@ -75,7 +75,7 @@ class BrfsOptions(C.Structure):
     _fields_ = [("witness_pruning", C.c_int32), ("stop_at_goal", C.c_int32), ("fingerprint", C.c_int32),
                 ("max_depth", C.c_uint32), ("max_states", C.c_uint64), ("expected_states", C.c_uint64),
                 ("timings", C.c_int32), ("world_rank", C.c_int32), ("world_size", C.c_int32),
-                ("stream", C.c_void_p)]
+                ("stream", C.c_void_p), ("comm", C.c_void_p)]
 
 
 class BrfsResult(C.Structure):
@@ -85,7 +85,12 @@ class BrfsResult(C.Structure):
                 ("search_s", C.c_double), ("count_ms", C.c_double), ("gen_ms", C.c_double),
                 ("dedup_ms", C.c_double), ("kernel_launches", C.c_uint64),
                 ("layer_counts", C.POINTER(C.c_uint64)), ("layer_capacity", C.c_uint32),
-                ("table_log2", C.c_uint32), ("rehashes", C.c_uint32), ("words", C.c_uint32)]
+                ("table_log2", C.c_uint32), ("rehashes", C.c_uint32), ("words", C.c_uint32),
+                ("local_states", C.c_uint64), ("exchanged", C.c_uint64)]
+
+
+class CommId(C.Structure):
+    _fields_ = [("bytes", C.c_char * 128)]
 
 
 class EnvConfig(C.Structure):
@@ -127,12 +132,18 @@ SIGNATURES = {
     "b2_hash_rows": (C.c_int, [P, P, U64, U32, P, P]),
     "b2_expand": (C.c_int, [P, P, U64, U32, C.c_int, C.POINTER(Expansion), P]),
     "b2_expand_noalloc": (C.c_int, [P, P, U64, U32, C.c_int, C.POINTER(Expansion), P]),
+    "b2_comm_id_new": (C.c_int, [C.POINTER(CommId)]),
+    "b2_comm_create": (C.c_int, [P, C.POINTER(CommId), U32, U32, PP]),
+    "b2_comm_set_timeout": (C.c_int, [P, C.c_double]),
+    "b2_comm_destroy": (None, [P]),
     "b2_brfs_options_default": (None, [C.POINTER(BrfsOptions)]),
     "b2_brfs_create": (C.c_int, [P, C.POINTER(BrfsOptions), PP]),
     "b2_brfs_run": (C.c_int, [P, C.POINTER(BrfsResult)]),
     "b2_brfs_states": (C.c_int, [P, U64, U64, P, U32]),
     "b2_brfs_nodes": (C.c_int, [P, U64, U64, P, P]),
     "b2_brfs_state_hashes": (C.c_int, [P, U64, U64, P]),
+    "b2_brfs_local_count": (C.c_int, [P, C.POINTER(C.c_uint64)]),
+    "b2_brfs_local": (C.c_int, [P, U64, U64, P, P, U32, P, P, P]),
     "b2_brfs_destroy": (None, [P]),
     "b2_env_config_default": (None, [C.POINTER(EnvConfig)]),
     "b2_env_create": (C.c_int, [P, C.POINTER(EnvConfig), PP]),

@@ -21,7 +21,7 @@
 // candidate count -> k_expand (regenerate, hash, optimistic insert) -> k_resolve (deferred inserts) -> scan of winners
 // (ids) -> host reads the new-state count.
 
-#include "scan.cuh"
+#include "brfs.cuh"
 
 #include <chrono>
 
@@ -29,11 +29,6 @@ namespace b2
 {
 namespace
 {
-using dev::insert;
-using dev::kEmpty;
-using dev::LayerMisc;
-using dev::Store;
-
 /// Phase B: the deferred inserts, resumed at their slots. Every row they can meet was written by the expansion
 /// kernel (or an earlier one), so the comparisons need no ordering within this kernel. Among equal candidates of the
 /// layer the smallest g takes the slot by atomicMin (the tag sits above g); a displaced one is marked lost.
@@ -84,31 +79,6 @@ __global__ void k_resolve(Store S)
         }
         if (!done)
             atomicOr(S.status, kStatusProbeLimit);
-    }
-}
-
-template<int OW, int WR>
-__global__ void __launch_bounds__(128) k_count(DevTask T, u32 pi, const u64* __restrict__ rows, u32 W,
-                                               const u32* __restrict__ frontier, u64 E, u32* __restrict__ counts,
-                                               LayerMisc* misc)
-{
-    for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < E; i += static_cast<u64>(gridDim.x) * blockDim.x)
-    {
-        const u64 g = frontier[i];
-        const auto st = load_row<WR>(rows + g * W, W);
-        if (goal_holds(T, st))
-        {
-            atomicAdd(&misc->goals, 1u);
-            atomicMin(&misc->first_goal, static_cast<u32>(i));
-        }
-        u32 c = 0;
-        u32 bind[kMaxLevels] = {};
-        for (u32 s = 0; s < T.nschemas; ++s)
-            enumerate<OW>(T, T.schemas[s].prog[pi], st, bind, [&](const u32*) {
-                ++c;
-                return true;
-            });
-        counts[i] = c;
     }
 }
 
@@ -173,24 +143,6 @@ __global__ void k_seed_root(Store S, u32* state_g)
         atomicOr(S.status, kStatusProbeLimit);
 }
 
-__global__ void k_rehash(u64* __restrict__ table, u64 mask, u32 max_probe, const u32* __restrict__ state_g, u64 n,
-                         const u64* __restrict__ hash, u32* status)
-{
-    for (u64 id = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; id < n; id += static_cast<u64>(gridDim.x) * blockDim.x)
-    {
-        const u64 g = state_g[id];
-        const u64 h = hash[g];
-        const u64 mine = (h & 0xFFFFFFFF00000000ull) | g;
-        u64 j = h & mask;
-        u32 probe = 0;
-        for (; probe < max_probe; ++probe, j = (j + 1) & mask)
-            if (atomicCAS(reinterpret_cast<unsigned long long*>(table + j), kEmpty, mine) == kEmpty)
-                break;
-        if (probe == max_probe)
-            atomicOr(status, kStatusProbeLimit);
-    }
-}
-
 struct WinIn
 {
     const u8* claimed;
@@ -206,16 +158,6 @@ struct WinOut
         if (v)
             state_g[rank] = static_cast<u32>(cand_begin + c);
     }
-};
-struct CountIn
-{
-    const u32* c;
-    __device__ __forceinline__ u32 operator()(u64 i) const { return c[i]; }
-};
-struct BaseOut
-{
-    u64* base;
-    __device__ __forceinline__ void operator()(u64 i, u64 e, u32) const { base[i] = e; }
 };
 
 __global__ void k_fingerprint(const u32* __restrict__ state_g, u64 first_id, u64 n, const u64* __restrict__ rows,
@@ -285,34 +227,6 @@ __global__ void k_gather_nodes(const u32* __restrict__ state_g, u64 first, u64 n
 
 using namespace b2;
 
-struct b2_brfs
-{
-    b2_task* task = nullptr;
-    b2_brfs_options opt{};
-    cudaStream_t stream = nullptr;
-    u32 W = 1;
-    // per candidate
-    DeviceBuffer rows, hash, par, kid;
-    u64 cap_cand = 0;
-    // per state
-    DeviceBuffer state_g;
-    u64 cap_states = 0;
-    // hash set
-    DeviceBuffer table;
-    u64 table_slots = 0;
-    u32 rehashes = 0;
-    // per layer scratch
-    DeviceBuffer counts, cand_base, flags, deferred, sums, misc;
-    u64 cap_layer = 0, cap_flags = 0;
-    dev::LayerMisc* misc_host = nullptr;  // pinned mirror of `misc`
-    // results
-    std::vector<u64> layer_begin;  // id of each layer's first state (+ the end)
-    u64 n_states = 0;
-    u64 launches = 0;
-    bool ran = false;
-    bool own_stream = false;
-};
-
 namespace
 {
 void ensure_cand(b2_brfs& B, u64 need, u64 used)
@@ -356,8 +270,6 @@ void ensure_layer(b2_brfs& B, u64 E, u64 G)
         B.cap_flags = cap;
     }
 }
-
-u32 max_probe(u64 slots) { return static_cast<u32>(std::min<u64>(slots, u64{1} << 20)); }
 
 /// Grows the hash set so that `states` entries keep it at most half full, and reinserts the stored states.
 void ensure_table(b2_brfs& B, u64 states)
@@ -661,8 +573,17 @@ b2_status b2_brfs_create(b2_task* task, const b2_brfs_options* options, b2_brfs*
             throw std::invalid_argument("a host-only task (created without a context) cannot run on the device");
         if (options->max_states != ~uint64_t{0})
             throw Error(B2_UNSUPPORTED, "b2_brfs: max_states is not supported by the device BrFS yet");
-        if (options->world_size != 1)
-            throw Error(B2_UNSUPPORTED, "b2_brfs: use the multi-GPU driver for world_size > 1");
+        if (options->comm)
+        {
+            if (options->comm->device != task->ctx->device)
+                throw std::invalid_argument("b2_brfs_create: the communicator belongs to another device");
+            if ((options->world_size != 1 || options->world_rank != 0) &&
+                (options->world_size != static_cast<int32_t>(options->comm->world) ||
+                 options->world_rank != static_cast<int32_t>(options->comm->rank)))
+                throw std::invalid_argument("b2_brfs_create: world_rank/world_size differ from the communicator's");
+        }
+        else if (options->world_size != 1 || options->world_rank != 0)
+            throw std::invalid_argument("b2_brfs_create: world_size > 1 needs a communicator (options.comm)");
         if (options->witness_pruning && task->witness_refused)
             throw Error(B2_UNSUPPORTED, "witness pruning with a witness parameter before an effect parameter");
         B2_CUDA(cudaSetDevice(task->ctx->device));
@@ -670,6 +591,7 @@ b2_status b2_brfs_create(b2_task* task, const b2_brfs_options* options, b2_brfs*
         b->task = task;
         b->opt = *options;
         b->W = task->prog.words;
+        b->comm = options->comm;
         if (options->stream)
             b->stream = static_cast<cudaStream_t>(options->stream);
         else
@@ -695,13 +617,21 @@ b2_status b2_brfs_run(b2_brfs* search, b2_brfs_result* result)
         *result = b2_brfs_result{};
         result->layer_counts = lc;
         result->layer_capacity = cap;
-        run_search(*search, *result);
+        if (search->comm)
+            shard_run(*search, *result);
+        else
+        {
+            run_search(*search, *result);
+            result->local_states = search->n_states;
+        }
     });
 }
 
 b2_status b2_brfs_states(b2_brfs* B, uint64_t first, uint64_t count, uint64_t* rows, uint32_t words)
 {
     return guarded([&] {
+        if (B && B->comm)
+            throw std::invalid_argument("b2_brfs_states: a sharded search's states are read per rank (b2_brfs_local)");
         if (!B || (count && !rows) || !B->ran)
             throw std::invalid_argument("b2_brfs_states: bad argument");
         if (first + count > B->n_states || words < B->W)
@@ -721,6 +651,8 @@ b2_status b2_brfs_states(b2_brfs* B, uint64_t first, uint64_t count, uint64_t* r
 b2_status b2_brfs_state_hashes(b2_brfs* B, uint64_t first, uint64_t count, uint64_t* hashes)
 {
     return guarded([&] {
+        if (B && B->comm)
+            throw std::invalid_argument("b2_brfs_state_hashes: a sharded search's states are read per rank (b2_brfs_local)");
         if (!B || (count && !hashes) || !B->ran || first + count > B->n_states)
             throw std::invalid_argument("b2_brfs_state_hashes: bad argument");
         if (!count)
@@ -738,6 +670,8 @@ b2_status b2_brfs_state_hashes(b2_brfs* B, uint64_t first, uint64_t count, uint6
 b2_status b2_brfs_nodes(b2_brfs* B, uint64_t first, uint64_t count, uint32_t* parent, uint32_t* index)
 {
     return guarded([&] {
+        if (B && B->comm)
+            throw std::invalid_argument("b2_brfs_nodes: a sharded search's states are read per rank (b2_brfs_local)");
         if (!B || (count && (!parent || !index)) || !B->ran || first + count > B->n_states)
             throw std::invalid_argument("b2_brfs_nodes: bad argument");
         if (!count)
@@ -757,10 +691,63 @@ b2_status b2_brfs_nodes(b2_brfs* B, uint64_t first, uint64_t count, uint32_t* pa
     });
 }
 
+static void rethrow(b2_status st)
+{
+    if (st == B2_OK)
+        return;
+    char msg[1024];
+    b2_last_error(msg, sizeof msg);
+    throw Error(st, msg);
+}
+
+b2_status b2_brfs_local_count(b2_brfs* B, uint64_t* count)
+{
+    return guarded([&] {
+        if (!B || !count || !B->ran)
+            throw std::invalid_argument("b2_brfs_local_count: bad argument");
+        *count = B->comm ? shard_local_count(*B) : B->n_states;
+    });
+}
+
+b2_status b2_brfs_local(b2_brfs* B, uint64_t first, uint64_t count, uint64_t* ids, uint64_t* rows, uint32_t words,
+                        uint64_t* hashes, uint32_t* parent, uint32_t* index)
+{
+    return guarded([&] {
+        if (!B || !B->ran)
+            throw std::invalid_argument("b2_brfs_local: bad argument");
+        B2_CUDA(cudaSetDevice(B->task->ctx->device));
+        if (B->comm)
+        {
+            shard_local(*B, first, count, ids, rows, words, hashes, parent, index);
+            return;
+        }
+        if (first + count > B->n_states || (rows && words < B->W))
+            throw std::invalid_argument("b2_brfs_local: range or width out of bounds");
+        if (ids)
+            for (uint64_t i = 0; i < count; ++i)
+                ids[i] = first + i;
+        if (rows)
+            rethrow(b2_brfs_states(B, first, count, rows, words));
+        if (hashes)
+            rethrow(b2_brfs_state_hashes(B, first, count, hashes));
+        if (parent || index)
+        {
+            std::vector<uint32_t> p(parent ? 0 : count), k(index ? 0 : count);
+            rethrow(b2_brfs_nodes(B, first, count, parent ? parent : p.data(), index ? index : k.data()));
+        }
+    });
+}
+
 void b2_brfs_destroy(b2_brfs* search)
 {
     if (!search)
         return;
+    if (search->shard)
+    {
+        cudaSetDevice(search->task->ctx->device);
+        cudaStreamSynchronize(search->stream);
+        shard_free(*search);
+    }
     if (search->stream)
     {
         cudaStreamSynchronize(search->stream);

@@ -1,0 +1,119 @@
+// Internal: the BrFS search object (brfs.cu, one GPU; dbrfs.cu, sharded over ranks) and the kernels both use.
+
+#pragma once
+
+#include "comm.hpp"
+#include "scan.cuh"
+
+#include <vector>
+
+namespace b2
+{
+namespace
+{
+using dev::insert;
+using dev::kEmpty;
+using dev::LayerMisc;
+using dev::Store;
+
+template<int OW, int WR>
+__global__ void __launch_bounds__(128) k_count(DevTask T, u32 pi, const u64* __restrict__ rows, u32 W,
+                                               const u32* __restrict__ frontier, u64 E, u32* __restrict__ counts,
+                                               LayerMisc* misc)
+{
+    for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < E; i += static_cast<u64>(gridDim.x) * blockDim.x)
+    {
+        const u64 g = frontier[i];
+        const auto st = load_row<WR>(rows + g * W, W);
+        if (goal_holds(T, st))
+        {
+            atomicAdd(&misc->goals, 1u);
+            atomicMin(&misc->first_goal, static_cast<u32>(i));
+        }
+        u32 c = 0;
+        u32 bind[kMaxLevels] = {};
+        for (u32 s = 0; s < T.nschemas; ++s)
+            enumerate<OW>(T, T.schemas[s].prog[pi], st, bind, [&](const u32*) {
+                ++c;
+                return true;
+            });
+        counts[i] = c;
+    }
+}
+
+/// Reinserts the states `state_g[0, n)` (arena indices) into an empty table.
+__global__ void k_rehash(u64* __restrict__ table, u64 mask, u32 max_probe, const u32* __restrict__ state_g, u64 n,
+                         const u64* __restrict__ hash, u32* status)
+{
+    for (u64 id = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; id < n; id += static_cast<u64>(gridDim.x) * blockDim.x)
+    {
+        const u64 g = state_g[id];
+        const u64 h = hash[g];
+        const u64 mine = (h & 0xFFFFFFFF00000000ull) | g;
+        u64 j = h & mask;
+        u32 probe = 0;
+        for (; probe < max_probe; ++probe, j = (j + 1) & mask)
+            if (atomicCAS(reinterpret_cast<unsigned long long*>(table + j), kEmpty, mine) == kEmpty)
+                break;
+        if (probe == max_probe)
+            atomicOr(status, kStatusProbeLimit);
+    }
+}
+
+struct CountIn
+{
+    const u32* c;
+    __device__ __forceinline__ u32 operator()(u64 i) const { return c[i]; }
+};
+struct BaseOut
+{
+    u64* base;
+    __device__ __forceinline__ void operator()(u64 i, u64 e, u32) const { base[i] = e; }
+};
+
+inline u32 max_probe(u64 slots) { return static_cast<u32>(std::min<u64>(slots, u64{1} << 20)); }
+}  // namespace
+
+struct ShardState;
+}  // namespace b2
+
+struct b2_brfs
+{
+    b2_task* task = nullptr;
+    b2_brfs_options opt{};
+    cudaStream_t stream = nullptr;
+    b2::u32 W = 1;
+    // per candidate
+    b2::DeviceBuffer rows, hash, par, kid;
+    b2::u64 cap_cand = 0;
+    // per state
+    b2::DeviceBuffer state_g;
+    b2::u64 cap_states = 0;
+    // hash set
+    b2::DeviceBuffer table;
+    b2::u64 table_slots = 0;
+    b2::u32 rehashes = 0;
+    // per layer scratch
+    b2::DeviceBuffer counts, cand_base, flags, deferred, sums, misc;
+    b2::u64 cap_layer = 0, cap_flags = 0;
+    b2::dev::LayerMisc* misc_host = nullptr;  // pinned mirror of `misc`
+    // results
+    std::vector<b2::u64> layer_begin;  // id of each layer's first state (+ the end)
+    b2::u64 n_states = 0;
+    b2::u64 launches = 0;
+    bool ran = false;
+    bool own_stream = false;
+    // sharded search (options.comm set)
+    b2_comm* comm = nullptr;
+    b2::ShardState* shard = nullptr;
+};
+
+namespace b2
+{
+/// The sharded search (dbrfs.cu): run, the rank's states, release.
+void shard_run(b2_brfs& B, b2_brfs_result& R);
+u64 shard_local_count(const b2_brfs& B);
+void shard_local(b2_brfs& B, u64 first, u64 count, u64* ids, u64* rows, u32 words, u64* hashes, u32* parent,
+                 u32* index);
+void shard_free(b2_brfs& B);
+}  // namespace b2

@@ -333,6 +333,44 @@ struct BrfsArgs
     u32 pi;               // 0: witness pruning, 1: off
 };
 
+// ------------------------------------------------------------------------------------------------ sharded BrFS
+constexpr u32 kMaxWorld = 64;
+
+/// The owner rank of a state hash among `world` ranks: the high 32 bits of the hash, scaled to [0, world).
+B2_DI u32 owner_of(u64 h, u32 world) { return static_cast<u32>(((h >> 32) * world) >> 32); }
+
+/// Per-layer values of a sharded search (device side, mirrored to pinned host memory).
+struct DistMisc
+{
+    LayerMisc lm;     // count pass over the local parents: goals, first local goal, status
+    u64 total_local;  // local candidates of the layer (scan of the local counts)
+    u64 goal_id;      // smallest goal id among the layer's parents (this rank's, then the MIN over ranks)
+    u64 new_packed;   // new states of the layer: all ranks | this rank's << 32
+    u64 recv;         // candidates this rank received
+    u64 fingerprint;
+    u32 goals_all;    // goal parents of the layer over all ranks
+    u32 barrier;      // reduced by all ranks between the exchange and the inserts
+};
+
+/// Arguments of the sharded expansion: each local parent's successors are staged as records [row | hash | c], c the
+/// successor's candidate index within the layer in canonical order (parent id, successor index) over all ranks.
+struct DExpandArgs
+{
+    const u64* rows;         // the rank's arena rows (parents)
+    const u32* frontier;     // arena index of each local parent (local parents are in id order)
+    const u32* frontier_id;  // id of each local parent
+    u64 E;                   // local parents
+    u64 layer_begin;         // id of the layer's first state
+    u64 limit;               // expand the parents with id < limit
+    const u64* gbase;        // [layer states] candidate offset of each parent of the layer (all ranks)
+    const u64* local_base;   // [E] staging record of each local parent's first successor
+    u64* staging;            // [local candidates, W + 2]
+    u64* hist;               // [world] staged records per owner rank
+    u32 world;
+    u32 W;
+    u32 pi;                  // 0: witness pruning, 1: off
+};
+
 /// Arguments of the env kernels (b2_env_batch and b2_step_out, flattened).
 struct EnvArgs
 {

@@ -116,6 +116,46 @@ B2_DI void brfs_expand(const BrfsArgs& a)
     }
 }
 
+/// Sharded BrFS: stages every successor of the local parents with id < limit as [row | hash | c] and counts the
+/// records per owner rank (block-local counts, then one atomic per block and rank).
+template<int PI>
+B2_DI void dbrfs_expand(const DExpandArgs& a)
+{
+    __shared__ u32 hist[kMaxWorld];
+    for (u32 d = threadIdx.x; d < a.world; d += blockDim.x)
+        hist[d] = 0;
+    __syncthreads();
+    for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < a.E; i += static_cast<u64>(gridDim.x) * blockDim.x)
+    {
+        const u64 id = a.frontier_id[i];
+        if (id >= a.limit)
+            continue;
+        const Row st = RowSel<WR>::load(a.rows + static_cast<u64>(a.frontier[i]) * W);
+        const u64 c0 = a.gbase[id - a.layer_begin];
+        u64* out = a.staging + a.local_base[i] * (W + 2);
+        u32 k = 0;
+        for_each_schema([&]<int S>() {
+            Run<S, PI>::go(st, [&](const u32* b) {
+                with_successor<S>(st, b, [&](const auto& nx, u64 h) {
+                    u64* r = out + static_cast<u64>(k) * (W + 2);
+#pragma unroll
+                    for (u32 q = 0; q < W; ++q)
+                        r[q] = nx.word(q);
+                    r[W] = h;
+                    r[W + 1] = c0 + k;
+                    atomicAdd(&hist[owner_of(h, a.world)], 1u);
+                });
+                ++k;
+                return true;
+            });
+        });
+    }
+    __syncthreads();
+    for (u32 d = threadIdx.x; d < a.world; d += blockDim.x)
+        if (hist[d])
+            atomicAdd(reinterpret_cast<unsigned long long*>(a.hist + d), static_cast<unsigned long long>(hist[d]));
+}
+
 // ------------------------------------------------------------------------------------------------ env
 template<int PI>
 B2_DI void env_init(const EnvArgs& a)
@@ -341,6 +381,8 @@ extern "C" __global__ void __launch_bounds__(128) b2j_brfs_count_w(b2::dev::Brfs
 extern "C" __global__ void __launch_bounds__(128) b2j_brfs_count_nw(b2::dev::BrfsArgs a) { b2::gen::brfs_count<1>(a); }
 extern "C" __global__ void __launch_bounds__(128) b2j_brfs_expand_w(b2::dev::BrfsArgs a) { b2::gen::brfs_expand<0>(a); }
 extern "C" __global__ void __launch_bounds__(128) b2j_brfs_expand_nw(b2::dev::BrfsArgs a) { b2::gen::brfs_expand<1>(a); }
+extern "C" __global__ void __launch_bounds__(128) b2j_dbrfs_expand_w(b2::dev::DExpandArgs a) { b2::gen::dbrfs_expand<0>(a); }
+extern "C" __global__ void __launch_bounds__(128) b2j_dbrfs_expand_nw(b2::dev::DExpandArgs a) { b2::gen::dbrfs_expand<1>(a); }
 extern "C" __global__ void b2j_env_init_w(b2::dev::EnvArgs a) { b2::gen::env_init<0>(a); }
 extern "C" __global__ void b2j_env_init_nw(b2::dev::EnvArgs a) { b2::gen::env_init<1>(a); }
 extern "C" __global__ void __launch_bounds__(128) b2j_env_step_w(b2::dev::EnvArgs a) { b2::gen::env_step<0>(a); }

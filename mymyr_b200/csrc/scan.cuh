@@ -1,5 +1,6 @@
 // Device-wide exclusive scan in three launches (tile sums, one-block scan of the sums, tile apply), generic over an
-// input functor (u32 value of element i) and an output functor (called with i, its exclusive prefix and its value).
+// input functor (the u32 or u64 value of element i) and an output functor (called with i, its exclusive prefix and its
+// value). Prefixes are u64.
 // Used for candidate offsets (successor counts per parent), CSR offsets and the ranks of new states.
 
 #pragma once
@@ -42,8 +43,9 @@ __global__ void __launch_bounds__(kScanBlock) k_tile_apply(In in, u64 n, const u
 {
     using Scan = cub::BlockScan<u64, kScanBlock>;
     __shared__ typename Scan::TempStorage tmp;
+    using V = decltype(in(u64{0}));
     const u64 base = blockIdx.x * kScanTile;
-    u32 v[kScanItems];
+    V v[kScanItems];
     u64 e[kScanItems];
 #pragma unroll
     for (int k = 0; k < kScanItems; ++k)

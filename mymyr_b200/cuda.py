@@ -26,6 +26,8 @@ class DeviceBrfsStats:
     rehashes: int = 0
     table_slots: int = 0
     kernel_launches: int = 0
+    local_states: int = 0  # states this rank stores (all of them on one GPU)
+    exchanged: int = 0     # successors this rank received from other ranks (sharded search)
 
 
 @dataclass
@@ -58,6 +60,13 @@ class BrfsResult:
     def state_hashes(self, first: int = 0, count: int | None = None) -> np.ndarray:
         """hash::state of every stored state, in id order."""
         return self._search.hashes(first, count)
+
+    def local(self, first: int = 0, count: int | None = None, *, rows: bool = True, hashes: bool = True,
+              nodes: bool = True) -> dict:
+        """The states this rank stores (all states on one GPU), in id order: ``ids`` and, as asked, ``rows``,
+        ``hashes``, ``parent`` and ``index`` (numpy arrays). A sharded search's states are read this way, per rank;
+        ``mymyr_b200.dist.gather_states`` assembles them over the ranks."""
+        return self._search.local(first, count, rows=rows, hashes=hashes, nodes=nodes)
 
     def close(self) -> None:
         """Releases the device state space (state_rows, nodes and state_hashes are unavailable afterwards)."""
@@ -108,6 +117,24 @@ class _Search:
         check(lib().b2_brfs_state_hashes(self._h, first, count, out.ctypes.data))
         return out
 
+    def local(self, first=0, count=None, *, rows=True, hashes=True, nodes=True):
+        n = C.c_uint64()
+        check(lib().b2_brfs_local_count(self._h, C.byref(n)))
+        if count is None:
+            count = n.value - first
+        out = {"ids": np.zeros(count, np.uint64)}
+        if rows:
+            out["rows"] = np.zeros((count, self.task.words), np.uint64)
+        if hashes:
+            out["hashes"] = np.zeros(count, np.uint64)
+        if nodes:
+            out["parent"] = np.zeros(count, np.uint32)
+            out["index"] = np.zeros(count, np.uint32)
+        ptr = lambda k: out[k].ctypes.data if k in out else None  # noqa: E731
+        check(lib().b2_brfs_local(self._h, first, count, ptr("ids"), ptr("rows"), self.task.words, ptr("hashes"),
+                                  ptr("parent"), ptr("index")))
+        return out
+
     def close(self):
         h = getattr(self, "_h", None)
         if h is not None and h.value and _lib._lib is not None:
@@ -121,10 +148,12 @@ class _Search:
 def brfs(task: Task, ctx: Context | None = None, witness_pruning: bool = True, canonical_order: bool = True,
          max_states: int | None = None, stop_at_goal: bool = True, fingerprint: bool = False,
          chunk_states: int | None = None, expected_states: int | None = None, max_depth: int | None = None,
-         timings: bool = False, stream=None) -> BrfsResult:
+         timings: bool = False, stream=None, comm=None) -> BrfsResult:
     """The device BrFS (cuda::brfs). Ids, per-layer counts and the fingerprint equal the reference CPU BrFS with
     deterministic ids. ``chunk_states`` is accepted for signature compatibility: layers are never chunked here, and
-    ids do not depend on it."""
+    ids do not depend on it. ``comm`` (a ``mymyr_b200.dist.Communicator``) shards the search over its ranks by state
+    hash: every rank calls brfs together and gets the same result; each rank reads its own states with
+    ``BrfsResult.local``."""
     if not canonical_order:
         raise ValueError("mymyr_b200 brfs: canonical_order=False is not supported (ids are defined in canonical order)")
     if ctx is not None and task.ctx is not None and ctx.device != task.ctx.device:
@@ -143,6 +172,9 @@ def brfs(task: Task, ctx: Context | None = None, witness_pruning: bool = True, c
         o.expected_states = int(expected_states)
     if stream is not None:
         o.stream = stream
+    if comm is not None:
+        o.comm = comm.handle
+        o.world_rank, o.world_size = comm.rank, comm.world
     s = _Search(task, o)
     r = s.run()
     res = BrfsResult(status=STATUS.get(r.status, str(r.status)), states=r.states, expanded=r.expanded,
@@ -151,7 +183,7 @@ def brfs(task: Task, ctx: Context | None = None, witness_pruning: bool = True, c
                      solved=bool(r.solved), goal_id=r.goal_id, fingerprint=r.fingerprint, search_s=r.search_s,
                      words=r.words,
                      stats=DeviceBrfsStats(r.count_ms, r.gen_ms, r.dedup_ms, r.rehashes, 1 << r.table_log2,
-                                           r.kernel_launches), _search=s)
+                                           r.kernel_launches, r.local_states, r.exchanged), _search=s)
     return res
 
 

@@ -1,0 +1,110 @@
+"""The sharded BrFS on 2+ GPUs (one process per GPU, NCCL) against the reference: the same states, ids, node records,
+hashes, layer counts and fingerprint as the reference's CPU BrFS with deterministic ids, on both matcher backends.
+Skipped on a box with fewer than two GPUs."""
+
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+from mymyr_b200 import tasks
+
+pytestmark = pytest.mark.gpu
+
+CASES = [
+    # name, text, max_depth, witness pruning, stop at goal
+    ("tower5", tasks.tower(5, 3), None, True, False),
+    ("transport_2_6_2", tasks.transport(2, 6, 2, 0), None, True, False),
+    ("transport_2_6_2_nw", tasks.transport(2, 6, 2, 0), None, False, False),
+    ("tile3x3", tasks.sliding_tile(3, 3, 30, 0), None, True, False),
+    ("tile4x4_d12", tasks.sliding_tile(4, 4, 60, 0), 12, True, False),
+    ("tower7_goal", tasks.tower(7, 0), None, True, True),
+    ("tile3x3_goal", tasks.sliding_tile(3, 3, 30, 0), None, True, True),
+]
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, matcher, out):
+    import torch.distributed as td
+
+    from mymyr_b200 import Context, Task, cuda
+    from mymyr_b200 import dist as bdist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    td.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                          timeout=datetime.timedelta(seconds=120))
+    try:
+        ctx = Context(rank)
+        comm = bdist.Communicator(ctx, timeout_s=60)
+        for name, text, depth, witness, stop in CASES:
+            task = Task.from_text(text, ctx, matcher=matcher)
+            r = cuda.brfs(task, comm=comm, max_depth=depth, stop_at_goal=stop, fingerprint=True,
+                          witness_pruning=witness)
+            g = bdist.gather_states(r)
+            if rank == 0:
+                out[name] = {"states": r.states, "expanded": r.expanded, "generated": r.generated,
+                             "layer_counts": r.layer_counts, "fingerprint": r.fingerprint, "solved": r.solved,
+                             "goal_id": r.goal_id, "num_goal_states": r.num_goal_states, "rows": g["rows"],
+                             "parent": g["parent"], "index": g["index"], "hashes": g["hashes"]}
+            out[(name, rank)] = (r.stats.local_states, r.stats.exchanged, r.states, r.fingerprint)
+            r.close()
+        comm.close()
+        td.barrier()
+    finally:
+        td.destroy_process_group()
+
+
+def _run(world, matcher):
+    import torch.multiprocessing as mp
+
+    mgr = mp.get_context("spawn").Manager()
+    out = mgr.dict()
+    mp.start_processes(_worker, args=(world, _free_port(), matcher, out), nprocs=world, join=True,
+                       start_method="spawn")
+    return dict(out)
+
+
+def _worlds():
+    n = torch.cuda.device_count() if torch.cuda.is_available() else 0
+    return sorted({2, n}) if n >= 2 else [2]
+
+
+@pytest.mark.parametrize("matcher", ["compiled", "interpreted"])
+@pytest.mark.parametrize("world", _worlds())
+def test_sharded_brfs_matches_reference(ref, world, matcher):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    from oracle import ref as oref
+
+    out = _run(world, matcher)
+    for name, text, depth, witness, stop in CASES:
+        got = out[name]
+        t = oref.RefTask(text)
+        exp = t.brfs(max_depth=depth, stop_at_goal=stop, witness_pruning=witness, fingerprint=True)
+        assert got["states"] == exp["states"], name
+        assert got["layer_counts"] == exp["layer_counts"], name
+        assert got["fingerprint"] == exp["fingerprint"], name
+        assert bool(got["solved"]) == bool(exp["solved"]), name
+        assert got["num_goal_states"] == exp["num_goal_states"], name
+        per_rank = [out[(name, r)] for r in range(world)]
+        assert sum(p[0] for p in per_rank) == got["states"], name  # the shards partition the states
+        assert len({(p[2], p[3]) for p in per_rank}) == 1, name    # every rank reports the same result
+        if not stop:
+            rows, par, idx = t.brfs_states(max_depth=depth, witness_pruning=witness)
+            np.testing.assert_array_equal(got["rows"], rows, err_msg=name)
+            np.testing.assert_array_equal(got["parent"], par, err_msg=name)
+            np.testing.assert_array_equal(got["index"], idx, err_msg=name)
+            assert [int(h) for h in got["hashes"]] == [oref.hash_state(r) for r in rows], name
+            assert sum(p[1] for p in per_rank) > 0, name  # successors crossed between ranks
