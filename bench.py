@@ -21,9 +21,8 @@ import json
 import math
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
+import threading
 import time
 from pathlib import Path
 
@@ -49,7 +48,7 @@ def bench_depth(args, world: int) -> tuple[int, str]:
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--env-steps", type=int, default=200)
@@ -79,53 +78,65 @@ def measured_peaks():
 
 
 class Clocks:
-    """nvidia-smi samples during the timed region."""
+    """SM clocks and clock-event reasons during the timed region, sampled by NVML every 50 ms from a thread (set up
+    before the timed region, so that no driver start-up cost falls inside it)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": "nvmlClocksEventReasonHwSlowdown",
+               "hw_thermal_slowdown": "nvmlClocksEventReasonHwThermalSlowdown",
+               "sw_thermal_slowdown": "nvmlClocksEventReasonSwThermalSlowdown",
+               "sw_power_cap": "nvmlClocksEventReasonSwPowerCap"}
 
-    def __init__(self, gpu: int):
-        self.gpu = gpu
-        self.proc = None
-        self.f = None
+    def __init__(self, cuda_index: int):
+        self.samples = []
+        self.error = None
+        self.h = None
+        self.stop = threading.Event()
+        try:
+            import pynvml
+            import torch
+
+            self.nv = pynvml
+            pynvml.nvmlInit()
+            p = torch.cuda.get_device_properties(cuda_index)
+            try:
+                bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+                self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(cuda_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.bits = {k: getattr(pynvml, v) for k, v in self.REASONS.items()}
+        except Exception as e:  # no NVML: the line says so
+            self.error = f"nvml unavailable: {e}"
+
+    def _run(self):
+        nv = self.nv
+        while not self.stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.samples.append((mhz, reasons))
+            except Exception as e:
+                self.error = str(e)
+                return
+            self.stop.wait(0.05)
 
     def __enter__(self):
-        try:
-            self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
-                                         stderr=subprocess.DEVNULL)
-        except Exception:
-            self.proc = None
+        if self.h is not None:
+            self.thread = threading.Thread(target=self._run, daemon=True)
+            self.thread.start()
         return self
 
     def __exit__(self, *a):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        self.stop.set()
+        if self.h is not None:
+            self.thread.join(timeout=5)
 
     def summary(self):
-        if self.proc is None or self.f is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.f.flush()
-        rows = []
-        for line in open(self.f.name):
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) >= 9:
-                rows.append(parts)
-        os.unlink(self.f.name)
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+        if self.h is None or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.error or "no samples"]}
+        reasons = sorted({k for _, r in self.samples for k, bit in self.bits.items() if r & bit})
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.samples), "source": "nvml"}
 
 
 def dist_setup(args):
@@ -257,6 +268,7 @@ def main():
         r.close()  # free the search's device buffers now (back to the pool for the next step)
         return r
 
+    clk = Clocks(local)  # NVML set up before the warm-up: no driver start-up inside the timed region
     r = one()
     expected = r.states
     for _ in range(max(0, args.warmup - 1)):
@@ -272,7 +284,7 @@ def main():
     barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     results = []
-    with Clocks(local) as clk:
+    with clk:
         ev0.record(stream)
         for _ in range(args.steps):
             results.append(one(expected))

@@ -318,7 +318,7 @@ Store make_store(b2_brfs& B, u64 layer_cand_begin)
 LayerMisc read_misc(b2_brfs& B)
 {
     B2_CUDA(cudaMemcpyAsync(B.misc_host, B.misc.p, sizeof(LayerMisc), cudaMemcpyDeviceToHost, B.stream));
-    B2_CUDA(cudaStreamSynchronize(B.stream));
+    stream_wait(B.stream);
     const LayerMisc m = *B.misc_host;
     if (m.status & kStatusProbeLimit)
         throw Error(B2_DEVICE_FAULT, "b2_brfs: a hash-set probe ran past its bound");
@@ -364,8 +364,9 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
     if (o.expected_states)
         ensure_layer(B, expect / 2, expect);  // a layer holds at most the states, and about twice as many candidates
     B.misc.alloc(sizeof(LayerMisc), s);
+    static_assert(sizeof(LayerMisc) <= PinnedPool::kBlock);
     if (!B.misc_host)
-        B2_CUDA(cudaMallocHost(&B.misc_host, sizeof(LayerMisc)));
+        B.misc_host = static_cast<LayerMisc*>(B.task->ctx->pinned.take());
     B2_CUDA(cudaMemsetAsync(B.misc.p, 0, sizeof(LayerMisc), s));
     ensure_table(B, expect);
     B2_CUDA(cudaMemcpyAsync(B.rows.p, P.initial.data(), W * 8, cudaMemcpyHostToDevice, s));
@@ -434,7 +435,7 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
                 E_exp = m.first_goal;
                 if (E_exp < E)
                     B2_CUDA(cudaMemcpyAsync(&G, B.cand_base.as<u64>() + E_exp, 8, cudaMemcpyDeviceToHost, s));
-                B2_CUDA(cudaStreamSynchronize(s));
+                stream_wait(s);
                 goals += 1;
                 stop = true;
             }
@@ -517,7 +518,7 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
         ++B.launches;
         fingerprint = read_misc(B).fingerprint;
     }
-    B2_CUDA(cudaStreamSynchronize(s));
+    stream_wait(s);
     R.states = B.n_states;
     R.expanded = expanded;
     R.generated = generated;
@@ -742,26 +743,22 @@ void b2_brfs_destroy(b2_brfs* search)
 {
     if (!search)
         return;
+    cudaSetDevice(search->task->ctx->device);
+    // the buffers are freed in stream order (after the search's last kernel), with no wait here
     if (search->shard)
-    {
-        cudaSetDevice(search->task->ctx->device);
-        cudaStreamSynchronize(search->stream);
         shard_free(*search);
-    }
     if (search->stream)
     {
-        cudaStreamSynchronize(search->stream);
-        // stream-ordered frees go on the search's stream, before a stream of its own is destroyed
         for (DeviceBuffer* b : {&search->rows, &search->hash, &search->par, &search->kid, &search->state_g,
                                 &search->table, &search->counts, &search->cand_base, &search->flags, &search->deferred,
                                 &search->sums, &search->misc})
             b->reset();
-        cudaStreamSynchronize(search->stream);
+        // the status mirror goes back to the context's pool once no copy into it can be pending
+        stream_drain(search->stream);
         if (search->own_stream)
             cudaStreamDestroy(search->stream);
     }
-    if (search->misc_host)
-        cudaFreeHost(search->misc_host);
+    search->task->ctx->pinned.give(search->misc_host);
     delete search;
 }
 

@@ -131,7 +131,7 @@ void comm_sync(b2_comm* c, cudaStream_t s)
 {
     const auto t0 = std::chrono::steady_clock::now();
     auto next_check = t0;
-    for (u64 spins = 0;; ++spins)
+    for (;;)
     {
         const cudaError_t e = cudaStreamQuery(s);
         if (e == cudaSuccess)
@@ -141,7 +141,8 @@ void comm_sync(b2_comm* c, cudaStream_t s)
         const auto now = std::chrono::steady_clock::now();
         if (now < next_check)
         {
-            if (spins > 1000)
+            // per-layer waits are short: poll; a wait past 50 ms (a slow peer) polls more gently
+            if (now - t0 > std::chrono::milliseconds(50))
                 std::this_thread::sleep_for(std::chrono::microseconds(20));
             continue;
         }

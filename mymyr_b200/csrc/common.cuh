@@ -12,6 +12,7 @@
 
 #include <cstdio>
 #include <memory>
+#include <mutex>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -150,12 +151,52 @@ struct DeviceBuffer
 };
 }  // namespace b2
 
+namespace b2
+{
+/// Small pinned host blocks (a search's status mirror), kept for reuse: page-locking memory per search would cost
+/// more than the search's own host work, and freeing pinned memory synchronizes the device.
+struct PinnedPool
+{
+    static constexpr size_t kBlock = 256;
+    std::mutex mu;
+    std::vector<void*> blocks;
+    void* take()
+    {
+        {
+            std::lock_guard lock(mu);
+            if (!blocks.empty())
+            {
+                void* p = blocks.back();
+                blocks.pop_back();
+                return p;
+            }
+        }
+        void* p = nullptr;
+        B2_CUDA(cudaMallocHost(&p, kBlock));
+        return p;
+    }
+    void give(void* p)
+    {
+        if (!p)
+            return;
+        std::lock_guard lock(mu);
+        blocks.push_back(p);
+    }
+    ~PinnedPool()
+    {
+        for (void* p : blocks)
+            cudaFreeHost(p);
+    }
+};
+}  // namespace b2
+
 struct b2_ctx
 {
     int device = 0;
     cudaDeviceProp prop{};
     int sms = 0;
     b2::DeviceBuffer scratch;  // per-call scratch of the stream-ordered calls (grown as needed)
+    b2::PinnedPool pinned;     // status mirrors of searches on this device
 };
 
 struct b2_task
@@ -244,4 +285,26 @@ inline unsigned grid_for(u64 n, unsigned block, unsigned cap = 1u << 20)
 }
 
 void check_status_word(const u32* dev_status, cudaStream_t s, const char* what);
+
+/// Waits for the stream by polling it (the per-layer waits of a search are short; a blocking wait's wake-up latency
+/// would dominate them).
+inline void stream_wait(cudaStream_t s)
+{
+    for (;;)
+    {
+        const cudaError_t e = cudaStreamQuery(s);
+        if (e == cudaSuccess)
+            return;
+        if (e != cudaErrorNotReady)
+            B2_CUDA(e);
+    }
+}
+
+/// stream_wait for release paths (no exception; an error ends the wait).
+inline void stream_drain(cudaStream_t s)
+{
+    while (cudaStreamQuery(s) == cudaErrorNotReady)
+    {
+    }
+}
 }  // namespace b2

@@ -406,11 +406,6 @@ struct ShardState
     std::vector<u64> layer_begin;
     u64 n_total = 0;
     u64 exchanged = 0;  // records received from other ranks
-    ~ShardState()
-    {
-        if (misc_host)
-            cudaFreeHost(misc_host);
-    }
     u64* hist() { return small.as<u64>(); }
     u64* matrix() { return small.as<u64>() + world; }
     u64* cursor() { return small.as<u64>() + world + world * world; }
@@ -565,8 +560,9 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
     ensure_cand(S, W, expect * 2, s);
     ensure_states(S, expect, s);
     S.misc.alloc(sizeof(DistMisc), s);
+    static_assert(sizeof(DistMisc) <= PinnedPool::kBlock);
     if (!S.misc_host)
-        B2_CUDA(cudaMallocHost(&S.misc_host, sizeof(DistMisc)));
+        S.misc_host = static_cast<DistMisc*>(B.task->ctx->pinned.take());
     S.small.alloc((3 * world + world * world) * 8, s);
     B2_CUDA(cudaMemsetAsync(S.misc.p, 0, sizeof(DistMisc), s));
     DistMisc* misc = S.misc.as<DistMisc>();
@@ -878,6 +874,7 @@ void shard_free(b2_brfs& B)
                             &S.counts, &S.local_base, &S.cg, &S.gbase, &S.staging, &S.fm, &S.f, &S.mark, &S.gmin,
                             &S.claimed, &S.small, &S.misc, &S.sums})
         b->reset();
+    B.task->ctx->pinned.give(S.misc_host);
     delete B.shard;
     B.shard = nullptr;
 }
