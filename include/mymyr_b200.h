@@ -262,6 +262,72 @@ b2_status b2_brfs_local(b2_brfs* search, uint64_t first, uint64_t count, uint64_
                         uint64_t* hashes, uint32_t* parent, uint32_t* index);
 void b2_brfs_destroy(b2_brfs* search);
 
+/* ------------------------------------------------------------------------------------------------ h^max
+ * The delete-relaxation heuristic h^max with unit costs (heuristics::Kind::Max; RelaxedTask grounding,
+ * include/mymyr/heuristics/relaxed_task.hpp:1-22; evaluation src/mymyr/heuristics/heuristics.cpp:185-420), evaluated on
+ * the device like cuda::DeviceHeuristic::evaluate (include/mymyr/cuda/heuristics.hpp:115). Creating it grounds the
+ * relaxation on the host from the task's initial state; tasks with negative preconditions or goals are refused
+ * (B2_UNSUPPORTED). A host-only task grounds (b2_heuristic_info_get) but cannot evaluate. */
+typedef struct b2_heuristic b2_heuristic;
+enum { B2_HEURISTIC_MAX = 2 }; /* heuristics::Kind::Max */
+#define B2_DEAD_END 0xFFFFFFFFu /* h of a dead end (DeviceHeuristic::k_dead_end) */
+
+typedef struct b2_heuristic_info {
+    uint32_t props;            /* propositions: the task's fluent slots */
+    uint32_t ops;              /* relaxed operators kept (those that add an atom outside their preconditions) */
+    uint64_t reached_atoms;    /* GroundingStats::reached_atoms: atoms of the delete-free fixpoint */
+    uint64_t ground_actions;   /* GroundingStats::ground_actions */
+    uint32_t goal_atoms;
+    uint32_t goal_unreachable; /* a goal atom is never reached: every state is a dead end */
+} b2_heuristic_info;
+
+b2_status b2_heuristic_create(b2_task* task, int32_t kind, b2_heuristic** out);
+b2_status b2_heuristic_info_get(const b2_heuristic* h, b2_heuristic_info* out);
+/* h of the n device rows rows + i * stride (`words` = the task's words) into out[0, n) (device u32, B2_DEAD_END for
+ * dead ends), on `stream`. */
+b2_status b2_heuristic_evaluate(b2_heuristic* h, const uint64_t* rows, uint64_t stride, uint32_t words, uint64_t n,
+                                uint32_t* out, void* stream);
+void b2_heuristic_destroy(b2_heuristic* h);
+
+/* ------------------------------------------------------------------------------------------------ A*
+ * Eager A* with h^max and unit costs (search::astar_eager, include/mymyr/search/best_first.hpp:9-15, 191;
+ * cuda::astar, include/mymyr/cuda/astar.hpp:110): the optimal plan cost of the reference. Each device step expands
+ * every open state of the lowest f at once (the reference's DeviceBestFirstOptions::single_bucket = false), so
+ * `expanded` and `generated` count the states of the final f layer that a one-at-a-time search leaves unexpanded. */
+typedef struct b2_astar b2_astar;
+
+typedef struct b2_astar_options {
+    uint64_t max_expansions;   /* 0: no limit (the search stops with B2_SEARCH_OUT_OF_STATES past it) */
+    uint64_t expected_states;  /* pre-sizes the state arena and table (0: grow) */
+    int32_t witness_pruning;   /* default 0, as the reference's A* */
+    int32_t timings;           /* per-phase device times */
+    void* stream;              /* NULL: a stream of its own */
+    b2_heuristic* heuristic;   /* an h^max of the same task to share (NULL: the search grounds its own) */
+} b2_astar_options;
+
+void b2_astar_options_default(b2_astar_options* o);
+
+typedef struct b2_astar_result {
+    uint32_t status;           /* B2_SEARCH_SOLVED, _EXHAUSTED (no plan), _UNSOLVABLE (dead-end or goal-false start),
+                                  _OUT_OF_STATES (max_expansions) */
+    uint32_t waves;            /* device steps (batches of equal f) */
+    double cost;               /* g of the goal state (solved) */
+    uint64_t expanded, generated, states, evaluations, dead_ends;
+    double initial_h;          /* -1: a dead end */
+    uint32_t f_layers;         /* f values expanded */
+    uint32_t plan_length;
+    double search_s, count_ms, expand_ms, insert_ms, eval_ms;
+    uint64_t kernel_launches;
+    uint64_t relaxed_ops, relaxed_atoms;
+} b2_astar_result;
+
+b2_status b2_astar_create(b2_task* task, const b2_astar_options* options, b2_astar** out);
+b2_status b2_astar_run(b2_astar* search, b2_astar_result* result);
+/* The plan as its states' transitions, root first: step i leaves state parent[i] (a state index of the search) by its
+ * index[i]-th successor in canonical order; *len = the plan length (steps are written when cap >= *len). */
+b2_status b2_astar_plan(b2_astar* search, uint32_t* parent, uint32_t* index, uint32_t cap, uint32_t* len);
+void b2_astar_destroy(b2_astar* search);
+
 /* ------------------------------------------------------------------------------------------------ env step
  * The batched environment of rl::HostEnv / cuda::DeviceEnv (include/mymyr/rl/env.hpp:214-260,
  * include/mymyr/cuda/env.hpp:125-198) over one task, Index action space, random policy or given actions. */

@@ -89,6 +89,29 @@ class BrfsResult(C.Structure):
                 ("local_states", C.c_uint64), ("exchanged", C.c_uint64)]
 
 
+class HeuristicInfo(C.Structure):
+    _fields_ = [("props", C.c_uint32), ("ops", C.c_uint32), ("reached_atoms", C.c_uint64),
+                ("ground_actions", C.c_uint64), ("goal_atoms", C.c_uint32), ("goal_unreachable", C.c_uint32)]
+
+
+class AstarOptions(C.Structure):
+    _fields_ = [("max_expansions", C.c_uint64), ("expected_states", C.c_uint64), ("witness_pruning", C.c_int32),
+                ("timings", C.c_int32), ("stream", C.c_void_p), ("heuristic", C.c_void_p)]
+
+
+class AstarResult(C.Structure):
+    _fields_ = [("status", C.c_uint32), ("waves", C.c_uint32), ("cost", C.c_double), ("expanded", C.c_uint64),
+                ("generated", C.c_uint64), ("states", C.c_uint64), ("evaluations", C.c_uint64),
+                ("dead_ends", C.c_uint64), ("initial_h", C.c_double), ("f_layers", C.c_uint32),
+                ("plan_length", C.c_uint32), ("search_s", C.c_double), ("count_ms", C.c_double),
+                ("expand_ms", C.c_double), ("insert_ms", C.c_double), ("eval_ms", C.c_double),
+                ("kernel_launches", C.c_uint64), ("relaxed_ops", C.c_uint64), ("relaxed_atoms", C.c_uint64)]
+
+
+B2_HEURISTIC_MAX = 2
+B2_DEAD_END = 0xFFFFFFFF
+
+
 class CommId(C.Structure):
     _fields_ = [("bytes", C.c_char * 128)]
 
@@ -145,6 +168,15 @@ SIGNATURES = {
     "b2_brfs_local_count": (C.c_int, [P, C.POINTER(C.c_uint64)]),
     "b2_brfs_local": (C.c_int, [P, U64, U64, P, P, U32, P, P, P]),
     "b2_brfs_destroy": (None, [P]),
+    "b2_heuristic_create": (C.c_int, [P, C.c_int32, PP]),
+    "b2_heuristic_info_get": (C.c_int, [P, C.POINTER(HeuristicInfo)]),
+    "b2_heuristic_evaluate": (C.c_int, [P, P, U64, U32, U64, P, P]),
+    "b2_heuristic_destroy": (None, [P]),
+    "b2_astar_options_default": (None, [C.POINTER(AstarOptions)]),
+    "b2_astar_create": (C.c_int, [P, C.POINTER(AstarOptions), PP]),
+    "b2_astar_run": (C.c_int, [P, C.POINTER(AstarResult)]),
+    "b2_astar_plan": (C.c_int, [P, P, P, U32, C.POINTER(C.c_uint32)]),
+    "b2_astar_destroy": (None, [P]),
     "b2_env_config_default": (None, [C.POINTER(EnvConfig)]),
     "b2_env_create": (C.c_int, [P, C.POINTER(EnvConfig), PP]),
     "b2_env_reset": (C.c_int, [P, C.POINTER(EnvBatch), P, P, P]),

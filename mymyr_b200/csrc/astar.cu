@@ -1,0 +1,1028 @@
+// A* with h^max on the device (search::astar_eager with heuristics::Kind::Max and unit costs,
+// src/mymyr/search/astar.cpp:67-256 and include/mymyr/search/best_first.hpp:9-15 of maichmueller/mymyr), and the
+// batched h^max evaluation it uses (heuristics::RelaxationHeuristic, src/mymyr/heuristics/heuristics.cpp:185-420;
+// cuda::DeviceHeuristic::evaluate, include/mymyr/cuda/heuristics.hpp:115).
+//
+// h^max. With unit costs, h^max(s) is the index of the first layer of the relaxed planning graph from s that holds
+// every goal atom: layer 0 = the atoms of s, layer k + 1 = layer k plus the adds of every operator whose
+// preconditions are in layer k (the least fixpoint of cost(p) = 0 for p in s, min over achievers of 1 + max over
+// their preconditions, which the reference computes by a generalized Dijkstra). One warp per state keeps the layer's
+// atom bitset in shared memory and sweeps the grounded operators (relax.cpp) lane by lane; a layer that adds nothing
+// ends the state as a dead end (+inf).
+//
+// A*. h^max is consistent, so the states leave the open list in f order with their final g, and a bucket of equal f
+// can be expanded as a batch: each wave expands the current frontier (all open states of the current f), its
+// successors are staged, inserted into the hash set in one kernel (all staged rows are in memory, so the insert is
+// single-phase: a new state takes an empty slot; an equal one lowers the state's g with atomicMin on (g << 32 |
+// candidate index), which also picks a deterministic parent among equal g), new states are goal-tested and
+// evaluated, and every state whose g was set or lowered is pushed: into the next wave if its f equals the current f,
+// else into the open list of later f. When the current f reaches the g of the best goal found, that g is the optimal
+// cost (a goal is recognized when generated and returned when it is the minimum f, as in the reference). Open entries
+// of states that were lowered later are stale and skipped (f != g + h).
+
+#include "brfs.cuh"
+#include "relax.hpp"
+
+#include <chrono>
+#include <cstddef>
+#include <stdexcept>
+
+namespace b2
+{
+namespace
+{
+constexpr u32 kDeadEnd = 0xFFFFFFFFu;
+constexpr u8 kClosed = 1, kGoal = 2, kDead = 4;
+
+struct HmaxArgs
+{
+    const u32* pre_begin;
+    const u32* pre;
+    const u32* add_begin;
+    const u32* add;
+    const u32* goal;
+    u32 ops, ngoal, W, unreachable;
+    // optional goal test of the evaluated states (A*): goal masks and the flags to mark
+    const u64* goal_pos;
+    const u64* goal_neg;
+    u8* flags;
+};
+
+__device__ __forceinline__ bool sbit(const u64* b, u32 s) { return (b[s >> 6] >> (s & 63)) & 1; }
+
+/// h^max of states: state i is row rows + node(i) * stride, node(i) = nodes[i] (or i), for i < n (*n_dev if given).
+/// Warp per state; shared memory: two W-word bitsets per warp.
+__global__ void k_hmax(HmaxArgs H, const u64* __restrict__ rows, u64 stride, const u32* __restrict__ nodes,
+                       const u32* n_dev, u64 n_host, u32* __restrict__ out, u32 out_by_node)
+{
+    extern __shared__ u64 sm[];
+    const u32 lane = threadIdx.x & 31, wib = threadIdx.x >> 5, wpb = blockDim.x >> 5;
+    u64* cur = sm + static_cast<u64>(wib) * 2 * H.W;
+    u64* nxt = cur + H.W;
+    const u64 n = n_dev ? *n_dev : n_host;
+    for (u64 i = static_cast<u64>(blockIdx.x) * wpb + wib; i < n; i += static_cast<u64>(gridDim.x) * wpb)
+    {
+        const u64 node = nodes ? nodes[i] : i;
+        const u64* row = rows + node * stride;
+        bool gpos = true, gneg = true;
+        for (u32 w = lane; w < H.W; w += 32)
+        {
+            const u64 x = row[w];
+            cur[w] = x;
+            nxt[w] = x;
+            if (H.flags)
+            {
+                gpos = gpos && (x & H.goal_pos[w]) == H.goal_pos[w];
+                gneg = gneg && (x & H.goal_neg[w]) == 0;
+            }
+        }
+        __syncwarp();
+        if (H.flags && __all_sync(0xFFFFFFFFu, gpos && gneg) && lane == 0)
+            H.flags[node] |= kGoal;
+        auto goal_reached = [&]() {
+            bool ok = true;
+            for (u32 q = lane; q < H.ngoal; q += 32)
+                ok = ok && sbit(cur, H.goal[q]);
+            return __all_sync(0xFFFFFFFFu, ok);
+        };
+        u32 h = 0;
+        if (H.unreachable)
+            h = kDeadEnd;
+        else if (!goal_reached())
+        {
+            for (u32 layer = 1;; ++layer)
+            {
+                bool changed = false;
+                for (u32 o = lane; o < H.ops; o += 32)
+                {
+                    bool app = true;
+                    for (u32 q = H.pre_begin[o], e = H.pre_begin[o + 1]; q < e && app; ++q)
+                        app = sbit(cur, H.pre[q]);
+                    if (!app)
+                        continue;
+                    for (u32 q = H.add_begin[o], e = H.add_begin[o + 1]; q < e; ++q)
+                    {
+                        const u32 s = H.add[q];
+                        if (!sbit(cur, s))
+                        {
+                            changed = true;
+                            if (!sbit(nxt, s))
+                                atomicOr(reinterpret_cast<unsigned long long*>(nxt + (s >> 6)), 1ull << (s & 63));
+                        }
+                    }
+                }
+                changed = __any_sync(0xFFFFFFFFu, changed);
+                __syncwarp();
+                if (!changed)
+                {
+                    h = kDeadEnd;
+                    break;
+                }
+                for (u32 w = lane; w < H.W; w += 32)
+                    cur[w] = nxt[w];
+                __syncwarp();
+                if (goal_reached())
+                {
+                    h = layer;
+                    break;
+                }
+            }
+        }
+        if (lane == 0)
+            out[out_by_node ? node : i] = h;
+        __syncwarp();
+    }
+}
+
+/// Per-wave counters of the A* (device side, mirrored to pinned host memory).
+struct AstarMisc
+{
+    LayerMisc lm;       // count pass: total candidates of the wave, status
+    u32 ntouched;       // states whose g was set or lowered this wave
+    u32 nfresh;         // new states this wave
+    u32 nnext;          // states of the next wave (f = current f)
+    u32 ndead;          // dead ends among this wave's new states
+    u64 nopen;          // open entries of later f
+    u64 best_goal;      // (g << 32 | state) of the best goal found (~0: none)
+    u64 fmin;           // smallest f of a valid open entry (bucket switch)
+    u64 nkeep;          // open entries kept by the extraction
+    u64 nfront;         // states extracted into the frontier
+};
+
+struct InsertArgs
+{
+    const u64* staging;
+    u64 G;
+    u32 W;
+    u32 wave;
+    u64 cand_begin;
+    const u32* frontier;
+    const u64* cand_base;
+    u64 nF;
+    u64* rows;
+    u64* hash;
+    u64* best;
+    u8* flags;
+    u32* stamp;
+    u32* par;
+    u32* kid;
+    u64* table;
+    u64 mask;
+    u32 max_probe;
+    u32 pad;
+    u32* touched;
+    u32* fresh;
+    AstarMisc* misc;
+};
+
+__global__ void k_astar_insert(InsertArgs a)
+{
+    const u32 W = a.W, RW = W + 2;
+    for (u64 r = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; r < a.G; r += static_cast<u64>(gridDim.x) * blockDim.x)
+    {
+        const u64* rec = a.staging + r * RW;
+        const u64 h = rec[W], c = rec[W + 1];
+        // the parent: the last frontier position p with cand_base[p] <= c
+        u64 lo = 0, hi = a.nF;
+        while (hi - lo > 1)
+        {
+            const u64 mid = (lo + hi) / 2;
+            if (a.cand_base[mid] <= c)
+                lo = mid;
+            else
+                hi = mid;
+        }
+        const u32 parent = a.frontier[lo];
+        const u64 cand = a.cand_begin + r;
+        a.par[cand] = parent;
+        a.kid[cand] = static_cast<u32>(c - a.cand_base[lo]);
+        const u32 gnew = static_cast<u32>(a.best[parent] >> 32) + 1;
+        const u64 key = (static_cast<u64>(gnew) << 32) | cand;
+        const u64 mine = (h & 0xFFFFFFFF00000000ull) | cand;
+        u64 j = h & a.mask;
+        bool done = false;
+        for (u32 probe = 0; probe < a.max_probe; ++probe, j = (j + 1) & a.mask)
+        {
+            u64 cur = __ldcg(a.table + j);
+            if (cur == kEmpty)
+            {
+                const u64 prev = atomicCAS(reinterpret_cast<unsigned long long*>(a.table + j), kEmpty, mine);
+                if (prev == kEmpty)
+                {
+                    u64* dst = a.rows + cand * W;
+                    for (u32 q = 0; q < W; ++q)
+                        dst[q] = rec[q];
+                    a.hash[cand] = h;
+                    atomicMin(reinterpret_cast<unsigned long long*>(a.best + cand), key);
+                    if (atomicExch(a.stamp + cand, a.wave) != a.wave)
+                        a.touched[atomicAdd(&a.misc->ntouched, 1u)] = static_cast<u32>(cand);
+                    a.fresh[atomicAdd(&a.misc->nfresh, 1u)] = static_cast<u32>(cand);
+                    done = true;
+                    break;
+                }
+                cur = prev;
+            }
+            if ((cur >> 32) != (mine >> 32))
+                continue;
+            const u64 o = cur & 0xFFFFFFFFull;
+            const u64* orow = o >= a.cand_begin ? a.staging + (o - a.cand_begin) * RW : a.rows + o * W;
+            bool eq = true;
+            for (u32 q = 0; q < W && eq; ++q)
+                eq = orow[q] == rec[q];
+            if (!eq)
+                continue;
+            done = true;
+            if (a.flags[o] & (kClosed | kDead))
+                break;  // expanded with its final g (h^max is consistent), or a dead end
+            const u64 old = atomicMin(reinterpret_cast<unsigned long long*>(a.best + o), key);
+            if ((old >> 32) > gnew && atomicExch(a.stamp + o, a.wave) != a.wave)
+                a.touched[atomicAdd(&a.misc->ntouched, 1u)] = static_cast<u32>(o);
+            break;
+        }
+        if (!done)
+            atomicOr(&a.misc->lm.status, kStatusProbeLimit);
+    }
+}
+
+/// Pushes the states whose g was set or lowered this wave: dead ends are marked, goals recorded, the others go to
+/// the next wave (f = fcur; closed now, as they will be expanded) or to the open list of later f.
+__global__ void k_astar_push(const u32* __restrict__ touched, AstarMisc* misc, const u64* __restrict__ best,
+                             const u32* __restrict__ h, u8* flags, u32 fcur, u32* next, u64* open)
+{
+    const u32 n = misc->ntouched;
+    for (u32 t = blockIdx.x * blockDim.x + threadIdx.x; t < n; t += gridDim.x * blockDim.x)
+    {
+        const u32 o = touched[t];
+        const u32 hv = h[o];
+        if (hv == kDeadEnd)
+        {
+            flags[o] |= kDead;
+            atomicAdd(&misc->ndead, 1u);
+            continue;
+        }
+        const u64 g = best[o] >> 32;
+        if (flags[o] & kGoal)
+            atomicMin(reinterpret_cast<unsigned long long*>(&misc->best_goal), (g << 32) | o);
+        const u64 f = g + hv;
+        if (f == fcur)
+        {
+            flags[o] |= kClosed;
+            next[atomicAdd(&misc->nnext, 1u)] = o;
+        }
+        else
+            open[atomicAdd(reinterpret_cast<unsigned long long*>(&misc->nopen), 1ull)] = (f << 32) | o;
+    }
+}
+
+__device__ __forceinline__ bool open_valid(u64 e, const u64* best, const u32* h, const u8* flags)
+{
+    const u32 o = static_cast<u32>(e);
+    return !(flags[o] & (kClosed | kDead)) && (e >> 32) == (best[o] >> 32) + h[o];
+}
+
+__global__ void k_astar_fmin(const u64* __restrict__ open, u64 n, const u64* __restrict__ best,
+                             const u32* __restrict__ h, const u8* __restrict__ flags, AstarMisc* misc)
+{
+    u64 m = ~u64{0};
+    for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < n; i += static_cast<u64>(gridDim.x) * blockDim.x)
+        if (open_valid(open[i], best, h, flags))
+            m = min(m, open[i] >> 32);
+    for (int s = 16; s > 0; s >>= 1)
+        m = min(m, __shfl_xor_sync(0xFFFFFFFFu, m, s));
+    if ((threadIdx.x & 31) == 0 && m != ~u64{0})
+        atomicMin(reinterpret_cast<unsigned long long*>(&misc->fmin), m);
+}
+
+/// The open entries of f = fmin become the frontier (closed now); the other valid ones are kept.
+__global__ void k_astar_extract(const u64* __restrict__ open, u64 n, const u64* __restrict__ best,
+                                const u32* __restrict__ h, u8* flags, u64 fmin, u32* front, u64* keep,
+                                AstarMisc* misc)
+{
+    for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < n; i += static_cast<u64>(gridDim.x) * blockDim.x)
+    {
+        const u64 e = open[i];
+        if (!open_valid(e, best, h, flags))
+            continue;
+        if ((e >> 32) == fmin)
+        {
+            const u32 o = static_cast<u32>(e);
+            flags[o] |= kClosed;
+            front[atomicAdd(reinterpret_cast<unsigned long long*>(&misc->nfront), 1ull)] = o;
+        }
+        else
+            keep[atomicAdd(reinterpret_cast<unsigned long long*>(&misc->nkeep), 1ull)] = e;
+    }
+}
+
+__global__ void k_astar_seed(u64* rows, u64* hash, u32 W, u64* best, u8* flags, u32* par, u32* kid, u64* table,
+                             u64 mask, u32 max_probe, AstarMisc* misc)
+{
+    const GlobalRow r{rows, W};
+    const u64 h = hash_words([&](u32 q) { return r.word(q); }, W);
+    hash[0] = h;
+    best[0] = 0;
+    flags[0] = kClosed;
+    par[0] = 0xFFFFFFFFu;
+    kid[0] = 0;
+    u64 j = h & mask;
+    for (u32 probe = 0; probe < max_probe && table[j] != kEmpty; ++probe)
+        j = (j + 1) & mask;
+    if (table[j] == kEmpty)
+        table[j] = h & 0xFFFFFFFF00000000ull;
+    else
+        atomicOr(&misc->lm.status, kStatusProbeLimit);
+}
+
+/// The path from the root to state `goal`: (parent state, successor index) per step, goal first.
+__global__ void k_astar_path(const u64* best, const u32* par, const u32* kid, u32 goal, u32 cap, u32* out_parent,
+                             u32* out_index, u32* len)
+{
+    u32 s = goal, n = 0;
+    while (s != 0 && n < cap)
+    {
+        const u32 c = static_cast<u32>(best[s]);  // the candidate that set the state's g
+        out_parent[n] = par[c];
+        out_index[n] = kid[c];
+        s = par[c];
+        ++n;
+    }
+    *len = s == 0 ? n : 0xFFFFFFFFu;
+}
+
+/// Moves every entry of an old table (tag | state) into a new one, probing from the state's full hash.
+__global__ void k_rehash_entries(const u64* __restrict__ old, u64 old_slots, u64* table, u64 mask, u32 max_probe,
+                                 const u64* __restrict__ hash, u32* status)
+{
+    for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < old_slots; i += static_cast<u64>(gridDim.x) * blockDim.x)
+    {
+        const u64 e = old[i];
+        if (e == kEmpty)
+            continue;
+        u64 j = hash[e & 0xFFFFFFFFull] & mask;
+        u32 probe = 0;
+        for (; probe < max_probe; ++probe, j = (j + 1) & mask)
+            if (atomicCAS(reinterpret_cast<unsigned long long*>(table + j), kEmpty, e) == kEmpty)
+                break;
+        if (probe == max_probe)
+            atomicOr(status, kStatusProbeLimit);
+    }
+}
+
+__global__ void k_iota(u32* p, u64 n)
+{
+    for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < n; i += static_cast<u64>(gridDim.x) * blockDim.x)
+        p[i] = static_cast<u32>(i);
+}
+}  // namespace
+}  // namespace b2
+
+using namespace b2;
+
+struct b2_heuristic
+{
+    b2_task* task = nullptr;
+    Relaxation R;
+    DeviceBuffer blob;  // u32: pre_begin | pre | add_begin | add | goal
+    DeviceBuffer goal_masks;  // u64: goal_pos | goal_neg
+    HmaxArgs args{};
+};
+
+namespace
+{
+b2_heuristic* make_heuristic(b2_task* task)
+{
+    auto H = std::make_unique<b2_heuristic>();
+    H->task = task;
+    try
+    {
+        H->R = ground_relaxation(task->spec, task->layout, task->statics, task->prog);
+    }
+    catch (const std::domain_error& e)
+    {
+        throw Error(B2_UNSUPPORTED, std::string("b2_heuristic: ") + e.what());
+    }
+    const Relaxation& R = H->R;
+    if (task->ctx)
+    {
+        B2_CUDA(cudaSetDevice(task->ctx->device));
+        std::vector<u32> blob;
+        auto put = [&](const std::vector<u32>& v) {
+            const u64 at = blob.size();
+            blob.insert(blob.end(), v.begin(), v.end());
+            blob.push_back(0);  // no empty array
+            return at;
+        };
+        const u64 o0 = put(R.pre_begin), o1 = put(R.pre), o2 = put(R.add_begin), o3 = put(R.add), o4 = put(R.goal);
+        H->blob.alloc(blob.size() * 4);
+        B2_CUDA(cudaMemcpy(H->blob.p, blob.data(), blob.size() * 4, cudaMemcpyHostToDevice));
+        const u32* b = H->blob.as<u32>();
+        const u32 W = task->prog.words;
+        std::vector<u64> masks(task->prog.goal_pos);
+        masks.insert(masks.end(), task->prog.goal_neg.begin(), task->prog.goal_neg.end());
+        H->goal_masks.alloc(masks.size() * 8);
+        B2_CUDA(cudaMemcpy(H->goal_masks.p, masks.data(), masks.size() * 8, cudaMemcpyHostToDevice));
+        H->args = HmaxArgs{b + o0, b + o1, b + o2, b + o3, b + o4, R.ops(), static_cast<u32>(R.goal.size()), W,
+                           R.goal_unreachable || task->prog.goal_unsat ? 1u : 0u, H->goal_masks.as<u64>(),
+                           H->goal_masks.as<u64>() + W, nullptr};
+    }
+    return H.release();
+}
+
+constexpr unsigned kHmaxThreads = 128;
+
+void launch_hmax(const b2_heuristic& H, const u64* rows, u64 stride, const u32* nodes, const u32* n_dev, u64 n_bound,
+                 u32* out, bool by_node, u8* flags, int sms, cudaStream_t s)
+{
+    HmaxArgs a = H.args;
+    a.flags = flags;
+    const unsigned warps = kHmaxThreads / 32;
+    const size_t smem = static_cast<size_t>(warps) * 2 * a.W * 8;
+    if (smem > 200 * 1024)
+        throw Error(B2_UNSUPPORTED, "b2_heuristic: state rows too wide for the h^max kernel's shared memory");
+    if (smem > 48 * 1024)
+        B2_CUDA(cudaFuncSetAttribute(k_hmax, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    const unsigned grid = grid_for(n_bound, warps, static_cast<unsigned>(sms) * 32);
+    k_hmax<<<grid, kHmaxThreads, smem, s>>>(a, rows, stride, nodes, n_dev, n_bound, out, by_node ? 1 : 0);
+    B2_CUDA(cudaGetLastError());
+}
+}  // namespace
+
+// ------------------------------------------------------------------------------------------------ A* search object
+struct b2_astar
+{
+    b2_task* task = nullptr;
+    b2_heuristic* H = nullptr;
+    bool own_h = false;
+    b2_astar_options opt{};
+    cudaStream_t stream = nullptr;
+    bool own_stream = false;
+    u32 W = 1;
+    // per candidate (state ids are candidate indices: every generated successor has one)
+    DeviceBuffer rows, hash, best, hval, flags, stamp, par, kid;
+    u64 cap_cand = 0, cand_next = 0;
+    DeviceBuffer table;
+    u64 table_slots = 0;
+    u64 n_states = 0;
+    // per wave
+    DeviceBuffer counts, cand_base, iota, staging, touched, fresh, front, next, sums;
+    u64 cap_front = 0, cap_wave = 0, cap_iota = 0;
+    DeviceBuffer open, keep;
+    u64 cap_open = 0;
+    DeviceBuffer misc;
+    AstarMisc* misc_host = nullptr;
+    DeviceBuffer hist;  // the staging kernel's per-owner counter (one rank)
+    u64 launches = 0;
+    bool ran = false;
+    u32 goal_state = 0;
+    bool solved = false;
+    u64 cost = 0;
+};
+
+namespace
+{
+void ensure_cand(b2_astar& A, u64 need)
+{
+    if (need <= A.cap_cand)
+        return;
+    const u64 cap = std::max<u64>(need, A.cap_cand + A.cap_cand / 2);
+    const u64 used = A.cand_next;
+    cudaStream_t s = A.stream;
+    A.rows.grow(cap * A.W * 8, used * A.W * 8, s);
+    A.hash.grow(cap * 8, used * 8, s);
+    A.best.grow(cap * 8, used * 8, s);
+    A.hval.grow(cap * 4, used * 4, s);
+    A.flags.grow(cap, used, s);
+    A.stamp.grow(cap * 4, used * 4, s);
+    A.par.grow(cap * 4, used * 4, s);
+    A.kid.grow(cap * 4, used * 4, s);
+    A.cap_cand = cap;
+}
+
+void rehash(b2_astar& A, u64 slots)
+{
+    // the table's entries (tag | state) move into a table of `slots` slots, probing from each state's full hash
+    DeviceBuffer old;
+    old.swap(A.table);
+    const u64 old_slots = A.table_slots;
+    A.table.alloc(slots * 8, A.stream);
+    B2_CUDA(cudaMemsetAsync(A.table.p, 0xFF, slots * 8, A.stream));
+    A.table_slots = slots;
+    if (old_slots)
+    {
+        auto* misc = A.misc.as<AstarMisc>();
+        k_rehash_entries<<<grid_for(old_slots, 256), 256, 0, A.stream>>>(old.as<u64>(), old_slots, A.table.as<u64>(),
+                                                                          slots - 1, max_probe(slots), A.hash.as<u64>(),
+                                                                          &misc->lm.status);
+        B2_CUDA(cudaGetLastError());
+        ++A.launches;
+    }
+}
+}  // namespace
+
+namespace
+{
+void ensure_table(b2_astar& A, u64 bound)
+{
+    if (bound * 4 <= A.table_slots * 3)
+        return;
+    u64 slots = A.table_slots ? A.table_slots : 1024;
+    while (bound * 2 > slots)
+        slots *= 2;
+    rehash(A, slots);
+}
+
+void ensure_wave(b2_astar& A, u64 nF)
+{
+    cudaStream_t s = A.stream;
+    if (nF > A.cap_front)
+    {
+        const u64 cap = std::max<u64>(nF, A.cap_front * 2);
+        A.counts.alloc(cap * 4, s);
+        A.cand_base.alloc((cap + 1) * 8, s);
+        A.cap_front = cap;
+    }
+    if (nF > A.cap_iota)
+    {
+        const u64 cap = std::max<u64>(nF, A.cap_iota * 2);
+        A.iota.alloc(cap * 4, s);
+        k_iota<<<grid_for(cap, 256), 256, 0, s>>>(A.iota.as<u32>(), cap);
+        B2_CUDA(cudaGetLastError());
+        ++A.launches;
+        A.cap_iota = cap;
+    }
+    if (A.sums.bytes < scan_scratch_bytes(nF))
+        A.sums.alloc(scan_scratch_bytes(std::max<u64>(nF, 1) * 2), s);
+}
+
+/// Buffers of a wave of G candidates: staging, touched / fresh / next lists, and room for G more open entries.
+void ensure_candidates(b2_astar& A, u64 G, u64 nopen)
+{
+    cudaStream_t s = A.stream;
+    if (G > A.cap_wave)
+    {
+        const u64 cap = std::max<u64>(G, A.cap_wave * 2);
+        A.staging.alloc(cap * (A.W + 2) * 8, s);
+        A.touched.alloc(cap * 4, s);
+        A.fresh.alloc(cap * 4, s);
+        A.cap_wave = cap;
+    }
+    if (A.next.bytes < G * 4)
+        A.next.alloc(std::max<u64>(G, 1) * 8, s);
+    if (nopen + G > A.cap_open)
+    {
+        const u64 cap = std::max<u64>(nopen + G, A.cap_open * 2);
+        A.open.grow(cap * 8, nopen * 8, s);
+        A.keep.alloc(cap * 8, s);
+        A.cap_open = cap;
+    }
+}
+
+const AstarMisc& read_misc(b2_astar& A)
+{
+    B2_CUDA(cudaMemcpyAsync(A.misc_host, A.misc.p, sizeof(AstarMisc), cudaMemcpyDeviceToHost, A.stream));
+    stream_wait(A.stream);
+    if (A.misc_host->lm.status & kStatusProbeLimit)
+        throw Error(B2_DEVICE_FAULT, "b2_astar: a hash-set probe ran past its bound");
+    if (A.misc_host->lm.status)
+        throw Error(B2_DEVICE_FAULT, "b2_astar: device status " + std::to_string(A.misc_host->lm.status));
+    return *A.misc_host;
+}
+
+void run_astar(b2_astar& A, b2_astar_result& R)
+{
+    const auto t0 = std::chrono::steady_clock::now();
+    b2_task* task = A.task;
+    const Program& P = task->prog;
+    const DevTask& T = task->dev;
+    const u32 pi = A.opt.witness_pruning ? 0 : 1;
+    const u32 W = A.W, RW = W + 2;
+    const unsigned sms = static_cast<unsigned>(task->ctx->sms);
+    cudaStream_t s = A.stream;
+    cudaEvent_t ev[6];
+    for (auto& e : ev)
+        B2_CUDA(cudaEventCreate(&e));
+    struct EvGuard
+    {
+        cudaEvent_t* e;
+        ~EvGuard()
+        {
+            for (int i = 0; i < 6; ++i)
+                cudaEventDestroy(e[i]);
+        }
+    } guard{ev};
+    R.relaxed_ops = A.H->R.ops();
+    R.relaxed_atoms = A.H->R.reached;
+    if (P.goal_unsat)
+    {
+        R.status = B2_SEARCH_UNSOLVABLE;
+        return;
+    }
+    const u64 expect = std::max<u64>(A.opt.expected_states, 4096);
+    ensure_cand(A, expect);
+    A.misc.alloc(sizeof(AstarMisc), s);
+    static_assert(sizeof(AstarMisc) <= PinnedPool::kBlock);
+    A.misc_host = static_cast<AstarMisc*>(task->ctx->pinned.take());
+    *A.misc_host = AstarMisc{};
+    A.misc_host->best_goal = ~u64{0};
+    B2_CUDA(cudaMemcpyAsync(A.misc.p, A.misc_host, sizeof(AstarMisc), cudaMemcpyHostToDevice, s));
+    ensure_table(A, expect);
+    AstarMisc* misc = A.misc.as<AstarMisc>();
+    B2_CUDA(cudaMemcpyAsync(A.rows.p, P.initial.data(), W * 8, cudaMemcpyHostToDevice, s));
+    k_astar_seed<<<1, 1, 0, s>>>(A.rows.as<u64>(), A.hash.as<u64>(), W, A.best.as<u64>(), A.flags.as<u8>(),
+                                 A.par.as<u32>(), A.kid.as<u32>(), A.table.as<u64>(), A.table_slots - 1,
+                                 max_probe(A.table_slots), misc);
+    B2_CUDA(cudaGetLastError());
+    ++A.launches;
+    ensure_wave(A, 1);
+    ensure_candidates(A, 1, 0);
+    A.front.alloc(1024 * 4, s);
+    B2_CUDA(cudaMemsetAsync(A.front.p, 0, 4, s));  // the frontier: the root (state 0)
+    launch_hmax(*A.H, A.rows.as<u64>(), W, A.front.as<u32>(), nullptr, 1, A.hval.as<u32>(), true, A.flags.as<u8>(),
+                static_cast<int>(sms), s);
+    ++A.launches;
+    u32 h0 = 0;
+    u8 f0 = 0;
+    B2_CUDA(cudaMemcpyAsync(&h0, A.hval.p, 4, cudaMemcpyDeviceToHost, s));
+    B2_CUDA(cudaMemcpyAsync(&f0, A.flags.p, 1, cudaMemcpyDeviceToHost, s));
+    stream_wait(s);
+    A.cand_next = 1;
+    A.n_states = 1;
+    R.evaluations = 1;
+    R.initial_h = h0 == kDeadEnd ? -1.0 : static_cast<double>(h0);
+    const bool dead_start = h0 == kDeadEnd && !(f0 & kGoal);
+    if (f0 & kGoal)
+    {
+        A.solved = true;
+        A.cost = 0;
+        A.goal_state = 0;
+    }
+    else if (dead_start)
+        R.dead_ends = 1;
+    u64 fcur = h0, nF = 1, nopen = 0, expanded = 0, generated = 0, fresh_total = 0, dead = 0;
+    u32 wave = 0, f_layers = 1;
+    double count_ms = 0, expand_ms = 0, insert_ms = 0, eval_ms = 0;
+    bool exhausted = false;
+    while (!A.solved && !dead_start)
+    {
+        if (A.opt.max_expansions && expanded >= A.opt.max_expansions)
+            break;
+        ++wave;
+        ensure_wave(A, nF);
+        // per-wave counters (the open-list count and the best goal persist)
+        B2_CUDA(cudaMemsetAsync(misc, 0, offsetof(AstarMisc, nopen), s));
+        const unsigned grid = grid_for(nF, 128, sms * 64);
+        if (A.opt.timings)
+            B2_CUDA(cudaEventRecord(ev[0], s));
+        if (task->jit)
+        {
+            dev::BrfsArgs a{};
+            a.frontier = A.front.as<u32>();
+            a.E = nF;
+            a.counts = A.counts.as<u32>();
+            a.misc = &misc->lm;
+            a.S.rows = A.rows.as<u64>();
+            a.S.W = W;
+            a.pi = pi;
+            jit_launch(task->jit->brfs_count[pi], grid, 128, &a, s);
+        }
+        else
+            dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
+                k_count<OW, WR><<<grid, 128, 0, s>>>(T, pi, A.rows.as<u64>(), W, A.front.as<u32>(), nF,
+                                                     A.counts.as<u32>(), &misc->lm);
+            });
+        device_scan(CountIn{A.counts.as<u32>()}, BaseOut{A.cand_base.as<u64>()}, nF, &misc->lm.total_cand,
+                    A.sums.as<u64>(), s);
+        A.launches += 4;
+        if (A.opt.timings)
+            B2_CUDA(cudaEventRecord(ev[1], s));
+        const u64 G = read_misc(A).lm.total_cand;
+        if (G > 0)
+        {
+            if (A.cand_next + G >= (u64{1} << 32) - 1)
+                throw Error(B2_CAPACITY, "b2_astar: more than 2^32 - 2 generated states");
+            ensure_cand(A, A.cand_next + G);
+            ensure_candidates(A, G, nopen);
+            ensure_table(A, A.n_states + G);
+            B2_CUDA(cudaMemsetAsync(A.best.as<u64>() + A.cand_next, 0xFF, G * 8, s));
+            B2_CUDA(cudaMemsetAsync(A.flags.as<u8>() + A.cand_next, 0, G, s));
+            B2_CUDA(cudaMemsetAsync(A.stamp.as<u32>() + A.cand_next, 0, G * 4, s));
+            dev::DExpandArgs a{};
+            a.rows = A.rows.as<u64>();
+            a.frontier = A.front.as<u32>();
+            a.frontier_id = A.iota.as<u32>();
+            a.E = nF;
+            a.layer_begin = 0;
+            a.limit = ~u64{0};
+            a.gbase = A.cand_base.as<u64>();
+            a.local_base = A.cand_base.as<u64>();
+            a.staging = A.staging.as<u64>();
+            a.hist = A.hist.as<u64>();
+            a.world = 1;
+            a.W = W;
+            a.pi = pi;
+            if (task->jit)
+                jit_launch(task->jit->dbrfs_expand[pi], grid, 128, &a, s);
+            else
+                dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() { k_dexpand<OW, WR><<<grid, 128, 0, s>>>(T, a); });
+            if (A.opt.timings)
+                B2_CUDA(cudaEventRecord(ev[2], s));
+            InsertArgs in{};
+            in.staging = A.staging.as<u64>();
+            in.G = G;
+            in.W = W;
+            in.wave = wave;
+            in.cand_begin = A.cand_next;
+            in.frontier = A.front.as<u32>();
+            in.cand_base = A.cand_base.as<u64>();
+            in.nF = nF;
+            in.rows = A.rows.as<u64>();
+            in.hash = A.hash.as<u64>();
+            in.best = A.best.as<u64>();
+            in.flags = A.flags.as<u8>();
+            in.stamp = A.stamp.as<u32>();
+            in.par = A.par.as<u32>();
+            in.kid = A.kid.as<u32>();
+            in.table = A.table.as<u64>();
+            in.mask = A.table_slots - 1;
+            in.max_probe = max_probe(A.table_slots);
+            in.touched = A.touched.as<u32>();
+            in.fresh = A.fresh.as<u32>();
+            in.misc = misc;
+            k_astar_insert<<<grid_for(G, 256, sms * 16), 256, 0, s>>>(in);
+            B2_CUDA(cudaGetLastError());
+            if (A.opt.timings)
+                B2_CUDA(cudaEventRecord(ev[3], s));
+            launch_hmax(*A.H, A.rows.as<u64>(), W, A.fresh.as<u32>(), &misc->nfresh, G, A.hval.as<u32>(), true,
+                        A.flags.as<u8>(), static_cast<int>(sms), s);
+            if (A.opt.timings)
+                B2_CUDA(cudaEventRecord(ev[4], s));
+            k_astar_push<<<grid_for(G, 256, sms * 16), 256, 0, s>>>(A.touched.as<u32>(), misc, A.best.as<u64>(),
+                                                                      A.hval.as<u32>(), A.flags.as<u8>(),
+                                                                      static_cast<u32>(fcur), A.next.as<u32>(),
+                                                                      A.open.as<u64>());
+            B2_CUDA(cudaGetLastError());
+            A.launches += 4;
+            if (A.opt.timings)
+                B2_CUDA(cudaEventRecord(ev[5], s));
+        }
+        const AstarMisc m = read_misc(A);
+        if (A.opt.timings && G > 0)
+        {
+            float a = 0, b = 0, c = 0, d = 0;
+            B2_CUDA(cudaEventElapsedTime(&a, ev[0], ev[1]));
+            B2_CUDA(cudaEventElapsedTime(&b, ev[1], ev[2]));
+            B2_CUDA(cudaEventElapsedTime(&c, ev[2], ev[3]));
+            B2_CUDA(cudaEventElapsedTime(&d, ev[3], ev[5]));
+            count_ms += a;
+            expand_ms += b;
+            insert_ms += c;
+            eval_ms += d;
+        }
+        expanded += nF;
+        generated += G;
+        fresh_total += m.nfresh;
+        dead += m.ndead;
+        A.cand_next += G;
+        A.n_states += m.nfresh;
+        nopen = m.nopen;
+        if (m.best_goal != ~u64{0} && (m.best_goal >> 32) <= fcur)
+        {
+            A.solved = true;
+            A.cost = m.best_goal >> 32;
+            A.goal_state = static_cast<u32>(m.best_goal);
+            break;
+        }
+        if (m.nnext > 0)
+        {
+            A.front.swap(A.next);
+            nF = m.nnext;
+            continue;
+        }
+        // the current f is done: the smallest f of the open list is next
+        if (nopen == 0)
+        {
+            exhausted = true;
+            break;
+        }
+        B2_CUDA(cudaMemsetAsync(&misc->fmin, 0xFF, 8, s));
+        k_astar_fmin<<<grid_for(nopen, 256, sms * 16), 256, 0, s>>>(A.open.as<u64>(), nopen, A.best.as<u64>(),
+                                                                      A.hval.as<u32>(), A.flags.as<u8>(), misc);
+        B2_CUDA(cudaGetLastError());
+        ++A.launches;
+        const u64 fmin = read_misc(A).fmin;
+        if (fmin == ~u64{0})
+        {
+            exhausted = true;
+            break;
+        }
+        if (m.best_goal != ~u64{0} && (m.best_goal >> 32) <= fmin)
+        {
+            A.solved = true;
+            A.cost = m.best_goal >> 32;
+            A.goal_state = static_cast<u32>(m.best_goal);
+            break;
+        }
+        fcur = fmin;
+        ++f_layers;
+        if (A.front.bytes < nopen * 4)
+            A.front.alloc(nopen * 8, s);
+        B2_CUDA(cudaMemsetAsync(&misc->nkeep, 0, 16, s));
+        k_astar_extract<<<grid_for(nopen, 256, sms * 16), 256, 0, s>>>(A.open.as<u64>(), nopen, A.best.as<u64>(),
+                                                                         A.hval.as<u32>(), A.flags.as<u8>(), fmin,
+                                                                         A.front.as<u32>(), A.keep.as<u64>(), misc);
+        B2_CUDA(cudaGetLastError());
+        ++A.launches;
+        const AstarMisc m4 = read_misc(A);
+        A.open.swap(A.keep);
+        nopen = m4.nkeep;
+        nF = m4.nfront;
+        A.misc_host->nopen = nopen;
+        B2_CUDA(cudaMemcpyAsync(&misc->nopen, &A.misc_host->nopen, 8, cudaMemcpyHostToDevice, s));
+        if (nF == 0)
+        {
+            exhausted = true;
+            break;
+        }
+    }
+    stream_wait(s);
+    R.status = A.solved ? B2_SEARCH_SOLVED
+                        : dead_start ? B2_SEARCH_UNSOLVABLE : exhausted ? B2_SEARCH_EXHAUSTED : B2_SEARCH_OUT_OF_STATES;
+    R.cost = A.solved ? static_cast<double>(A.cost) : 0.0;
+    R.expanded = expanded;
+    R.generated = generated;
+    R.states = A.n_states;
+    R.evaluations += fresh_total;
+    R.dead_ends += dead;
+    R.waves = wave;
+    R.f_layers = f_layers;
+    R.plan_length = A.solved ? static_cast<u32>(A.cost) : 0;
+    R.count_ms = count_ms;
+    R.expand_ms = expand_ms;
+    R.insert_ms = insert_ms;
+    R.eval_ms = eval_ms;
+    R.kernel_launches = A.launches;
+    R.search_s = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+}
+}  // namespace
+
+extern "C" {
+
+b2_status b2_heuristic_create(b2_task* task, int32_t kind, b2_heuristic** out)
+{
+    return guarded([&] {
+        if (!task || !out)
+            throw std::invalid_argument("b2_heuristic_create: null argument");
+        if (kind != B2_HEURISTIC_MAX)
+            throw Error(B2_UNSUPPORTED, "b2_heuristic_create: the device evaluates h^max only");
+        *out = make_heuristic(task);
+    });
+}
+
+b2_status b2_heuristic_info_get(const b2_heuristic* h, b2_heuristic_info* out)
+{
+    return guarded([&] {
+        if (!h || !out)
+            throw std::invalid_argument("b2_heuristic_info_get: null argument");
+        out->props = h->R.props;
+        out->ops = h->R.ops();
+        out->reached_atoms = h->R.reached;
+        out->ground_actions = h->R.ground_actions;
+        out->goal_atoms = static_cast<uint32_t>(h->R.goal.size());
+        out->goal_unreachable = h->R.goal_unreachable ? 1 : 0;
+    });
+}
+
+b2_status b2_heuristic_evaluate(b2_heuristic* h, const uint64_t* rows, uint64_t stride, uint32_t words, uint64_t n,
+                                uint32_t* out, void* stream)
+{
+    return guarded([&] {
+        if (!h || (n && (!rows || !out)))
+            throw std::invalid_argument("b2_heuristic_evaluate: null argument");
+        if (!h->task->ctx)
+            throw std::invalid_argument("a host-only task (created without a context) cannot run on the device");
+        if (words != h->task->prog.words || stride < words)
+            throw std::invalid_argument("b2_heuristic_evaluate: rows must have the task's " +
+                                        std::to_string(h->task->prog.words) + " words (stride >= words)");
+        if (!n)
+            return;
+        B2_CUDA(cudaSetDevice(h->task->ctx->device));
+        launch_hmax(*h, rows, stride, nullptr, nullptr, n, out, false, nullptr, h->task->ctx->sms,
+                    static_cast<cudaStream_t>(stream));
+    });
+}
+
+void b2_heuristic_destroy(b2_heuristic* h) { delete h; }
+
+void b2_astar_options_default(b2_astar_options* o)
+{
+    if (!o)
+        return;
+    *o = b2_astar_options{};
+}
+
+b2_status b2_astar_create(b2_task* task, const b2_astar_options* options, b2_astar** out)
+{
+    return guarded([&] {
+        if (!task || !options || !out)
+            throw std::invalid_argument("b2_astar_create: null argument");
+        if (!task->ctx)
+            throw std::invalid_argument("a host-only task (created without a context) cannot run on the device");
+        if (options->witness_pruning && task->witness_refused)
+            throw Error(B2_UNSUPPORTED, "witness pruning with a witness parameter before an effect parameter");
+        B2_CUDA(cudaSetDevice(task->ctx->device));
+        auto A = std::make_unique<b2_astar>();
+        A->task = task;
+        A->opt = *options;
+        A->W = task->prog.words;
+        if (options->heuristic)
+        {
+            if (options->heuristic->task != task)
+                throw std::invalid_argument("b2_astar_create: the heuristic belongs to another task");
+            A->H = options->heuristic;
+        }
+        else
+        {
+            A->H = make_heuristic(task);
+            A->own_h = true;
+        }
+        if (options->stream)
+            A->stream = static_cast<cudaStream_t>(options->stream);
+        else
+        {
+            B2_CUDA(cudaStreamCreateWithFlags(&A->stream, cudaStreamNonBlocking));
+            A->own_stream = true;
+        }
+        A->hist.alloc(64, A->stream);
+        *out = A.release();
+    });
+}
+
+b2_status b2_astar_run(b2_astar* A, b2_astar_result* result)
+{
+    return guarded([&] {
+        if (!A || !result)
+            throw std::invalid_argument("b2_astar_run: null argument");
+        if (A->ran)
+            throw std::invalid_argument("b2_astar_run: the search ran already");
+        A->ran = true;
+        B2_CUDA(cudaSetDevice(A->task->ctx->device));
+        *result = b2_astar_result{};
+        run_astar(*A, *result);
+    });
+}
+
+b2_status b2_astar_plan(b2_astar* A, uint32_t* parent, uint32_t* index, uint32_t cap, uint32_t* len)
+{
+    return guarded([&] {
+        if (!A || !len || !A->ran)
+            throw std::invalid_argument("b2_astar_plan: bad argument");
+        if (!A->solved)
+            throw std::invalid_argument("b2_astar_plan: the search found no plan");
+        const u32 n = static_cast<u32>(A->cost);
+        *len = n;
+        if (cap < n || !n)
+            return;
+        if (!parent || !index)
+            throw std::invalid_argument("b2_astar_plan: null output");
+        B2_CUDA(cudaSetDevice(A->task->ctx->device));
+        DeviceBuffer tmp;
+        tmp.alloc((2 * static_cast<u64>(n) + 1) * 4);
+        u32* tp = tmp.as<u32>();
+        k_astar_path<<<1, 1, 0, A->stream>>>(A->best.as<u64>(), A->par.as<u32>(), A->kid.as<u32>(), A->goal_state, n,
+                                            tp, tp + n, tp + 2 * n);
+        B2_CUDA(cudaGetLastError());
+        std::vector<u32> host(2 * static_cast<u64>(n) + 1);
+        B2_CUDA(cudaMemcpyAsync(host.data(), tp, host.size() * 4, cudaMemcpyDeviceToHost, A->stream));
+        B2_CUDA(cudaStreamSynchronize(A->stream));
+        if (host[2 * n] != n)
+            throw Error(B2_DEVICE_FAULT, "b2_astar_plan: the parent chain does not reach the root in cost steps");
+        for (u32 i = 0; i < n; ++i)  // root first
+        {
+            parent[i] = host[n - 1 - i];
+            index[i] = host[n + n - 1 - i];
+        }
+    });
+}
+
+void b2_astar_destroy(b2_astar* A)
+{
+    if (!A)
+        return;
+    cudaSetDevice(A->task->ctx->device);
+    for (DeviceBuffer* b : {&A->rows, &A->hash, &A->best, &A->hval, &A->flags, &A->stamp, &A->par, &A->kid,
+                            &A->table, &A->counts, &A->cand_base, &A->iota, &A->staging, &A->touched, &A->fresh,
+                            &A->front, &A->next, &A->sums, &A->open, &A->keep, &A->misc, &A->hist})
+        b->reset();
+    if (A->stream)
+    {
+        stream_drain(A->stream);
+        if (A->own_stream)
+            cudaStreamDestroy(A->stream);
+    }
+    A->task->ctx->pinned.give(A->misc_host);
+    if (A->own_h)
+        delete A->H;
+    delete A;
+}
+
+}  // extern "C"

@@ -148,6 +148,14 @@ struct DeviceBuffer
     {
         return static_cast<T*>(p);
     }
+    /// Exchanges two buffers' allocations.
+    void swap(DeviceBuffer& o) noexcept
+    {
+        std::swap(p, o.p);
+        std::swap(bytes, o.bytes);
+        std::swap(stream, o.stream);
+        std::swap(pooled, o.pooled);
+    }
 };
 }  // namespace b2
 

@@ -78,69 +78,6 @@ __global__ void k_dscatter(const u32* __restrict__ counts, const u32* __restrict
     }
 }
 
-/// Interpreted matcher: the records of the local parents' successors (the compiled twin is b2j_dbrfs_expand).
-template<int OW, int WR>
-__global__ void __launch_bounds__(128) k_dexpand(DevTask T, DExpandArgs a)
-{
-    __shared__ u32 hist[kMaxWorld];
-    for (u32 d = threadIdx.x; d < a.world; d += blockDim.x)
-        hist[d] = 0;
-    __syncthreads();
-    const u32 W = a.W;
-    for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < a.E; i += static_cast<u64>(gridDim.x) * blockDim.x)
-    {
-        const u64 id = a.frontier_id[i];
-        if (id >= a.limit)
-            continue;
-        const auto st = load_row<WR>(a.rows + static_cast<u64>(a.frontier[i]) * W, W);
-        const u64 c0 = a.gbase[id - a.layer_begin];
-        u64* out = a.staging + a.local_base[i] * (W + 2);
-        u32 k = 0;
-        u32 bind[kMaxLevels] = {};
-        for (u32 s = 0; s < T.nschemas; ++s)
-        {
-            const DSchema& sc = T.schemas[s];
-            enumerate<OW>(T, sc.prog[a.pi], st, bind, [&](const u32* b) {
-                u64* r = out + static_cast<u64>(k) * (W + 2);
-                u64 h;
-                if constexpr (WR > 0)
-                {
-                    RegRow<WR> nx = st;
-                    for (u32 q = sc.del_begin; q < sc.del_end; ++q)
-                    {
-                        const u64 key = pattern_key(T, T.lits[q], b);
-                        if (key < T.fluent_count)
-                            nx.clear(static_cast<u32>(key));
-                    }
-                    for (u32 q = sc.add_begin; q < sc.add_end; ++q)
-                        nx.set(static_cast<u32>(pattern_key(T, T.lits[q], b)));
-                    h = hash_words([&](u32 q) { return nx.word(q); }, W);
-                    for (u32 q = 0; q < W; ++q)
-                        r[q] = nx.word(q);
-                }
-                else
-                {
-                    Effects e;
-                    collect_effects(T, sc, b, e);
-                    const SuccRow<decltype(st)> nx{st, e};
-                    h = hash_words([&](u32 q) { return nx.word(q); }, W);
-                    for (u32 q = 0; q < W; ++q)
-                        r[q] = nx.word(q);
-                }
-                r[W] = h;
-                r[W + 1] = c0 + k;
-                atomicAdd(&hist[owner_of(h, a.world)], 1u);
-                ++k;
-                return true;
-            });
-        }
-    }
-    __syncthreads();
-    for (u32 d = threadIdx.x; d < a.world; d += blockDim.x)
-        if (hist[d])
-            atomicAdd(reinterpret_cast<unsigned long long*>(a.hist + d), static_cast<unsigned long long>(hist[d]));
-}
-
 constexpr unsigned kPushThreads = 256;
 constexpr u32 kPushSmemWords = 5120;  // 40 KB of staged records per block (with the static arrays, under 48 KB)
 

@@ -1,6 +1,7 @@
 """Device searches: ``brfs`` mirrors mymyr.cuda.brfs (python/src/cuda_bindings.cpp:2715-2745 in maichmueller/mymyr) and
-returns a result with the fields of BrfsResult and DeviceBrfsStats; ``hash_rows`` mirrors mymyr.hash_rows
-(python/src/module.cpp:187)."""
+returns a result with the fields of BrfsResult and DeviceBrfsStats; ``astar`` mirrors mymyr.cuda.astar with h^max
+(python/src/cuda_heuristics_bindings.cpp:518) and ``Heuristic`` mymyr.cuda.Heuristic's h^max (:385-450); ``hash_rows``
+mirrors mymyr.hash_rows (python/src/module.cpp:187)."""
 
 from __future__ import annotations
 
@@ -203,3 +204,144 @@ def hash_rows(states, *, numeric_words: int = 0, stream=None, ctx: Context | Non
     st = stream if stream is not None else torch.cuda.current_stream(states.device).cuda_stream
     check(lib().b2_hash_rows(ctx.handle, states.data_ptr(), states.shape[0], states.shape[1], out.data_ptr(), st))
     return out
+
+
+class Heuristic:
+    """h^max on the device (mymyr.cuda.Heuristic with kind "max"): grounds the delete relaxation of the task on
+    creation; ``evaluate(states)`` returns h of each row (uint32, ``DEAD_END`` for dead ends)."""
+
+    DEAD_END = _lib.B2_DEAD_END
+
+    def __init__(self, task: Task, kind: str = "max"):
+        if kind != "max":
+            raise ValueError("mymyr_b200 Heuristic: the device evaluates h^max only")
+        self.task = task
+        h = C.c_void_p()
+        check(lib().b2_heuristic_create(task.handle, _lib.B2_HEURISTIC_MAX, C.byref(h)))
+        self._h = h
+        info = _lib.HeuristicInfo()
+        check(lib().b2_heuristic_info_get(h, C.byref(info)))
+        self.info = {k: getattr(info, k) for k, _ in _lib.HeuristicInfo._fields_}
+
+    @property
+    def handle(self):
+        return self._h
+
+    def evaluate(self, states, *, stream=None):
+        """h of a CUDA [N, W] tensor of 64-bit words -> [N] int64 (uint32 values; DEAD_END for dead ends)."""
+        import torch
+
+        if not states.is_cuda or states.dim() != 2 or states.element_size() != 8:
+            raise ValueError("Heuristic.evaluate: states must be a CUDA [N, W] tensor of 64-bit words")
+        states = states.contiguous()
+        n, W = states.shape
+        out = torch.empty(n, dtype=torch.int32, device=states.device)
+        st = stream if stream is not None else torch.cuda.current_stream(states.device).cuda_stream
+        check(lib().b2_heuristic_evaluate(self._h, states.data_ptr(), W, W, n, out.data_ptr(), st))
+        return out.to(torch.int64) & 0xFFFFFFFF
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value and _lib._lib is not None:
+            _lib._lib.b2_heuristic_destroy(h)
+        self._h = None
+
+
+ASTAR_STATUS = {0: "solved", 1: "exhausted", 2: "out_of_states", 3: "unsolvable"}
+
+
+@dataclass
+class AstarResult:
+    """search::BestFirstResult's fields for A* (status, cost, plan length, expanded, generated, states, evaluations,
+    dead ends, initial h) plus the device's counters."""
+
+    status: str
+    cost: float
+    plan_length: int
+    expanded: int
+    generated: int
+    states: int
+    evaluations: int
+    dead_ends: int
+    initial_h: float
+    waves: int
+    f_layers: int
+    search_s: float
+    stats: dict = field(default_factory=dict)
+    _search: object = None
+
+    @property
+    def solved(self) -> bool:
+        return self.status == "solved"
+
+    def plan_steps(self):
+        """The plan as (parent state, successor index) per step, root first (b2_astar_plan)."""
+        n = C.c_uint32()
+        check(lib().b2_astar_plan(self._search, None, None, 0, C.byref(n)))
+        p = np.zeros(n.value, np.uint32)
+        k = np.zeros(n.value, np.uint32)
+        check(lib().b2_astar_plan(self._search, p.ctypes.data, k.ctypes.data, n.value, C.byref(n)))
+        return p, k
+
+    def plan(self, task: Task):
+        """The plan's actions as (schema index, binding) and its states, replayed from the initial state with the
+        batched expand (the successor index is a position in canonical order)."""
+        import torch
+
+        from . import rl
+
+        _, idx = self.plan_steps()
+        row = torch.from_numpy(task.initial_state().view(np.int64)).reshape(1, -1).to(f"cuda:{task.ctx.device}")
+        actions, states = [], [row.cpu().numpy().view(np.uint64)[0].copy()]
+        for k in idx:
+            e = rl.expand(task, row, succ=True)
+            j = int(e.offsets[0]) + int(k)
+            actions.append((int(e.schema[j]), tuple(int(x) for x in e.binding[j].tolist() if x >= 0)))
+            row = e.succ[j: j + 1].clone()
+            states.append(row.cpu().numpy().view(np.uint64)[0].copy())
+        return actions, states
+
+    def close(self):
+        if self._search is not None and _lib._lib is not None:
+            _lib._lib.b2_astar_destroy(self._search)
+        self._search = None
+
+    def __del__(self):
+        self.close()
+
+
+def astar(task: Task, ctx: Context | None = None, heuristic="max", *, witness_pruning: bool = False,
+          max_expansions: int | None = None, expected_states: int | None = None, timings: bool = False,
+          stream=None) -> AstarResult:
+    """Eager A* with h^max and unit costs on the device (mymyr.cuda.astar / search::astar_eager): the optimal plan
+    cost. ``heuristic`` is "max" or a ``Heuristic`` of the same task (to share its grounding)."""
+    if ctx is not None and task.ctx is not None and ctx.device != task.ctx.device:
+        raise ValueError("mymyr_b200 astar: the task lives on another device than ctx")
+    o = _lib.AstarOptions()
+    lib().b2_astar_options_default(C.byref(o))
+    o.witness_pruning = int(bool(witness_pruning))
+    o.timings = int(bool(timings))
+    if max_expansions is not None:
+        o.max_expansions = int(max_expansions)
+    if expected_states is not None:
+        o.expected_states = int(expected_states)
+    if stream is not None:
+        o.stream = stream
+    if isinstance(heuristic, Heuristic):
+        o.heuristic = heuristic.handle
+    elif heuristic != "max":
+        raise ValueError("mymyr_b200 astar: the device runs h^max only")
+    h = C.c_void_p()
+    check(lib().b2_astar_create(task.handle, C.byref(o), C.byref(h)))
+    r = _lib.AstarResult()
+    try:
+        check(lib().b2_astar_run(h, C.byref(r)))
+    except Exception:
+        lib().b2_astar_destroy(h)
+        raise
+    stats = {k: getattr(r, k) for k in ("count_ms", "expand_ms", "insert_ms", "eval_ms", "kernel_launches",
+                                        "relaxed_ops", "relaxed_atoms")}
+    return AstarResult(status=ASTAR_STATUS.get(r.status, str(r.status)), cost=r.cost, plan_length=r.plan_length,
+                       expanded=r.expanded, generated=r.generated, states=r.states, evaluations=r.evaluations,
+                       dead_ends=r.dead_ends, initial_h=r.initial_h, waves=r.waves, f_layers=r.f_layers,
+                       search_s=r.search_s, stats=stats, _search=h)

@@ -7,6 +7,7 @@ predicates, as the reference's normalization compiles them. The random source is
     transport(2, 40, 2, seed=0)      config [2]: two-room gripper transport for the env step
     sliding_tile(4, 4, 60, seed=0)   config [3]: 4x4 sliding tile, BrFS to depth 22
     random_domain(seed=0)            config [4]: 24 predicates, 16 schemas of 3-5 parameters, 200 typed objects
+    logistics(8, 4, 6, 2, 30, seed=0)  config [5]: logistics for A* with h^max
 """
 
 from __future__ import annotations
@@ -259,6 +260,74 @@ def random_domain(seed: int = 0, n_types: int = 10, per_type: int = 20, n_unary:
         t.fluent_init.append((p, args))
     p, sig = sigs[-1]
     t.goal.append((p, True, tuple(ty * per_type for ty in sig)))
+    return t.text()
+
+
+def logistics(n_cities: int = 8, locs_per_city: int = 4, n_trucks: int = 6, n_airplanes: int = 2,
+              n_packages: int = 30, seed: int = 0) -> str:
+    """Logistics: packages travel by truck between the locations of a city and by airplane between airports (the
+    first location of every city); predicates at(object, location), in(package, vehicle), in-city(location, city)
+    (static) plus type predicates and airport; schemas load, unload, drive, fly, unit cost. Trucks start in distinct
+    cities (one per city while there are trucks); a package's origin and destination are drawn among the locations a
+    truck or an airplane serves (the airport only, in a city without a truck), and differ."""
+    rng = SplitMix(seed)
+    C, L = n_cities, n_cities * locs_per_city
+    cities = list(range(C))
+    locs = list(range(C, C + L))
+    trucks = list(range(C + L, C + L + n_trucks))
+    planes = list(range(C + L + n_trucks, C + L + n_trucks + n_airplanes))
+    pkgs = list(range(C + L + n_trucks + n_airplanes, C + L + n_trucks + n_airplanes + n_packages))
+    t = TaskText(n=C + L + n_trucks + n_airplanes + n_packages)
+    city = t.pred("S", 1, "city")
+    location = t.pred("S", 1, "location")
+    truck = t.pred("S", 1, "truck")
+    airplane = t.pred("S", 1, "airplane")
+    vehicle = t.pred("S", 1, "vehicle")
+    package = t.pred("S", 1, "package")
+    airport = t.pred("S", 1, "airport")
+    in_city = t.pred("S", 2, "in-city")
+    at = t.pred("F", 2, "at")
+    inside = t.pred("F", 2, "in")
+    city_of = {}
+    for c in cities:
+        t.static_init.append((city, (c,)))
+        for k in range(locs_per_city):
+            l = locs[c * locs_per_city + k]
+            city_of[l] = c
+            t.static_init.append((location, (l,)))
+            t.static_init.append((in_city, (l, c)))
+            if k == 0:
+                t.static_init.append((airport, (l,)))
+    for v in trucks:
+        t.static_init += [(truck, (v,)), (vehicle, (v,))]
+    for v in planes:
+        t.static_init += [(airplane, (v,)), (vehicle, (v,))]
+    for p in pkgs:
+        t.static_init.append((package, (p,)))
+    truck_cities = rng.shuffle(cities)[:n_trucks] if n_trucks <= C else [rng.below(C) for _ in trucks]
+    for v, c in zip(trucks, truck_cities):
+        t.fluent_init.append((at, (v, locs[c * locs_per_city + rng.below(locs_per_city)])))
+    for v in planes:
+        t.fluent_init.append((at, (v, locs[rng.below(C) * locs_per_city])))
+    served = [l for l in locs if city_of[l] in set(truck_cities) or (l - C) % locs_per_city == 0]
+    for p in pkgs:
+        a = served[rng.below(len(served))]
+        b = a
+        while b == a:
+            b = served[rng.below(len(served))]
+        t.fluent_init.append((at, (p, a)))
+        t.goal.append((at, True, (p, b)))
+    t.schemas.append(("load", 3, [(package, 1, (0,)), (vehicle, 1, (1,)), (location, 1, (2,)), (at, 1, (1, 2)),
+                                  (at, 1, (0, 2))],
+                      [(at, 0, (0, 2)), (inside, 1, (0, 1))]))
+    t.schemas.append(("unload", 3, [(package, 1, (0,)), (vehicle, 1, (1,)), (location, 1, (2,)), (at, 1, (1, 2)),
+                                    (inside, 1, (0, 1))],
+                      [(inside, 0, (0, 1)), (at, 1, (0, 2))]))
+    t.schemas.append(("drive", 4, [(truck, 1, (0,)), (location, 1, (1,)), (location, 1, (2,)), (city, 1, (3,)),
+                                   (at, 1, (0, 1)), (in_city, 1, (1, 3)), (in_city, 1, (2, 3))],
+                      [(at, 0, (0, 1)), (at, 1, (0, 2))]))
+    t.schemas.append(("fly", 3, [(airplane, 1, (0,)), (airport, 1, (1,)), (airport, 1, (2,)), (at, 1, (0, 1))],
+                      [(at, 0, (0, 1)), (at, 1, (0, 2))]))
     return t.text()
 
 

@@ -36,7 +36,7 @@ def lib():
         L.ref_task_open.argtypes = [C.c_char_p, C.c_int, C.c_int]
         L.ref_task_close.argtypes = [P]
         for name in ("ref_task_info", "ref_initial_state", "ref_is_goal", "ref_brfs", "ref_brfs_states", "ref_expand",
-                     "ref_env_reset", "ref_env_step", "ref_pool_bench", "ref_astar"):
+                     "ref_env_reset", "ref_env_step", "ref_pool_bench", "ref_astar", "ref_hmax", "ref_ground_stats"):
             getattr(L, name).restype = C.c_int64
         L.ref_task_info.argtypes = [P, P]
         L.ref_initial_state.argtypes = [P, P, C.c_uint32]
@@ -60,6 +60,8 @@ def lib():
                                    C.c_uint32, P, P, P]
         L.ref_pool_bench.argtypes = [P, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint64, P, P]
         L.ref_astar.argtypes = [P, P, P]
+        L.ref_hmax.argtypes = [P, P, C.c_uint64, C.c_uint32, P]
+        L.ref_ground_stats.argtypes = [P, P]
         _L = L
     return _L
 
@@ -165,6 +167,19 @@ class RefTask:
         _check(lib().ref_astar(self.h, out.ctypes.data, C.byref(sec)))
         return dict(solved=bool(out[0]), cost=out[1], plan_length=int(out[2]), expanded=int(out[3]),
                     generated=int(out[4]), seconds=sec.value)
+
+    def hmax(self, rows: np.ndarray) -> np.ndarray:
+        """h^max (unit costs, grounded) of each row; +inf for dead ends."""
+        rows = np.ascontiguousarray(rows, np.uint64)
+        out = np.zeros(rows.shape[0], np.float64)
+        _check(lib().ref_hmax(self.h, rows.ctypes.data, rows.shape[0], rows.shape[1], out.ctypes.data))
+        return out
+
+    def ground_stats(self) -> dict:
+        out = np.zeros(5, np.uint64)
+        _check(lib().ref_ground_stats(self.h, out.ctypes.data))
+        return dict(zip(["reached_atoms", "ground_actions", "operators", "propositions", "rounds"],
+                        (int(x) for x in out)))
 
     def pool_bench(self, num_envs, steps, threads, seed=0):
         sec = C.c_double()

