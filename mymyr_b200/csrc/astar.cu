@@ -11,14 +11,18 @@
 // ends the state as a dead end (+inf).
 //
 // A*. h^max is consistent, so the states leave the open list in f order with their final g, and a bucket of equal f
-// can be expanded as a batch: each wave expands the current frontier (all open states of the current f), its
-// successors are staged, inserted into the hash set in one kernel (all staged rows are in memory, so the insert is
-// single-phase: a new state takes an empty slot; an equal one lowers the state's g with atomicMin on (g << 32 |
-// candidate index), which also picks a deterministic parent among equal g), new states are goal-tested and
-// evaluated, and every state whose g was set or lowered is pushed: into the next wave if its f equals the current f,
-// else into the open list of later f. When the current f reaches the g of the best goal found, that g is the optimal
-// cost (a goal is recognized when generated and returned when it is the minimum f, as in the reference). Open entries
-// of states that were lowered later are stale and skipped (f != g + h).
+// can be expanded as a batch: each wave expands the current frontier (all open states of the current f) into staged
+// records [row | hash | c] (c: the successor's index in the wave, in canonical order), inserts them into the hash set
+// in one kernel (all staged rows are in memory, so the insert is single-phase), gives the new states compact ids by a
+// scan, goal-tests and evaluates them, and pushes every state whose g was set or lowered: into the next wave if its f
+// equals the current f, else into the open list of later f. When the current f reaches the g of the best goal found,
+// that g is the optimal cost (a goal is recognized when generated and returned when it is the minimum f, as in the
+// reference). Open entries of states lowered later are stale and skipped (f != g + h).
+//
+// A state's best path is one u64, key = g << 48 | parent << 16 | successor index: atomicMin on it keeps the smallest
+// g and, among equal g, the smallest (parent, successor index), so the plan is deterministic and needs no parent
+// arrays. A table slot holds (hash >> 32) << 32 | id, id a state or, during a wave's insert, 2^31 | r for the wave's
+// record r that claimed the slot (rewritten to the new state's id by the id scan).
 
 #include "brfs.cuh"
 #include "relax.hpp"
@@ -53,7 +57,7 @@ __device__ __forceinline__ bool sbit(const u64* b, u32 s) { return (b[s >> 6] >>
 /// h^max of states: state i is row rows + node(i) * stride, node(i) = nodes[i] (or i), for i < n (*n_dev if given).
 /// Warp per state; shared memory: two W-word bitsets per warp.
 __global__ void k_hmax(HmaxArgs H, const u64* __restrict__ rows, u64 stride, const u32* __restrict__ nodes,
-                       const u32* n_dev, u64 n_host, u32* __restrict__ out, u32 out_by_node)
+                       const u64* n_dev, u64 n_host, u32* __restrict__ out, u32 out_by_node)
 {
     extern __shared__ u64 sm[];
     const u32 lane = threadIdx.x & 31, wib = threadIdx.x >> 5, wpb = blockDim.x >> 5;
@@ -137,17 +141,23 @@ __global__ void k_hmax(HmaxArgs H, const u64* __restrict__ rows, u64 stride, con
 /// Per-wave counters of the A* (device side, mirrored to pinned host memory).
 struct AstarMisc
 {
-    LayerMisc lm;       // count pass: total candidates of the wave, status
-    u32 ntouched;       // states whose g was set or lowered this wave
-    u32 nfresh;         // new states this wave
-    u32 nnext;          // states of the next wave (f = current f)
-    u32 ndead;          // dead ends among this wave's new states
-    u64 nopen;          // open entries of later f
-    u64 best_goal;      // (g << 32 | state) of the best goal found (~0: none)
-    u64 fmin;           // smallest f of a valid open entry (bucket switch)
-    u64 nkeep;          // open entries kept by the extraction
-    u64 nfront;         // states extracted into the frontier
+    LayerMisc lm;   // count pass: total candidates of the wave, status
+    u32 ntouched;   // states whose g was set or lowered this wave
+    u32 nnext;      // states of the next wave (f = current f)
+    u32 ndead;      // dead ends among the wave's new states
+    u32 pad;
+    u64 nfresh;     // new states this wave (the id scan's total)
+    u64 nopen;      // open entries of later f
+    u64 best_goal;  // (g << 32 | state) of the best goal found (~0: none)
+    u64 fmin;       // smallest f of a valid open entry (bucket switch)
+    u64 nkeep;      // open entries kept by the extraction
+    u64 nfront;     // states extracted into the frontier
 };
+
+constexpr u32 kWaveBit = 0x80000000u;
+constexpr u64 kNoParent = 0xFFFFFFFFull;
+
+__device__ __forceinline__ u32 key_g(u64 key) { return static_cast<u32>(key >> 48); }
 
 struct InsertArgs
 {
@@ -155,23 +165,21 @@ struct InsertArgs
     u64 G;
     u32 W;
     u32 wave;
-    u64 cand_begin;
     const u32* frontier;
     const u64* cand_base;
     u64 nF;
-    u64* rows;
-    u64* hash;
-    u64* best;
-    u8* flags;
-    u32* stamp;
-    u32* par;
-    u32* kid;
+    const u64* rows;   // states
+    u64* best;         // per state
+    const u8* flags;   // per state
+    u32* stamp;        // per state
     u64* table;
     u64 mask;
     u32 max_probe;
     u32 pad;
+    u64* best_rec;     // per record: the key of a record that claimed a slot
+    u64* slot_of;      // per record: its slot
+    u8* claimed;       // per record
     u32* touched;
-    u32* fresh;
     AstarMisc* misc;
 };
 
@@ -192,13 +200,15 @@ __global__ void k_astar_insert(InsertArgs a)
             else
                 hi = mid;
         }
-        const u32 parent = a.frontier[lo];
-        const u64 cand = a.cand_begin + r;
-        a.par[cand] = parent;
-        a.kid[cand] = static_cast<u32>(c - a.cand_base[lo]);
-        const u32 gnew = static_cast<u32>(a.best[parent] >> 32) + 1;
-        const u64 key = (static_cast<u64>(gnew) << 32) | cand;
-        const u64 mine = (h & 0xFFFFFFFF00000000ull) | cand;
+        const u64 parent = a.frontier[lo], kid = c - a.cand_base[lo];
+        const u32 gnew = key_g(a.best[parent]) + 1;
+        if (kid > 0xFFFF || gnew > 0xFFFF)
+        {
+            atomicOr(&a.misc->lm.status, kStatusCapacity);  // a state with 2^16 successors, or a path of 2^16 steps
+            continue;
+        }
+        const u64 key = (static_cast<u64>(gnew) << 48) | (parent << 16) | kid;
+        const u64 tag = h & 0xFFFFFFFF00000000ull;
         u64 j = h & a.mask;
         bool done = false;
         for (u32 probe = 0; probe < a.max_probe; ++probe, j = (j + 1) & a.mask)
@@ -206,43 +216,89 @@ __global__ void k_astar_insert(InsertArgs a)
             u64 cur = __ldcg(a.table + j);
             if (cur == kEmpty)
             {
-                const u64 prev = atomicCAS(reinterpret_cast<unsigned long long*>(a.table + j), kEmpty, mine);
+                const u64 prev = atomicCAS(reinterpret_cast<unsigned long long*>(a.table + j), kEmpty,
+                                           tag | kWaveBit | r);
                 if (prev == kEmpty)
                 {
-                    u64* dst = a.rows + cand * W;
-                    for (u32 q = 0; q < W; ++q)
-                        dst[q] = rec[q];
-                    a.hash[cand] = h;
-                    atomicMin(reinterpret_cast<unsigned long long*>(a.best + cand), key);
-                    if (atomicExch(a.stamp + cand, a.wave) != a.wave)
-                        a.touched[atomicAdd(&a.misc->ntouched, 1u)] = static_cast<u32>(cand);
-                    a.fresh[atomicAdd(&a.misc->nfresh, 1u)] = static_cast<u32>(cand);
+                    a.claimed[r] = 1;
+                    a.slot_of[r] = j;
+                    atomicMin(reinterpret_cast<unsigned long long*>(a.best_rec + r), key);
                     done = true;
                     break;
                 }
                 cur = prev;
             }
-            if ((cur >> 32) != (mine >> 32))
+            if ((cur & 0xFFFFFFFF00000000ull) != tag)
                 continue;
-            const u64 o = cur & 0xFFFFFFFFull;
-            const u64* orow = o >= a.cand_begin ? a.staging + (o - a.cand_begin) * RW : a.rows + o * W;
+            const u32 holder = static_cast<u32>(cur);
+            const bool wave = holder & kWaveBit;
+            const u64 o = holder & ~kWaveBit;
+            const u64* orow = wave ? a.staging + o * RW : a.rows + o * W;
             bool eq = true;
             for (u32 q = 0; q < W && eq; ++q)
                 eq = orow[q] == rec[q];
             if (!eq)
                 continue;
             done = true;
-            if (a.flags[o] & (kClosed | kDead))
-                break;  // expanded with its final g (h^max is consistent), or a dead end
-            const u64 old = atomicMin(reinterpret_cast<unsigned long long*>(a.best + o), key);
-            if ((old >> 32) > gnew && atomicExch(a.stamp + o, a.wave) != a.wave)
-                a.touched[atomicAdd(&a.misc->ntouched, 1u)] = static_cast<u32>(o);
+            if (wave)
+                atomicMin(reinterpret_cast<unsigned long long*>(a.best_rec + o), key);
+            else if (!(a.flags[o] & (kClosed | kDead)))  // closed states have their final g (h^max is consistent)
+            {
+                const u64 old = atomicMin(reinterpret_cast<unsigned long long*>(a.best + o), key);
+                if (key_g(old) > gnew && atomicExch(a.stamp + o, a.wave) != a.wave)
+                    a.touched[atomicAdd(&a.misc->ntouched, 1u)] = static_cast<u32>(o);
+            }
             break;
         }
         if (!done)
             atomicOr(&a.misc->lm.status, kStatusProbeLimit);
     }
 }
+
+/// The id scan's input: whether record r claimed a slot.
+struct ClaimIn
+{
+    const u8* claimed;
+    __device__ __forceinline__ u32 operator()(u64 r) const { return claimed[r]; }
+};
+
+/// The id scan's output: record r that claimed a slot becomes state n_states + its rank; its row, hash and key move to
+/// the state arrays, its slot is rewritten to the state's id, and the state is listed fresh and touched.
+struct ClaimOut
+{
+    const u64* staging;
+    u32 W;
+    u32 wave;
+    u64 n_states;
+    const u64* best_rec;
+    const u64* slot_of;
+    u64* table;
+    u64* rows;
+    u64* hash;
+    u64* best;
+    u8* flags;
+    u32* stamp;
+    u32* fresh;
+    u32* touched;
+    AstarMisc* misc;
+    __device__ __forceinline__ void operator()(u64 r, u64 rank, u32 v) const
+    {
+        if (!v)
+            return;
+        const u64 s = n_states + rank;
+        const u64* rec = staging + r * (W + 2);
+        for (u32 q = 0; q < W; ++q)
+            rows[s * W + q] = rec[q];
+        const u64 h = rec[W];
+        hash[s] = h;
+        best[s] = best_rec[r];
+        flags[s] = 0;
+        stamp[s] = wave;
+        table[slot_of[r]] = (h & 0xFFFFFFFF00000000ull) | s;
+        fresh[rank] = static_cast<u32>(s);
+        touched[atomicAdd(&misc->ntouched, 1u)] = static_cast<u32>(s);
+    }
+};
 
 /// Pushes the states whose g was set or lowered this wave: dead ends are marked, goals recorded, the others go to
 /// the next wave (f = fcur; closed now, as they will be expanded) or to the open list of later f.
@@ -260,7 +316,7 @@ __global__ void k_astar_push(const u32* __restrict__ touched, AstarMisc* misc, c
             atomicAdd(&misc->ndead, 1u);
             continue;
         }
-        const u64 g = best[o] >> 32;
+        const u64 g = key_g(best[o]);
         if (flags[o] & kGoal)
             atomicMin(reinterpret_cast<unsigned long long*>(&misc->best_goal), (g << 32) | o);
         const u64 f = g + hv;
@@ -277,7 +333,7 @@ __global__ void k_astar_push(const u32* __restrict__ touched, AstarMisc* misc, c
 __device__ __forceinline__ bool open_valid(u64 e, const u64* best, const u32* h, const u8* flags)
 {
     const u32 o = static_cast<u32>(e);
-    return !(flags[o] & (kClosed | kDead)) && (e >> 32) == (best[o] >> 32) + h[o];
+    return !(flags[o] & (kClosed | kDead)) && (e >> 32) == static_cast<u64>(key_g(best[o])) + h[o];
 }
 
 __global__ void k_astar_fmin(const u64* __restrict__ open, u64 n, const u64* __restrict__ best,
@@ -314,16 +370,14 @@ __global__ void k_astar_extract(const u64* __restrict__ open, u64 n, const u64* 
     }
 }
 
-__global__ void k_astar_seed(u64* rows, u64* hash, u32 W, u64* best, u8* flags, u32* par, u32* kid, u64* table,
-                             u64 mask, u32 max_probe, AstarMisc* misc)
+__global__ void k_astar_seed(u64* rows, u64* hash, u32 W, u64* best, u8* flags, u64* table, u64 mask, u32 max_probe,
+                             AstarMisc* misc)
 {
     const GlobalRow r{rows, W};
     const u64 h = hash_words([&](u32 q) { return r.word(q); }, W);
     hash[0] = h;
-    best[0] = 0;
+    best[0] = kNoParent << 16;  // g 0, no parent
     flags[0] = kClosed;
-    par[0] = 0xFFFFFFFFu;
-    kid[0] = 0;
     u64 j = h & mask;
     for (u32 probe = 0; probe < max_probe && table[j] != kEmpty; ++probe)
         j = (j + 1) & mask;
@@ -333,17 +387,17 @@ __global__ void k_astar_seed(u64* rows, u64* hash, u32 W, u64* best, u8* flags, 
         atomicOr(&misc->lm.status, kStatusProbeLimit);
 }
 
-/// The path from the root to state `goal`: (parent state, successor index) per step, goal first.
-__global__ void k_astar_path(const u64* best, const u32* par, const u32* kid, u32 goal, u32 cap, u32* out_parent,
-                             u32* out_index, u32* len)
+/// The path from the root to state `goal` by the states' keys: (parent state, successor index) per step, goal first.
+__global__ void k_astar_path(const u64* best, u32 goal, u32 cap, u32* out_parent, u32* out_index, u32* len)
 {
     u32 s = goal, n = 0;
     while (s != 0 && n < cap)
     {
-        const u32 c = static_cast<u32>(best[s]);  // the candidate that set the state's g
-        out_parent[n] = par[c];
-        out_index[n] = kid[c];
-        s = par[c];
+        const u64 key = best[s];
+        const u32 p = static_cast<u32>((key >> 16) & 0xFFFFFFFFull);
+        out_parent[n] = p;
+        out_index[n] = static_cast<u32>(key & 0xFFFF);
+        s = p;
         ++n;
     }
     *len = s == 0 ? n : 0xFFFFFFFFu;
@@ -430,7 +484,7 @@ b2_heuristic* make_heuristic(b2_task* task)
 
 constexpr unsigned kHmaxThreads = 128;
 
-void launch_hmax(const b2_heuristic& H, const u64* rows, u64 stride, const u32* nodes, const u32* n_dev, u64 n_bound,
+void launch_hmax(const b2_heuristic& H, const u64* rows, u64 stride, const u32* nodes, const u64* n_dev, u64 n_bound,
                  u32* out, bool by_node, u8* flags, int sms, cudaStream_t s)
 {
     HmaxArgs a = H.args;
@@ -457,16 +511,18 @@ struct b2_astar
     cudaStream_t stream = nullptr;
     bool own_stream = false;
     u32 W = 1;
-    // per candidate (state ids are candidate indices: every generated successor has one)
-    DeviceBuffer rows, hash, best, hval, flags, stamp, par, kid;
-    u64 cap_cand = 0, cand_next = 0;
+    // per state
+    DeviceBuffer rows, hash, best, hval, flags, stamp;
+    u64 cap_states = 0, n_states = 0;
     DeviceBuffer table;
     u64 table_slots = 0;
-    u64 n_states = 0;
-    // per wave
-    DeviceBuffer counts, cand_base, iota, staging, touched, fresh, front, next, sums;
-    u64 cap_front = 0, cap_wave = 0, cap_iota = 0;
-    DeviceBuffer open, keep;
+    // per wave: frontier-sized and candidate-sized scratch
+    DeviceBuffer counts, cand_base, iota, sums;
+    u64 cap_front = 0, cap_iota = 0;
+    DeviceBuffer staging, best_rec, slot_of, claimed, touched, fresh;
+    u64 cap_wave = 0;
+    DeviceBuffer front, next;  // state lists (swapped between waves)
+    DeviceBuffer open, keep;   // open entries (f << 32 | state)
     u64 cap_open = 0;
     DeviceBuffer misc;
     AstarMisc* misc_host = nullptr;
@@ -480,12 +536,14 @@ struct b2_astar
 
 namespace
 {
-void ensure_cand(b2_astar& A, u64 need)
+u64 grow_to(u64 need, u64 cap) { return std::max<u64>(need, cap * 2); }
+
+void ensure_states(b2_astar& A, u64 need)
 {
-    if (need <= A.cap_cand)
+    if (need <= A.cap_states)
         return;
-    const u64 cap = std::max<u64>(need, A.cap_cand + A.cap_cand / 2);
-    const u64 used = A.cand_next;
+    const u64 cap = grow_to(need, A.cap_states);
+    const u64 used = A.n_states;
     cudaStream_t s = A.stream;
     A.rows.grow(cap * A.W * 8, used * A.W * 8, s);
     A.hash.grow(cap * 8, used * 8, s);
@@ -493,9 +551,7 @@ void ensure_cand(b2_astar& A, u64 need)
     A.hval.grow(cap * 4, used * 4, s);
     A.flags.grow(cap, used, s);
     A.stamp.grow(cap * 4, used * 4, s);
-    A.par.grow(cap * 4, used * 4, s);
-    A.kid.grow(cap * 4, used * 4, s);
-    A.cap_cand = cap;
+    A.cap_states = cap;
 }
 
 void rehash(b2_astar& A, u64 slots)
@@ -517,10 +573,7 @@ void rehash(b2_astar& A, u64 slots)
         ++A.launches;
     }
 }
-}  // namespace
 
-namespace
-{
 void ensure_table(b2_astar& A, u64 bound)
 {
     if (bound * 4 <= A.table_slots * 3)
@@ -531,46 +584,51 @@ void ensure_table(b2_astar& A, u64 bound)
     rehash(A, slots);
 }
 
-void ensure_wave(b2_astar& A, u64 nF)
+void ensure_front(b2_astar& A, u64 nF)
 {
     cudaStream_t s = A.stream;
     if (nF > A.cap_front)
     {
-        const u64 cap = std::max<u64>(nF, A.cap_front * 2);
+        const u64 cap = grow_to(nF, A.cap_front);
         A.counts.alloc(cap * 4, s);
         A.cand_base.alloc((cap + 1) * 8, s);
         A.cap_front = cap;
     }
     if (nF > A.cap_iota)
     {
-        const u64 cap = std::max<u64>(nF, A.cap_iota * 2);
+        const u64 cap = grow_to(nF, A.cap_iota);
         A.iota.alloc(cap * 4, s);
         k_iota<<<grid_for(cap, 256), 256, 0, s>>>(A.iota.as<u32>(), cap);
         B2_CUDA(cudaGetLastError());
         ++A.launches;
         A.cap_iota = cap;
     }
-    if (A.sums.bytes < scan_scratch_bytes(nF))
-        A.sums.alloc(scan_scratch_bytes(std::max<u64>(nF, 1) * 2), s);
+    if (A.front.bytes < nF * 4)
+        A.front.grow(grow_to(nF, A.front.bytes / 4) * 4, A.front.bytes, s);
 }
 
-/// Buffers of a wave of G candidates: staging, touched / fresh / next lists, and room for G more open entries.
-void ensure_candidates(b2_astar& A, u64 G, u64 nopen)
+/// Scratch of a wave of G candidates, and room for G more open entries and next-wave states.
+void ensure_wave(b2_astar& A, u64 G, u64 nopen)
 {
     cudaStream_t s = A.stream;
     if (G > A.cap_wave)
     {
-        const u64 cap = std::max<u64>(G, A.cap_wave * 2);
+        const u64 cap = grow_to(G, A.cap_wave);
         A.staging.alloc(cap * (A.W + 2) * 8, s);
+        A.best_rec.alloc(cap * 8, s);
+        A.slot_of.alloc(cap * 8, s);
+        A.claimed.alloc(cap, s);
         A.touched.alloc(cap * 4, s);
         A.fresh.alloc(cap * 4, s);
         A.cap_wave = cap;
     }
     if (A.next.bytes < G * 4)
-        A.next.alloc(std::max<u64>(G, 1) * 8, s);
+        A.next.alloc(grow_to(G, A.next.bytes / 4) * 4, s);
+    if (A.sums.bytes < scan_scratch_bytes(std::max(G, A.cap_front)))
+        A.sums.alloc(scan_scratch_bytes(grow_to(std::max(G, A.cap_front), 0)), s);
     if (nopen + G > A.cap_open)
     {
-        const u64 cap = std::max<u64>(nopen + G, A.cap_open * 2);
+        const u64 cap = grow_to(nopen + G, A.cap_open);
         A.open.grow(cap * 8, nopen * 8, s);
         A.keep.alloc(cap * 8, s);
         A.cap_open = cap;
@@ -583,6 +641,8 @@ const AstarMisc& read_misc(b2_astar& A)
     stream_wait(A.stream);
     if (A.misc_host->lm.status & kStatusProbeLimit)
         throw Error(B2_DEVICE_FAULT, "b2_astar: a hash-set probe ran past its bound");
+    if (A.misc_host->lm.status & kStatusCapacity)
+        throw Error(B2_CAPACITY, "b2_astar: a state with 2^16 successors or a path of 2^16 steps");
     if (A.misc_host->lm.status)
         throw Error(B2_DEVICE_FAULT, "b2_astar: device status " + std::to_string(A.misc_host->lm.status));
     return *A.misc_host;
@@ -595,7 +655,7 @@ void run_astar(b2_astar& A, b2_astar_result& R)
     const Program& P = task->prog;
     const DevTask& T = task->dev;
     const u32 pi = A.opt.witness_pruning ? 0 : 1;
-    const u32 W = A.W, RW = W + 2;
+    const u32 W = A.W;
     const unsigned sms = static_cast<unsigned>(task->ctx->sms);
     cudaStream_t s = A.stream;
     cudaEvent_t ev[6];
@@ -618,7 +678,7 @@ void run_astar(b2_astar& A, b2_astar_result& R)
         return;
     }
     const u64 expect = std::max<u64>(A.opt.expected_states, 4096);
-    ensure_cand(A, expect);
+    ensure_states(A, expect);
     A.misc.alloc(sizeof(AstarMisc), s);
     static_assert(sizeof(AstarMisc) <= PinnedPool::kBlock);
     A.misc_host = static_cast<AstarMisc*>(task->ctx->pinned.take());
@@ -629,13 +689,12 @@ void run_astar(b2_astar& A, b2_astar_result& R)
     AstarMisc* misc = A.misc.as<AstarMisc>();
     B2_CUDA(cudaMemcpyAsync(A.rows.p, P.initial.data(), W * 8, cudaMemcpyHostToDevice, s));
     k_astar_seed<<<1, 1, 0, s>>>(A.rows.as<u64>(), A.hash.as<u64>(), W, A.best.as<u64>(), A.flags.as<u8>(),
-                                 A.par.as<u32>(), A.kid.as<u32>(), A.table.as<u64>(), A.table_slots - 1,
-                                 max_probe(A.table_slots), misc);
+                                 A.table.as<u64>(), A.table_slots - 1, max_probe(A.table_slots), misc);
     B2_CUDA(cudaGetLastError());
     ++A.launches;
-    ensure_wave(A, 1);
-    ensure_candidates(A, 1, 0);
-    A.front.alloc(1024 * 4, s);
+    A.n_states = 1;
+    ensure_front(A, std::max<u64>(expect / 8, 1024));
+    ensure_wave(A, std::max<u64>(expect / 2, 1024), 0);
     B2_CUDA(cudaMemsetAsync(A.front.p, 0, 4, s));  // the frontier: the root (state 0)
     launch_hmax(*A.H, A.rows.as<u64>(), W, A.front.as<u32>(), nullptr, 1, A.hval.as<u32>(), true, A.flags.as<u8>(),
                 static_cast<int>(sms), s);
@@ -645,8 +704,6 @@ void run_astar(b2_astar& A, b2_astar_result& R)
     B2_CUDA(cudaMemcpyAsync(&h0, A.hval.p, 4, cudaMemcpyDeviceToHost, s));
     B2_CUDA(cudaMemcpyAsync(&f0, A.flags.p, 1, cudaMemcpyDeviceToHost, s));
     stream_wait(s);
-    A.cand_next = 1;
-    A.n_states = 1;
     R.evaluations = 1;
     R.initial_h = h0 == kDeadEnd ? -1.0 : static_cast<double>(h0);
     const bool dead_start = h0 == kDeadEnd && !(f0 & kGoal);
@@ -667,7 +724,7 @@ void run_astar(b2_astar& A, b2_astar_result& R)
         if (A.opt.max_expansions && expanded >= A.opt.max_expansions)
             break;
         ++wave;
-        ensure_wave(A, nF);
+        ensure_front(A, nF);
         // per-wave counters (the open-list count and the best goal persist)
         B2_CUDA(cudaMemsetAsync(misc, 0, offsetof(AstarMisc, nopen), s));
         const unsigned grid = grid_for(nF, 128, sms * 64);
@@ -690,6 +747,8 @@ void run_astar(b2_astar& A, b2_astar_result& R)
                 k_count<OW, WR><<<grid, 128, 0, s>>>(T, pi, A.rows.as<u64>(), W, A.front.as<u32>(), nF,
                                                      A.counts.as<u32>(), &misc->lm);
             });
+        if (A.sums.bytes < scan_scratch_bytes(nF))
+            A.sums.alloc(scan_scratch_bytes(grow_to(nF, 0)), s);
         device_scan(CountIn{A.counts.as<u32>()}, BaseOut{A.cand_base.as<u64>()}, nF, &misc->lm.total_cand,
                     A.sums.as<u64>(), s);
         A.launches += 4;
@@ -698,14 +757,15 @@ void run_astar(b2_astar& A, b2_astar_result& R)
         const u64 G = read_misc(A).lm.total_cand;
         if (G > 0)
         {
-            if (A.cand_next + G >= (u64{1} << 32) - 1)
-                throw Error(B2_CAPACITY, "b2_astar: more than 2^32 - 2 generated states");
-            ensure_cand(A, A.cand_next + G);
-            ensure_candidates(A, G, nopen);
+            if (A.n_states + G >= kWaveBit)
+                throw Error(B2_CAPACITY, "b2_astar: more than 2^31 states");
+            ensure_wave(A, G, nopen);
+            ensure_states(A, A.n_states + G);
             ensure_table(A, A.n_states + G);
-            B2_CUDA(cudaMemsetAsync(A.best.as<u64>() + A.cand_next, 0xFF, G * 8, s));
-            B2_CUDA(cudaMemsetAsync(A.flags.as<u8>() + A.cand_next, 0, G, s));
-            B2_CUDA(cudaMemsetAsync(A.stamp.as<u32>() + A.cand_next, 0, G * 4, s));
+            B2_CUDA(cudaMemsetAsync(A.best_rec.p, 0xFF, G * 8, s));
+            B2_CUDA(cudaMemsetAsync(A.claimed.p, 0, G, s));
+            if (A.opt.timings)
+                B2_CUDA(cudaEventRecord(ev[2], s));
             dev::DExpandArgs a{};
             a.rows = A.rows.as<u64>();
             a.frontier = A.front.as<u32>();
@@ -724,32 +784,32 @@ void run_astar(b2_astar& A, b2_astar_result& R)
                 jit_launch(task->jit->dbrfs_expand[pi], grid, 128, &a, s);
             else
                 dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() { k_dexpand<OW, WR><<<grid, 128, 0, s>>>(T, a); });
-            if (A.opt.timings)
-                B2_CUDA(cudaEventRecord(ev[2], s));
             InsertArgs in{};
             in.staging = A.staging.as<u64>();
             in.G = G;
             in.W = W;
             in.wave = wave;
-            in.cand_begin = A.cand_next;
             in.frontier = A.front.as<u32>();
             in.cand_base = A.cand_base.as<u64>();
             in.nF = nF;
             in.rows = A.rows.as<u64>();
-            in.hash = A.hash.as<u64>();
             in.best = A.best.as<u64>();
             in.flags = A.flags.as<u8>();
             in.stamp = A.stamp.as<u32>();
-            in.par = A.par.as<u32>();
-            in.kid = A.kid.as<u32>();
             in.table = A.table.as<u64>();
             in.mask = A.table_slots - 1;
             in.max_probe = max_probe(A.table_slots);
+            in.best_rec = A.best_rec.as<u64>();
+            in.slot_of = A.slot_of.as<u64>();
+            in.claimed = A.claimed.as<u8>();
             in.touched = A.touched.as<u32>();
-            in.fresh = A.fresh.as<u32>();
             in.misc = misc;
             k_astar_insert<<<grid_for(G, 256, sms * 16), 256, 0, s>>>(in);
             B2_CUDA(cudaGetLastError());
+            ClaimOut co{A.staging.as<u64>(), W, wave, A.n_states, A.best_rec.as<u64>(), A.slot_of.as<u64>(),
+                        A.table.as<u64>(), A.rows.as<u64>(), A.hash.as<u64>(), A.best.as<u64>(), A.flags.as<u8>(),
+                        A.stamp.as<u32>(), A.fresh.as<u32>(), A.touched.as<u32>(), misc};
+            device_scan(ClaimIn{A.claimed.as<u8>()}, co, G, &misc->nfresh, A.sums.as<u64>(), s);
             if (A.opt.timings)
                 B2_CUDA(cudaEventRecord(ev[3], s));
             launch_hmax(*A.H, A.rows.as<u64>(), W, A.fresh.as<u32>(), &misc->nfresh, G, A.hval.as<u32>(), true,
@@ -761,7 +821,7 @@ void run_astar(b2_astar& A, b2_astar_result& R)
                                                                       static_cast<u32>(fcur), A.next.as<u32>(),
                                                                       A.open.as<u64>());
             B2_CUDA(cudaGetLastError());
-            A.launches += 4;
+            A.launches += 7;
             if (A.opt.timings)
                 B2_CUDA(cudaEventRecord(ev[5], s));
         }
@@ -770,19 +830,18 @@ void run_astar(b2_astar& A, b2_astar_result& R)
         {
             float a = 0, b = 0, c = 0, d = 0;
             B2_CUDA(cudaEventElapsedTime(&a, ev[0], ev[1]));
-            B2_CUDA(cudaEventElapsedTime(&b, ev[1], ev[2]));
-            B2_CUDA(cudaEventElapsedTime(&c, ev[2], ev[3]));
-            B2_CUDA(cudaEventElapsedTime(&d, ev[3], ev[5]));
+            B2_CUDA(cudaEventElapsedTime(&b, ev[2], ev[3]));
+            B2_CUDA(cudaEventElapsedTime(&c, ev[3], ev[4]));
+            B2_CUDA(cudaEventElapsedTime(&d, ev[4], ev[5]));
             count_ms += a;
-            expand_ms += b;
-            insert_ms += c;
-            eval_ms += d;
+            expand_ms += b;  // staging + insert + ids
+            eval_ms += c;
+            insert_ms += d;  // push
         }
         expanded += nF;
         generated += G;
         fresh_total += m.nfresh;
         dead += m.ndead;
-        A.cand_next += G;
         A.n_states += m.nfresh;
         nopen = m.nopen;
         if (m.best_goal != ~u64{0} && (m.best_goal >> 32) <= fcur)
@@ -824,8 +883,7 @@ void run_astar(b2_astar& A, b2_astar_result& R)
         }
         fcur = fmin;
         ++f_layers;
-        if (A.front.bytes < nopen * 4)
-            A.front.alloc(nopen * 8, s);
+        ensure_front(A, nopen);
         B2_CUDA(cudaMemsetAsync(&misc->nkeep, 0, 16, s));
         k_astar_extract<<<grid_for(nopen, 256, sms * 16), 256, 0, s>>>(A.open.as<u64>(), nopen, A.best.as<u64>(),
                                                                          A.hval.as<u32>(), A.flags.as<u8>(), fmin,
@@ -988,8 +1046,7 @@ b2_status b2_astar_plan(b2_astar* A, uint32_t* parent, uint32_t* index, uint32_t
         DeviceBuffer tmp;
         tmp.alloc((2 * static_cast<u64>(n) + 1) * 4);
         u32* tp = tmp.as<u32>();
-        k_astar_path<<<1, 1, 0, A->stream>>>(A->best.as<u64>(), A->par.as<u32>(), A->kid.as<u32>(), A->goal_state, n,
-                                            tp, tp + n, tp + 2 * n);
+        k_astar_path<<<1, 1, 0, A->stream>>>(A->best.as<u64>(), A->goal_state, n, tp, tp + n, tp + 2 * n);
         B2_CUDA(cudaGetLastError());
         std::vector<u32> host(2 * static_cast<u64>(n) + 1);
         B2_CUDA(cudaMemcpyAsync(host.data(), tp, host.size() * 4, cudaMemcpyDeviceToHost, A->stream));
@@ -1009,9 +1066,9 @@ void b2_astar_destroy(b2_astar* A)
     if (!A)
         return;
     cudaSetDevice(A->task->ctx->device);
-    for (DeviceBuffer* b : {&A->rows, &A->hash, &A->best, &A->hval, &A->flags, &A->stamp, &A->par, &A->kid,
-                            &A->table, &A->counts, &A->cand_base, &A->iota, &A->staging, &A->touched, &A->fresh,
-                            &A->front, &A->next, &A->sums, &A->open, &A->keep, &A->misc, &A->hist})
+    for (DeviceBuffer* b : {&A->rows, &A->hash, &A->best, &A->hval, &A->flags, &A->stamp, &A->table, &A->counts,
+                            &A->cand_base, &A->iota, &A->sums, &A->staging, &A->best_rec, &A->slot_of, &A->claimed,
+                            &A->touched, &A->fresh, &A->front, &A->next, &A->open, &A->keep, &A->misc, &A->hist})
         b->reset();
     if (A->stream)
     {
