@@ -56,6 +56,7 @@ def parse():
     ap.add_argument("--depth", type=int, default=None,
                     help="BrFS depth at every N (default: 22 + log2(N), weak scaling; profiling runs use a smaller case)")
     ap.add_argument("--quick", action="store_true", help="timed BrFS only: no e2e, CPU baseline or env leg")
+    ap.add_argument("--no-astar", action="store_true", help="skip the A* leg")
     return ap.parse_args()
 
 
@@ -236,6 +237,52 @@ def env_secondary(args, device, world=1, rank=0, pg=None):
             "parallelism": f"env ids sharded over {world} GPUs" if world > 1 else "single"}
 
 
+def astar_secondary(args, device, with_cpu: bool):
+    """A* with h^max on config [5] (logistics, 8 cities x 4 locations, 6 trucks, 2 airplanes, 2 packages): the time
+    to the optimal plan and the expansions/s, on one GPU (device events around each search), next to the reference's
+    CPU A* (search::astar_eager, one thread: it has no thread option) on the same task."""
+    import torch
+
+    from mymyr_b200 import cuda as b2cuda
+    from mymyr_b200 import tasks
+    from mymyr_b200.task import Task
+
+    cfg = (8, 4, 6, 2, 2, 0)
+    text = tasks.logistics(*cfg)
+    t = Task.from_text(text)
+    H = b2cuda.Heuristic(t)
+    stream = torch.cuda.Stream(device)
+    r = b2cuda.astar(t, heuristic=H, stream=stream.cuda_stream)
+    expected = r.states
+    r.close()
+    runs = []
+    for _ in range(3):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        r = b2cuda.astar(t, heuristic=H, stream=stream.cuda_stream, expected_states=expected, timings=True)
+        b.record(stream)
+        stream.synchronize()
+        runs.append((a.elapsed_time(b), r.expanded, r.generated, r.cost, r.stats))
+        r.close()
+    ms = statistics.median(x[0] for x in runs)
+    out = {"metric": "A* expansions/sec (h^max, logistics 8x4 cities/locations, 6 trucks, 2 airplanes, 2 packages)",
+           "value": runs[-1][1] / (ms / 1000.0), "unit": "expansions/s", "ms_per_search": ms,
+           "cost": runs[-1][3], "expanded": runs[-1][1], "generated": runs[-1][2],
+           "phases_ms": {k: runs[-1][4][k] for k in ("count_ms", "expand_ms", "eval_ms")},
+           "note": "each device step expands a whole f layer, so it expands more states than the one-at-a-time "
+                   "reference; the time to the optimal plan compares the two"}
+    if with_cpu:
+        from oracle import ref
+
+        if ref.available():
+            rr = ref.RefTask(text).astar()
+            out["cpu_baseline"] = {"ms_per_search": rr["seconds"] * 1000, "expanded": rr["expanded"],
+                                   "value": rr["expanded"] / rr["seconds"], "unit": "expansions/s", "cores": 1,
+                                   "kind": "reference", "cost": rr["cost"],
+                                   "sample": "one full search (search::astar_eager, h^max, unit costs)"}
+    return out
+
+
 def main():
     args = parse()
     world, rank, local = dist_setup(args)
@@ -353,6 +400,7 @@ def main():
     e2e_value = expanded * args.steps / e2e_s
 
     secondary = None if args.no_secondary else env_secondary(args, device, world, rank, pg)
+    astar_line = None if (args.no_astar or rank != 0) else astar_secondary(args, device, with_cpu=world == 1)
     base = cpu_baseline() if rank == 0 and world == 1 else None
     if rank == 0:
         line = {
@@ -383,6 +431,7 @@ def main():
                                   "rank": statistics.mean(r.stats.dedup_ms for r in results),
                                   "wall": statistics.mean(r.search_s * 1000 for r in results)},
             "secondary": secondary,
+            "astar": astar_line,
         }
         print(json.dumps(line), flush=True)
     if comm is not None:
