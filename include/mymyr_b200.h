@@ -303,6 +303,8 @@ typedef struct b2_astar_options {
     int32_t timings;           /* per-phase device times */
     void* stream;              /* NULL: a stream of its own */
     b2_heuristic* heuristic;   /* an h^max of the same task to share (NULL: the search grounds its own) */
+    uint64_t chunk_candidates; /* successors staged at once: an f layer with more is expanded in chunks (bounded
+                                  memory; 0: 2^26; at least 2^16) */
 } b2_astar_options;
 
 void b2_astar_options_default(b2_astar_options* o);
@@ -321,6 +323,7 @@ typedef struct b2_astar_result {
     uint64_t relaxed_ops, relaxed_atoms;
 } b2_astar_result;
 
+/* The task (and a shared heuristic) must outlive the search object. */
 b2_status b2_astar_create(b2_task* task, const b2_astar_options* options, b2_astar** out);
 b2_status b2_astar_run(b2_astar* search, b2_astar_result* result);
 /* The plan as its states' transitions, root first: step i leaves state parent[i] (a state index of the search) by its

@@ -96,7 +96,8 @@ class HeuristicInfo(C.Structure):
 
 class AstarOptions(C.Structure):
     _fields_ = [("max_expansions", C.c_uint64), ("expected_states", C.c_uint64), ("witness_pruning", C.c_int32),
-                ("timings", C.c_int32), ("stream", C.c_void_p), ("heuristic", C.c_void_p)]
+                ("timings", C.c_int32), ("stream", C.c_void_p), ("heuristic", C.c_void_p),
+                ("chunk_candidates", C.c_uint64)]
 
 
 class AstarResult(C.Structure):

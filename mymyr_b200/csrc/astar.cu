@@ -27,6 +27,7 @@
 #include "brfs.cuh"
 #include "relax.hpp"
 
+#include <array>
 #include <chrono>
 #include <cstddef>
 #include <stdexcept>
@@ -138,21 +139,34 @@ __global__ void k_hmax(HmaxArgs H, const u64* __restrict__ rows, u64 stride, con
     }
 }
 
-/// Per-wave counters of the A* (device side, mirrored to pinned host memory).
+/// Per-wave counters of the A* (device side, mirrored to pinned host memory). The first block (up to nnext) restarts
+/// with every chunk of a wave, nnext with every wave; the rest persists.
 struct AstarMisc
 {
     LayerMisc lm;   // count pass: total candidates of the wave, status
-    u32 ntouched;   // states whose g was set or lowered this wave
+    u32 ntouched;   // states whose g was set or lowered by the chunk
+    u32 ndead;      // dead ends among the chunk's new states
+    u64 nfresh;     // new states of the chunk (the id scan's total)
     u32 nnext;      // states of the next wave (f = current f)
-    u32 ndead;      // dead ends among the wave's new states
     u32 pad;
-    u64 nfresh;     // new states this wave (the id scan's total)
     u64 nopen;      // open entries of later f
     u64 best_goal;  // (g << 32 | state) of the best goal found (~0: none)
     u64 fmin;       // smallest f of a valid open entry (bucket switch)
     u64 nkeep;      // open entries kept by the extraction
     u64 nfront;     // states extracted into the frontier
 };
+
+/// Chunks of a wave whose candidates exceed `chunk`: chunk k starts at the first frontier state whose first
+/// successor's index is in [k * chunk, (k + 1) * chunk) (bounds[k] = that state, ~0 if none).
+__global__ void k_chunk_bounds(const u64* __restrict__ cand_base, u64 nF, u64 chunk, u64* bounds)
+{
+    for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < nF; i += static_cast<u64>(gridDim.x) * blockDim.x)
+    {
+        const u64 k = cand_base[i] / chunk;
+        if (i == 0 || cand_base[i - 1] / chunk != k)
+            bounds[k] = i;
+    }
+}
 
 constexpr u32 kWaveBit = 0x80000000u;
 constexpr u64 kNoParent = 0xFFFFFFFFull;
@@ -164,7 +178,7 @@ struct InsertArgs
     const u64* staging;
     u64 G;
     u32 W;
-    u32 wave;
+    u32 wave;          // the chunk's stamp (unique per chunk): a state is listed touched once per chunk
     const u32* frontier;
     const u64* cand_base;
     u64 nF;
@@ -521,6 +535,7 @@ struct b2_astar
     u64 cap_front = 0, cap_iota = 0;
     DeviceBuffer staging, best_rec, slot_of, claimed, touched, fresh;
     u64 cap_wave = 0;
+    DeviceBuffer bounds;  // chunk starts of a large wave
     DeviceBuffer front, next;  // state lists (swapped between waves)
     DeviceBuffer open, keep;   // open entries (f << 32 | state)
     u64 cap_open = 0;
@@ -622,8 +637,7 @@ void ensure_wave(b2_astar& A, u64 G, u64 nopen)
         A.fresh.alloc(cap * 4, s);
         A.cap_wave = cap;
     }
-    if (A.next.bytes < G * 4)
-        A.next.alloc(grow_to(G, A.next.bytes / 4) * 4, s);
+    (void)0;
     if (A.sums.bytes < scan_scratch_bytes(std::max(G, A.cap_front)))
         A.sums.alloc(scan_scratch_bytes(grow_to(std::max(G, A.cap_front), 0)), s);
     if (nopen + G > A.cap_open)
@@ -678,6 +692,7 @@ void run_astar(b2_astar& A, b2_astar_result& R)
         return;
     }
     const u64 expect = std::max<u64>(A.opt.expected_states, 4096);
+    const u64 chunk = A.opt.chunk_candidates ? std::max<u64>(A.opt.chunk_candidates, u64{1} << 16) : u64{1} << 26;
     ensure_states(A, expect);
     A.misc.alloc(sizeof(AstarMisc), s);
     static_assert(sizeof(AstarMisc) <= PinnedPool::kBlock);
@@ -694,7 +709,7 @@ void run_astar(b2_astar& A, b2_astar_result& R)
     ++A.launches;
     A.n_states = 1;
     ensure_front(A, std::max<u64>(expect / 8, 1024));
-    ensure_wave(A, std::max<u64>(expect / 2, 1024), 0);
+    ensure_wave(A, std::min(std::max<u64>(expect / 2, 1024), chunk), 0);
     B2_CUDA(cudaMemsetAsync(A.front.p, 0, 4, s));  // the frontier: the root (state 0)
     launch_hmax(*A.H, A.rows.as<u64>(), W, A.front.as<u32>(), nullptr, 1, A.hval.as<u32>(), true, A.flags.as<u8>(),
                 static_cast<int>(sms), s);
@@ -716,7 +731,7 @@ void run_astar(b2_astar& A, b2_astar_result& R)
     else if (dead_start)
         R.dead_ends = 1;
     u64 fcur = h0, nF = 1, nopen = 0, expanded = 0, generated = 0, fresh_total = 0, dead = 0;
-    u32 wave = 0, f_layers = 1;
+    u32 wave = 0, f_layers = 1, stamp = 0;
     double count_ms = 0, expand_ms = 0, insert_ms = 0, eval_ms = 0;
     bool exhausted = false;
     while (!A.solved && !dead_start)
@@ -755,43 +770,82 @@ void run_astar(b2_astar& A, b2_astar_result& R)
         if (A.opt.timings)
             B2_CUDA(cudaEventRecord(ev[1], s));
         const u64 G = read_misc(A).lm.total_cand;
-        if (G > 0)
+        // the wave's chunks: [first state, end state, first candidate, end candidate)
+        std::vector<std::array<u64, 4>> chunks;
+        if (G > 0 && G <= chunk)
+            chunks.push_back({0, nF, 0, G});
+        else if (G > 0)
         {
-            if (A.n_states + G >= kWaveBit)
+            const u64 nk = (G + chunk - 1) / chunk;
+            A.bounds.alloc(nk * 8, s);
+            B2_CUDA(cudaMemsetAsync(A.bounds.p, 0xFF, nk * 8, s));
+            k_chunk_bounds<<<grid_for(nF, 256, sms * 16), 256, 0, s>>>(A.cand_base.as<u64>(), nF, chunk,
+                                                                        A.bounds.as<u64>());
+            B2_CUDA(cudaGetLastError());
+            ++A.launches;
+            std::vector<u64> starts(nk);
+            B2_CUDA(cudaMemcpyAsync(starts.data(), A.bounds.p, nk * 8, cudaMemcpyDeviceToHost, s));
+            stream_wait(s);
+            std::vector<u64> first;  // the chunks' first states (ids without one merge into the previous chunk)
+            for (u64 k = 0; k < nk; ++k)
+                if (starts[k] != ~u64{0})
+                    first.push_back(starts[k]);
+            std::vector<u64> cb(first.size());
+            for (u64 k = 0; k < first.size(); ++k)
+                B2_CUDA(cudaMemcpyAsync(&cb[k], A.cand_base.as<u64>() + first[k], 8, cudaMemcpyDeviceToHost, s));
+            stream_wait(s);
+            for (u64 k = 0; k < first.size(); ++k)
+                chunks.push_back({first[k], k + 1 < first.size() ? first[k + 1] : nF, cb[k],
+                                  k + 1 < first.size() ? cb[k + 1] : G});
+        }
+        u64 nnext = 0;
+        for (u64 ci = 0; ci < chunks.size(); ++ci)
+        {
+            ++stamp;  // a state lowered again by a later chunk of the wave must be pushed again
+            const u64 i0 = chunks[ci][0], i1 = chunks[ci][1], c0 = chunks[ci][2], Gc = chunks[ci][3] - c0;
+            if (Gc == 0)
+                continue;
+            if (A.n_states + Gc >= kWaveBit)
                 throw Error(B2_CAPACITY, "b2_astar: more than 2^31 states");
-            ensure_wave(A, G, nopen);
-            ensure_states(A, A.n_states + G);
-            ensure_table(A, A.n_states + G);
-            B2_CUDA(cudaMemsetAsync(A.best_rec.p, 0xFF, G * 8, s));
-            B2_CUDA(cudaMemsetAsync(A.claimed.p, 0, G, s));
+            ensure_wave(A, Gc, nopen);
+            if (A.next.bytes < (nnext + Gc) * 4)
+                A.next.grow(grow_to(nnext + Gc, A.next.bytes / 4) * 4, nnext * 4, s);
+            ensure_states(A, A.n_states + Gc);
+            ensure_table(A, A.n_states + Gc);
+            if (ci > 0)
+                B2_CUDA(cudaMemsetAsync(misc, 0, offsetof(AstarMisc, nnext), s));
+            B2_CUDA(cudaMemsetAsync(A.best_rec.p, 0xFF, Gc * 8, s));
+            B2_CUDA(cudaMemsetAsync(A.claimed.p, 0, Gc, s));
             if (A.opt.timings)
                 B2_CUDA(cudaEventRecord(ev[2], s));
+            const unsigned gridc = grid_for(i1 - i0, 128, sms * 64);
             dev::DExpandArgs a{};
             a.rows = A.rows.as<u64>();
-            a.frontier = A.front.as<u32>();
+            a.frontier = A.front.as<u32>() + i0;
             a.frontier_id = A.iota.as<u32>();
-            a.E = nF;
+            a.E = i1 - i0;
             a.layer_begin = 0;
             a.limit = ~u64{0};
-            a.gbase = A.cand_base.as<u64>();
-            a.local_base = A.cand_base.as<u64>();
+            a.gbase = A.cand_base.as<u64>() + i0;
+            a.local_base = A.cand_base.as<u64>() + i0;
+            a.stage_base = c0;
             a.staging = A.staging.as<u64>();
             a.hist = A.hist.as<u64>();
             a.world = 1;
             a.W = W;
             a.pi = pi;
             if (task->jit)
-                jit_launch(task->jit->dbrfs_expand[pi], grid, 128, &a, s);
+                jit_launch(task->jit->dbrfs_expand[pi], gridc, 128, &a, s);
             else
-                dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() { k_dexpand<OW, WR><<<grid, 128, 0, s>>>(T, a); });
+                dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() { k_dexpand<OW, WR><<<gridc, 128, 0, s>>>(T, a); });
             InsertArgs in{};
             in.staging = A.staging.as<u64>();
-            in.G = G;
+            in.G = Gc;
             in.W = W;
-            in.wave = wave;
-            in.frontier = A.front.as<u32>();
-            in.cand_base = A.cand_base.as<u64>();
-            in.nF = nF;
+            in.wave = stamp;
+            in.frontier = A.front.as<u32>() + i0;
+            in.cand_base = A.cand_base.as<u64>() + i0;
+            in.nF = i1 - i0;
             in.rows = A.rows.as<u64>();
             in.best = A.best.as<u64>();
             in.flags = A.flags.as<u8>();
@@ -804,46 +858,52 @@ void run_astar(b2_astar& A, b2_astar_result& R)
             in.claimed = A.claimed.as<u8>();
             in.touched = A.touched.as<u32>();
             in.misc = misc;
-            k_astar_insert<<<grid_for(G, 256, sms * 16), 256, 0, s>>>(in);
+            k_astar_insert<<<grid_for(Gc, 256, sms * 16), 256, 0, s>>>(in);
             B2_CUDA(cudaGetLastError());
-            ClaimOut co{A.staging.as<u64>(), W, wave, A.n_states, A.best_rec.as<u64>(), A.slot_of.as<u64>(),
+            ClaimOut co{A.staging.as<u64>(), W, stamp, A.n_states, A.best_rec.as<u64>(), A.slot_of.as<u64>(),
                         A.table.as<u64>(), A.rows.as<u64>(), A.hash.as<u64>(), A.best.as<u64>(), A.flags.as<u8>(),
                         A.stamp.as<u32>(), A.fresh.as<u32>(), A.touched.as<u32>(), misc};
-            device_scan(ClaimIn{A.claimed.as<u8>()}, co, G, &misc->nfresh, A.sums.as<u64>(), s);
+            device_scan(ClaimIn{A.claimed.as<u8>()}, co, Gc, &misc->nfresh, A.sums.as<u64>(), s);
             if (A.opt.timings)
                 B2_CUDA(cudaEventRecord(ev[3], s));
-            launch_hmax(*A.H, A.rows.as<u64>(), W, A.fresh.as<u32>(), &misc->nfresh, G, A.hval.as<u32>(), true,
+            launch_hmax(*A.H, A.rows.as<u64>(), W, A.fresh.as<u32>(), &misc->nfresh, Gc, A.hval.as<u32>(), true,
                         A.flags.as<u8>(), static_cast<int>(sms), s);
             if (A.opt.timings)
                 B2_CUDA(cudaEventRecord(ev[4], s));
-            k_astar_push<<<grid_for(G, 256, sms * 16), 256, 0, s>>>(A.touched.as<u32>(), misc, A.best.as<u64>(),
-                                                                      A.hval.as<u32>(), A.flags.as<u8>(),
-                                                                      static_cast<u32>(fcur), A.next.as<u32>(),
-                                                                      A.open.as<u64>());
+            k_astar_push<<<grid_for(Gc, 256, sms * 16), 256, 0, s>>>(A.touched.as<u32>(), misc, A.best.as<u64>(),
+                                                                       A.hval.as<u32>(), A.flags.as<u8>(),
+                                                                       static_cast<u32>(fcur), A.next.as<u32>(),
+                                                                       A.open.as<u64>());
             B2_CUDA(cudaGetLastError());
             A.launches += 7;
             if (A.opt.timings)
                 B2_CUDA(cudaEventRecord(ev[5], s));
+            const AstarMisc mc = read_misc(A);
+            if (A.opt.timings)
+            {
+                float x = 0, y = 0, z = 0;
+                B2_CUDA(cudaEventElapsedTime(&x, ev[2], ev[3]));
+                B2_CUDA(cudaEventElapsedTime(&y, ev[3], ev[4]));
+                B2_CUDA(cudaEventElapsedTime(&z, ev[4], ev[5]));
+                expand_ms += x;  // staging + insert + ids
+                eval_ms += y;
+                insert_ms += z;  // push
+            }
+            fresh_total += mc.nfresh;
+            dead += mc.ndead;
+            A.n_states += mc.nfresh;
+            nopen = mc.nopen;
+            nnext = mc.nnext;
         }
-        const AstarMisc m = read_misc(A);
-        if (A.opt.timings && G > 0)
+        if (A.opt.timings)
         {
-            float a = 0, b = 0, c = 0, d = 0;
-            B2_CUDA(cudaEventElapsedTime(&a, ev[0], ev[1]));
-            B2_CUDA(cudaEventElapsedTime(&b, ev[2], ev[3]));
-            B2_CUDA(cudaEventElapsedTime(&c, ev[3], ev[4]));
-            B2_CUDA(cudaEventElapsedTime(&d, ev[4], ev[5]));
-            count_ms += a;
-            expand_ms += b;  // staging + insert + ids
-            eval_ms += c;
-            insert_ms += d;  // push
+            float x = 0;
+            B2_CUDA(cudaEventElapsedTime(&x, ev[0], ev[1]));
+            count_ms += x;
         }
+        const AstarMisc m = *A.misc_host;  // as of the last chunk (or the count pass of a wave without successors)
         expanded += nF;
         generated += G;
-        fresh_total += m.nfresh;
-        dead += m.ndead;
-        A.n_states += m.nfresh;
-        nopen = m.nopen;
         if (m.best_goal != ~u64{0} && (m.best_goal >> 32) <= fcur)
         {
             A.solved = true;
@@ -851,10 +911,10 @@ void run_astar(b2_astar& A, b2_astar_result& R)
             A.goal_state = static_cast<u32>(m.best_goal);
             break;
         }
-        if (m.nnext > 0)
+        if (nnext > 0)
         {
             A.front.swap(A.next);
-            nF = m.nnext;
+            nF = nnext;
             continue;
         }
         // the current f is done: the smallest f of the open list is next
@@ -1068,7 +1128,7 @@ void b2_astar_destroy(b2_astar* A)
     cudaSetDevice(A->task->ctx->device);
     for (DeviceBuffer* b : {&A->rows, &A->hash, &A->best, &A->hval, &A->flags, &A->stamp, &A->table, &A->counts,
                             &A->cand_base, &A->iota, &A->sums, &A->staging, &A->best_rec, &A->slot_of, &A->claimed,
-                            &A->touched, &A->fresh, &A->front, &A->next, &A->open, &A->keep, &A->misc, &A->hist})
+                            &A->touched, &A->fresh, &A->front, &A->next, &A->open, &A->keep, &A->misc, &A->hist, &A->bounds})
         b->reset();
     if (A->stream)
     {

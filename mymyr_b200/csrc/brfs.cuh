@@ -57,7 +57,7 @@ __global__ void __launch_bounds__(128) k_dexpand(DevTask T, dev::DExpandArgs a)
             continue;
         const auto st = load_row<WR>(a.rows + static_cast<u64>(a.frontier[i]) * W, W);
         const u64 c0 = a.gbase[id - a.layer_begin];
-        u64* out = a.staging + a.local_base[i] * (W + 2);
+        u64* out = a.staging + (a.local_base[i] - a.stage_base) * (W + 2);
         u32 k = 0;
         u32 bind[kMaxLevels] = {};
         for (u32 s = 0; s < T.nschemas; ++s)

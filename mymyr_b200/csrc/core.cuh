@@ -363,7 +363,8 @@ struct DExpandArgs
     u64 layer_begin;         // id of the layer's first state
     u64 limit;               // expand the parents with id < limit
     const u64* gbase;        // [layer states] candidate offset of each parent of the layer (all ranks)
-    const u64* local_base;   // [E] staging record of each local parent's first successor
+    const u64* local_base;   // [E] staging record of each local parent's first successor (minus stage_base)
+    u64 stage_base;          // subtracted from local_base (a chunk of a larger batch stages from 0)
     u64* staging;            // [local candidates, W + 2]
     u64* hist;               // [world] staged records per owner rank
     u32 world;

@@ -132,7 +132,7 @@ B2_DI void dbrfs_expand(const DExpandArgs& a)
             continue;
         const Row st = RowSel<WR>::load(a.rows + static_cast<u64>(a.frontier[i]) * W);
         const u64 c0 = a.gbase[id - a.layer_begin];
-        u64* out = a.staging + a.local_base[i] * (W + 2);
+        u64* out = a.staging + (a.local_base[i] - a.stage_base) * (W + 2);
         u32 k = 0;
         for_each_schema([&]<int S>() {
             Run<S, PI>::go(st, [&](const u32* b) {

@@ -269,6 +269,7 @@ class AstarResult:
     search_s: float
     stats: dict = field(default_factory=dict)
     _search: object = None
+    _owners: tuple = ()  # the task (and shared heuristic) the search reads until it is closed
 
     @property
     def solved(self) -> bool:
@@ -305,6 +306,7 @@ class AstarResult:
         if self._search is not None and _lib._lib is not None:
             _lib._lib.b2_astar_destroy(self._search)
         self._search = None
+        self._owners = ()
 
     def __del__(self):
         self.close()
@@ -312,9 +314,10 @@ class AstarResult:
 
 def astar(task: Task, ctx: Context | None = None, heuristic="max", *, witness_pruning: bool = False,
           max_expansions: int | None = None, expected_states: int | None = None, timings: bool = False,
-          stream=None) -> AstarResult:
+          stream=None, chunk_candidates: int | None = None) -> AstarResult:
     """Eager A* with h^max and unit costs on the device (mymyr.cuda.astar / search::astar_eager): the optimal plan
-    cost. ``heuristic`` is "max" or a ``Heuristic`` of the same task (to share its grounding)."""
+    cost. ``heuristic`` is "max" or a ``Heuristic`` of the same task (to share its grounding). ``chunk_candidates``
+    bounds the successors staged at once (an f layer with more is expanded in chunks; default 2^26)."""
     if ctx is not None and task.ctx is not None and ctx.device != task.ctx.device:
         raise ValueError("mymyr_b200 astar: the task lives on another device than ctx")
     o = _lib.AstarOptions()
@@ -327,6 +330,8 @@ def astar(task: Task, ctx: Context | None = None, heuristic="max", *, witness_pr
         o.expected_states = int(expected_states)
     if stream is not None:
         o.stream = stream
+    if chunk_candidates is not None:
+        o.chunk_candidates = int(chunk_candidates)
     if isinstance(heuristic, Heuristic):
         o.heuristic = heuristic.handle
     elif heuristic != "max":
@@ -344,4 +349,4 @@ def astar(task: Task, ctx: Context | None = None, heuristic="max", *, witness_pr
     return AstarResult(status=ASTAR_STATUS.get(r.status, str(r.status)), cost=r.cost, plan_length=r.plan_length,
                        expanded=r.expanded, generated=r.generated, states=r.states, evaluations=r.evaluations,
                        dead_ends=r.dead_ends, initial_h=r.initial_h, waves=r.waves, f_layers=r.f_layers,
-                       search_s=r.search_s, stats=stats, _search=h)
+                       search_s=r.search_s, stats=stats, _search=h, _owners=(task, heuristic))

@@ -78,7 +78,47 @@ def test_astar_config5(ref):
     text = tasks.logistics(8, 4, 6, 2, 2, 0)
     t = Task.from_text(text)
     r = b2cuda.astar(t, timings=True)
-    assert r.solved and r.cost == 14  # the reference's optimal cost (astar_eager, h^max)
+    assert r.solved and r.cost == _golden_costs()[(8, 4, 6, 2, 2, 0)]  # the reference's optimal cost
+    _check_plan(ref.RefTask(text), t, r)
+    r.close()
+
+
+def _golden_costs():
+    from pathlib import Path
+
+    out = {}
+    for line in (Path(__file__).parent / "golden" / "astar_costs.txt").read_text().splitlines():
+        if line.startswith("#"):
+            continue
+        cfg, rest = line.split("|")
+        out[tuple(int(x) for x in cfg.split())] = int(rest.split()[0])
+    return out
+
+
+def test_astar_chunked_waves(ref):
+    """Waves split into chunks of 2^16 successors (bounded memory) find the same optimal cost, a valid plan, and
+    expand and store exactly the states of the unchunked search; repeated runs agree (no order dependence)."""
+    cfg = (8, 4, 6, 2, 2, 0)
+    text = tasks.logistics(*cfg)
+    t = Task.from_text(text)
+    runs = []
+    for chunk in (1 << 16, None, None):
+        r = b2cuda.astar(t, chunk_candidates=chunk)
+        assert r.solved and r.cost == _golden_costs()[cfg]
+        _check_plan(ref.RefTask(text), t, r)
+        runs.append((r.expanded, r.generated, r.states, r.waves))
+        r.close()
+    assert runs[0] == runs[1] == runs[2], runs
+
+
+@pytest.mark.slow
+def test_astar_config5_three_packages(ref):
+    """3 packages: the reference's CPU A* needs about 13 minutes (golden cost from tests/golden/astar_costs.txt)."""
+    cfg = (8, 4, 6, 2, 3, 0)
+    text = tasks.logistics(*cfg)
+    t = Task.from_text(text)
+    r = b2cuda.astar(t)
+    assert r.solved and r.cost == _golden_costs()[cfg]
     _check_plan(ref.RefTask(text), t, r)
     r.close()
 
