@@ -57,6 +57,8 @@ def parse():
                     help="BrFS depth at every N (default: 22 + log2(N), weak scaling; profiling runs use a smaller case)")
     ap.add_argument("--quick", action="store_true", help="timed BrFS only: no e2e, CPU baseline or env leg")
     ap.add_argument("--no-astar", action="store_true", help="skip the A* leg")
+    ap.add_argument("--leg", choices=["all", "astar", "env"], default="all",
+                    help="run one leg alone and print its JSON (profiling runs)")
     return ap.parse_args()
 
 
@@ -301,6 +303,14 @@ def main():
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
         pg = dist
+    if args.leg != "all":
+        out = astar_secondary(args, device, with_cpu=False) if args.leg == "astar" else \
+            env_secondary(args, device, world, rank, pg)
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+        if pg is not None:
+            pg.destroy_process_group()
+        return
     from mymyr_b200 import cuda as b2cuda
     from mymyr_b200 import tasks
     from mymyr_b200.task import Context, Task

@@ -95,9 +95,89 @@ B2_DI void brfs_count(const BrfsArgs& a)
     }
 }
 
+/// A successor waiting in a warp's queue for its insert.
+struct QEntry
+{
+    u64 w[W];
+    u64 h;
+    u64 g;
+    u32 i, k;
+};
+/// Queue entries per warp: about 25 KB per 128-thread block.
+constexpr u32 kQueue = W <= 4 ? 112u : W <= 6 ? 96u : 80u;
+
+/// The expansion with warp-cooperative inserts (rows in registers): each lane runs its parent's matcher and queues
+/// every successor (row, hash, candidate index) in shared memory; after the round all 32 lanes insert the queued
+/// successors together, so the insert runs on full warps instead of the few lanes whose matcher emitted. A successor
+/// that finds the queue full is inserted in place. Same inserts, same protocol: only which thread issues them changes.
+template<int PI>
+B2_DI void brfs_expand_queued(const BrfsArgs& a)
+{
+    __shared__ QEntry q[4][kQueue];  // blockDim.x = 128: four warps
+    __shared__ u32 qn[4];
+    const u32 wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0)
+        qn[wid] = 0;
+    __syncwarp();
+    const u64 stride = static_cast<u64>(gridDim.x) * blockDim.x;
+    for (u64 base = blockIdx.x * static_cast<u64>(blockDim.x) + wid * 32; base < a.E; base += stride)
+    {
+        const u64 i = base + lane;
+        if (i < a.E)
+        {
+            const u64 pg = a.frontier[i];
+            const Row st = RowSel<WR>::load(a.S.rows + pg * W);
+            const u64 g0 = a.S.layer_cand_begin + a.cand_base[i];
+            u32 k = 0;
+            for_each_schema([&]<int S>() {
+                Run<S, PI>::go(st, [&](const u32* b) {
+                    with_successor<S>(st, b, [&](const auto& nx, u64 h) {
+                        const u32 s = atomicAdd(&qn[wid], 1u);
+                        if (s < kQueue)
+                        {
+                            QEntry& e = q[wid][s];
+#pragma unroll
+                            for (u32 x = 0; x < W; ++x)
+                                e.w[x] = nx.word(x);
+                            e.h = h;
+                            e.g = g0 + k;
+                            e.i = static_cast<u32>(i);
+                            e.k = k;
+                        }
+                        else
+                            insert<static_cast<int>(W)>(a.S, nx, h, g0 + k, static_cast<u32>(i), k);
+                    });
+                    ++k;
+                    return true;
+                });
+            });
+        }
+        __syncwarp();
+        const u32 n = min(qn[wid], kQueue);
+        for (u32 s = lane; s < n; s += 32)
+        {
+            const QEntry& e = q[wid][s];
+            Row r;
+#pragma unroll
+            for (int x = 0; x < WR; ++x)
+                r.w[x] = static_cast<u32>(x) < W ? e.w[x < static_cast<int>(W) ? x : 0] : 0;
+            insert<static_cast<int>(W)>(a.S, r, e.h, e.g, e.i, e.k);
+        }
+        __syncwarp();
+        if (lane == 0)
+            qn[wid] = 0;
+        __syncwarp();
+    }
+}
+
 template<int PI>
 B2_DI void brfs_expand(const BrfsArgs& a)
 {
+    if constexpr (WR > 0)
+    {
+        brfs_expand_queued<PI>(a);
+        return;
+    }
     for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < a.E; i += static_cast<u64>(gridDim.x) * blockDim.x)
     {
         const u64 pg = a.frontier[i];
