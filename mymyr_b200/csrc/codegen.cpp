@@ -142,6 +142,45 @@ struct Gen
                 o << "        }\n";
             }
         }
+        else if (f.step <= 32 && 64 % f.step == 0)
+        {
+            // a strided run word by word: the run's bits in a word are those congruent to s_ modulo the step
+            u64 rep = 0;
+            for (u32 b = 0; b < 64; b += static_cast<u32>(f.step))
+                rep |= u64{1} << b;
+            const u64 span = static_cast<u64>(f.count - 1) * f.step;
+            o << "        const u64 e_ = s_ + " << span << "ull;\n"
+              << "        const u64 rep_ = " << hex(rep) << " << (s_ % " << f.step << "u);\n";
+            auto body = [&](const std::string& w, const std::string& wv) {
+                o << "          u64 m_ = " << wv << " & rep_;\n"
+                  << "          if ((s_ >> 6) == " << w << ") m_ &= ~0ull << (s_ & 63);\n"
+                  << "          if ((e_ >> 6) == " << w << ") m_ &= (e_ & 63) == 63 ? ~0ull : ((2ull << (e_ & 63)) - 1);\n"
+                  << "          while (m_) { const u32 bt_ = __ffsll(static_cast<long long>(m_)) - 1; m_ &= m_ - 1;\n"
+                  << "            const u32 r_ = static_cast<u32>((64ull * " << w << " + bt_ - s_) / " << f.step
+                  << "u);\n";
+                if (f.map_lo != kNone)
+                    o << "            const u32 ob_ = " << f.map_lo << "u + r_;\n";
+                else
+                    o << "            const u32 ob_ = DOM[" << P.pos_dom_begin[f.map_pos] << "u + r_];\n";
+                set_runtime("ob_");
+                o << "          }\n";
+            };
+            if (P.words <= 8)
+                for (u32 w = 0; w < P.words; ++w)
+                {
+                    const std::string ws = std::to_string(w) + "u";
+                    o << "        if ((s_ >> 6) <= " << ws << " && (e_ >> 6) >= " << ws << ") {\n";
+                    body(ws, "st.word(" + ws + ")");
+                    o << "        }\n";
+                }
+            else
+            {
+                o << "        for (u32 w_ = static_cast<u32>(s_ >> 6); w_ <= static_cast<u32>(e_ >> 6) && w_ < "
+                  << P.words << "u; ++w_) {\n";
+                body("w_", "st.word(w_)");
+                o << "        }\n";
+            }
+        }
         else
         {
             o << "        for (u32 r_ = 0; r_ < " << f.count << "u; ++r_)\n"
@@ -158,6 +197,11 @@ struct Gen
             o << "      " << c << k << " &= " << (f.neg ? "~" : "") << "x" << k << ";\n";
         o << "    }\n";
     }
+
+    /// Leaf of a buffered (selectivity-ordered) matcher: the binding's canonical key (8 bits per parameter, the first
+    /// parameter highest) into the buffer; a full buffer hands the state to the index-order matcher.
+    std::string canon;  // the index-order matcher of the schema being generated, for the fallback
+    u32 buffer_arity = 0;
 
     void level(const DProgram& pg, u32 d, u32 arity)
     {
@@ -180,7 +224,15 @@ struct Gen
         o << "      b[" << L.param << "] = o" << D << ";\n";
         for (u32 c = L.chk_begin; c < L.chk_end; ++c)
             o << "      if (!" << holds_expr(P.lits[P.checks[c]]) << ") continue;\n";
-        if (d + 1 == pg.nlevels)
+        if (d + 1 == pg.nlevels && buffer_arity)
+        {
+            o << "      {\n        u64 key_ = 0;\n";
+            for (u32 v = 0; v < buffer_arity; ++v)
+                o << "        key_ |= static_cast<u64>(b[" << v << "]) << " << 8 * (buffer_arity - 1 - v) << ";\n";
+            o << "        if (nb_ == 16u) return " << canon << "::go(st, emit);\n"
+              << "        buf_[nb_++] = key_;\n      }\n";
+        }
+        else if (d + 1 == pg.nlevels)
         {
             o << "      if (!emit(static_cast<const u32*>(b))) return false;\n";
             if (pg.first_exist < pg.nlevels)
@@ -197,11 +249,11 @@ struct Gen
         o << "    }\n  }\n";
     }
 
-    void run(u32 s, u32 pi)
+    /// One matcher struct `name` over program pg: index order emits as it goes; a buffered one (buffer_arity set)
+    /// collects up to 16 bindings, sorts their keys and emits them in canonical order.
+    void run_struct(const std::string& name, const DSchema& S, const DProgram& pg)
     {
-        const DSchema& S = P.schemas[s];
-        const DProgram& pg = S.prog[pi];
-        o << "template<> struct Run<" << s << ", " << pi << "> {\n"
+        o << "template<> struct " << name << " {\n"
           << "template<class St, class E> B2_DI static bool go(const St& st, E&& emit) {\n"
           << "  (void)st;\n  u32 b[" << (S.arity ? S.arity : 1) << "] = {};\n";
         if (pg.never)
@@ -209,6 +261,8 @@ struct Gen
             o << "  return true;\n}\n};\n";
             return;
         }
+        if (buffer_arity)
+            o << "  u64 buf_[16];\n  u32 nb_ = 0;\n";
         for (u32 c = pg.pre_begin; c < pg.pre_end; ++c)
             o << "  if (!" << holds_expr(P.lits[P.checks[c]]) << ") return true;\n";
         if (pg.nlevels == 0)
@@ -217,9 +271,40 @@ struct Gen
         {
             // a witness exit jumps to the end of the last effect-relevant level's loop body
             level(pg, 0, S.arity);
+            if (buffer_arity)
+            {
+                o << "  for (u32 i_ = 1; i_ < nb_; ++i_) {\n"
+                  << "    const u64 x_ = buf_[i_];\n    u32 j_ = i_;\n"
+                  << "    while (j_ > 0 && buf_[j_ - 1] > x_) { buf_[j_] = buf_[j_ - 1]; --j_; }\n"
+                  << "    buf_[j_] = x_;\n  }\n"
+                  << "  for (u32 i_ = 0; i_ < nb_; ++i_) {\n    const u64 k_ = buf_[i_];\n";
+                for (u32 v = 0; v < buffer_arity; ++v)
+                    o << "    b[" << v << "] = static_cast<u32>((k_ >> " << 8 * (buffer_arity - 1 - v) << ") & 0xffu);\n";
+                o << "    if (!emit(static_cast<const u32*>(b))) return false;\n  }\n";
+            }
             o << "  return true;\n";
         }
         o << "}\n};\n";
+    }
+
+    void run(u32 s, u32 pi)
+    {
+        const DSchema& S = P.schemas[s];
+        const DProgram& pg = S.prog[pi];
+        const std::string name = "Run<" + std::to_string(s) + ", " + std::to_string(pi) + ">";
+        // the selectivity order applies when the program binds every parameter (witness pruning without
+        // witness-only parameters binds them all too)
+        const bool fast = S.fast_on && !pg.never && pg.first_exist == pg.nlevels && pg.nlevels == S.arity;
+        if (!fast)
+        {
+            run_struct(name, S, pg);
+            return;
+        }
+        canon = "RunCanon<" + std::to_string(s) + ", " + std::to_string(pi) + ">";
+        run_struct(canon, S, pg);
+        buffer_arity = S.arity;
+        run_struct(name, S, S.fast);
+        buffer_arity = 0;
     }
 
     std::string source()
@@ -259,7 +344,8 @@ struct Gen
             o << "  return true;\n";
         }
         o << "}\n";
-        o << "template<int S, int PI> struct Run;\ntemplate<int S> struct Eff;\n";
+        o << "template<int S, int PI> struct Run;\ntemplate<int S, int PI> struct RunCanon;\n"
+          << "template<int S> struct Eff;\n";
         for (u32 s = 0; s < P.nschemas; ++s)
         {
             for (u32 pi = 0; pi < 2; ++pi)

@@ -651,6 +651,100 @@ struct Compiler
         return order;
     }
 
+    /// Estimated candidates of parameter v once the parameters in `placed` are bound: its static domain, narrowed by
+    /// every positive precondition literal of arity 1 or 2 whose other parameters are placed: the literal's atoms
+    /// (fluent: in the initial state; static: all) over the values of its bound positions.
+    double candidates(std::size_t s, u32 v, const std::vector<bool>& placed, const std::vector<u64>& init_count,
+                      const std::vector<std::vector<u32>>& static_pos_values) const
+    {
+        const Schema& sc = T.schemas[s];
+        double e = 0;
+        for (u32 w = 0; w < OW; ++w)
+            e += std::popcount(dom0[s][v][w]);
+        for (const Lit& l : sc.pre)
+        {
+            const u32 ar = T.arity[l.pred];
+            if (!l.pos || ar == 0 || ar > 2 || T.kind[l.pred] == kDerived)
+                continue;
+            bool has_v = false, others_placed = true;
+            for (i32 t : l.terms)
+                if (t >= 0)
+                {
+                    if (static_cast<u32>(t) == v)
+                        has_v = true;
+                    else if (!placed[t])
+                        others_placed = false;
+                }
+            if (!has_v || !others_placed)
+                continue;
+            const bool fluent = T.kind[l.pred] == kFluent;
+            double atoms = fluent ? static_cast<double>(init_count[l.pred]) : static_cast<double>(satoms[l.pred].size());
+            double values = 1;
+            for (u32 i = 0; i < ar; ++i)
+                if (l.terms[i] < 0 || static_cast<u32>(l.terms[i]) != v)
+                    values *= std::max<double>(1, fluent ? L.dsize[L.pos_begin[l.pred] + i]
+                                                         : static_pos_values[l.pred][i]);
+            e = std::min(e, std::max(atoms / values, 0.5));
+        }
+        return e;
+    }
+
+    /// A selectivity order for schema s (greedy: the parameter with the fewest estimated candidates next) and the
+    /// estimated nodes of its search and of index order's.
+    std::vector<u32> selective_order(std::size_t s, double& cost_sel, double& cost_idx) const
+    {
+        const Schema& sc = T.schemas[s];
+        std::vector<u64> init_count(T.kind.size(), 0);
+        for (const auto& a : T.fluent_init)
+            ++init_count[a[0]];
+        std::vector<std::vector<u32>> spv(T.kind.size());
+        for (std::size_t p = 0; p < T.kind.size(); ++p)
+        {
+            if (T.kind[p] != kStatic)
+                continue;
+            spv[p].assign(T.arity[p], 0);
+            for (u32 i = 0; i < T.arity[p]; ++i)
+            {
+                std::vector<u8> seen(n, 0);
+                for (auto* a : satoms[p])
+                    if (!seen[(*a)[1 + i]]++)
+                        ++spv[p][i];
+            }
+        }
+        auto cost = [&](const std::vector<u32>& order) {
+            std::vector<bool> placed(sc.arity, false);
+            double nodes = 1, total = 0;
+            for (u32 v : order)
+            {
+                nodes *= candidates(s, v, placed, init_count, spv);
+                total += nodes;
+                placed[v] = true;
+            }
+            return total;
+        };
+        std::vector<u32> order, idx(sc.arity);
+        std::vector<bool> placed(sc.arity, false);
+        for (u32 d = 0; d < sc.arity; ++d)
+        {
+            idx[d] = d;
+            u32 best = kNone;
+            double best_e = 0;
+            for (u32 v = 0; v < sc.arity; ++v)
+            {
+                if (placed[v])
+                    continue;
+                const double e = candidates(s, v, placed, init_count, spv);
+                if (best == kNone || e < best_e)
+                    best = v, best_e = e;
+            }
+            placed[best] = true;
+            order.push_back(best);
+        }
+        cost_sel = cost(order);
+        cost_idx = cost(idx);
+        return order;
+    }
+
     DProgram matcher(std::size_t s, const std::vector<u32>& order, u32 first_exist)
     {
         const Schema& sc = T.schemas[s];
@@ -854,6 +948,15 @@ struct Compiler
             }
             else
                 ds.prog[0] = matcher(s, order, first_exist);
+            // the compiled matcher's selectivity order: keys of 8 bits per parameter (at most 256 objects, 8
+            // parameters) sort into canonical order
+            double cost_sel = 0, cost_idx = 0;
+            const std::vector<u32> sel = selective_order(s, cost_sel, cost_idx);
+            if (sc.arity >= 2 && n <= 256 && sel != all && cost_sel * 2 <= cost_idx && !ds.prog[1].never)
+            {
+                ds.fast = matcher(s, sel, sc.arity);
+                ds.fast_on = 1;
+            }
             ds.add_begin = static_cast<u32>(P.lits.size());
             for (const Lit& l : sc.eff)
                 if (l.pos)

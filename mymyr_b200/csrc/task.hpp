@@ -146,8 +146,13 @@ struct DSchema
     u32 arity = 0;
     u32 add_begin = 0, add_end = 0;  // into lits
     u32 del_begin = 0, del_end = 0;
-    u32 pad = 0;
+    u32 fast_on = 0;   // the compiled matcher binds in `fast`'s order and sorts (see below)
     DProgram prog[2];  // [0] witness pruning on, [1] off
+    /// Every parameter in a selectivity order (most constrained first, from static estimates), for the compiled
+    /// matcher: its bindings are buffered and sorted into canonical order before they are emitted. Used when the
+    /// estimated search is at most half of index order's, and for witness pruning only when the schema has no
+    /// witness-only parameter. The interpreted matcher always binds in index order.
+    DProgram fast;
 };
 
 /// Everything the kernels read, as host vectors (uploaded into one device blob) plus scalar facts.
