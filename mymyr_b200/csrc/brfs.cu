@@ -126,6 +126,15 @@ __global__ void __launch_bounds__(128) k_expand(DevTask T, u32 pi, const u32* __
     }
 }
 
+/// Goal states among the parents frontier[0, n) (a layer cut short by max_states).
+__global__ void k_count_goals(DevTask T, const u64* __restrict__ rows, u32 W, const u32* __restrict__ frontier, u64 n,
+                              u32* out)
+{
+    for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < n; i += static_cast<u64>(gridDim.x) * blockDim.x)
+        if (goal_holds(T, GlobalRow{rows + static_cast<u64>(frontier[i]) * W, W}))
+            atomicAdd(out, 1u);
+}
+
 __global__ void k_seed_root(Store S, u32* state_g)
 {
     const GlobalRow r{S.rows, S.W};
@@ -378,7 +387,7 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
     u64 layer_begin = 0, layer_end = 1;
     B.layer_begin.assign(1, 0);
     u32 layers = 0;
-    bool exhausted = false, solved = false;
+    bool exhausted = false, solved = false, full = false;
     u64 expanded = 0, generated = 0, goals = 0, goal_id = 0, fingerprint = 0;
     double count_ms = 0, gen_ms = 0, dedup_ms = 0;
     std::vector<std::array<u64, 3>> counts;
@@ -392,6 +401,11 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
         }
         if (layers == o.max_depth)
             break;
+        if (B.n_states >= o.max_states)
+        {
+            full = true;  // the store is full before the layer (max_states <= 1)
+            break;
+        }
         ++layers;
         ensure_layer(B, E, 0);
         LayerMisc* misc = B.misc.as<LayerMisc>();
@@ -423,24 +437,14 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
         LayerMisc m = read_misc(B);
         u64 E_exp = E, G = m.total_cand;
         bool stop = false;
-        if (m.goals)
+        const u32 layer_goals = m.goals, first_goal = m.first_goal;
+        if (layer_goals && o.stop_at_goal)
         {
-            if (!solved)
-            {
-                solved = true;
-                goal_id = layer_begin + m.first_goal;
-            }
-            if (o.stop_at_goal)
-            {
-                E_exp = m.first_goal;
-                if (E_exp < E)
-                    B2_CUDA(cudaMemcpyAsync(&G, B.cand_base.as<u64>() + E_exp, 8, cudaMemcpyDeviceToHost, s));
-                stream_wait(s);
-                goals += 1;
-                stop = true;
-            }
-            else
-                goals += m.goals;
+            E_exp = first_goal;
+            if (E_exp < E)
+                B2_CUDA(cudaMemcpyAsync(&G, B.cand_base.as<u64>() + E_exp, 8, cudaMemcpyDeviceToHost, s));
+            stream_wait(s);
+            stop = true;
         }
         if (G >= (u64{1} << 32) - 1 - cand_next)
             throw Error(B2_CAPACITY, "b2_brfs: more than 2^32 - 2 candidates");
@@ -496,6 +500,48 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
                 dedup_ms += c;
             }
         }
+        // the goal parents reached: under stop_at_goal the first one (expansion stops there), else all of them
+        u64 goals_layer = o.stop_at_goal ? (layer_goals ? 1 : 0) : layer_goals;
+        bool goal_reached = layer_goals > 0;
+        if (B.n_states + N >= o.max_states && N > 0)
+        {
+            // max_states: the search stops right after storing state max_states - 1 (inside its parent's expansion,
+            // as run_flat does, src/mymyr/search/brfs.cpp:301-384): the layer's parents up to that parent are
+            // expanded, its successors up to that candidate generated
+            const u64 last = o.max_states - 1;
+            u32 gstar = 0, pstar = 0;
+            B2_CUDA(cudaMemcpyAsync(&gstar, B.state_g.as<u32>() + last, 4, cudaMemcpyDeviceToHost, s));
+            stream_wait(s);
+            B2_CUDA(cudaMemcpyAsync(&pstar, B.par.as<u32>() + gstar, 4, cudaMemcpyDeviceToHost, s));
+            stream_wait(s);
+            N = o.max_states - B.n_states;
+            E_exp = static_cast<u64>(pstar) + 1;
+            G = gstar - cand_next + 1;
+            full = stop = true;
+            if (o.stop_at_goal)
+            {
+                goals_layer = 0;  // the layer's first goal parent lies after the cut (E_exp was at most it)
+                goal_reached = false;
+            }
+            else
+            {
+                LayerMisc* misc = B.misc.as<LayerMisc>();
+                B2_CUDA(cudaMemsetAsync(&misc->goals, 0, 4, s));
+                k_count_goals<<<grid_for(E_exp, 256), 256, 0, s>>>(T, B.rows.as<u64>(), W,
+                                                                     B.state_g.as<u32>() + layer_begin, E_exp,
+                                                                     &misc->goals);
+                B2_CUDA(cudaGetLastError());
+                ++B.launches;
+                goals_layer = read_misc(B).goals;
+                goal_reached = layer_goals > 0 && first_goal <= pstar;
+            }
+        }
+        if (goal_reached && !solved)
+        {
+            solved = true;
+            goal_id = layer_begin + first_goal;
+        }
+        goals += goals_layer;
         expanded += E_exp;
         generated += G;
         counts.push_back({E_exp, G, N});
@@ -533,7 +579,8 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
     R.dedup_ms = dedup_ms;
     R.kernel_launches = B.launches;
     R.status = solved ? B2_SEARCH_SOLVED
-                      : (exhausted || layers >= o.max_depth ? B2_SEARCH_EXHAUSTED : B2_SEARCH_OUT_OF_STATES);
+                      : full ? B2_SEARCH_OUT_OF_STATES
+                             : (exhausted || layers >= o.max_depth ? B2_SEARCH_EXHAUSTED : B2_SEARCH_OUT_OF_STATES);
     R.rehashes = B.rehashes;
     u32 lg = 0;
     while ((u64{1} << lg) < B.table_slots)
@@ -572,8 +619,8 @@ b2_status b2_brfs_create(b2_task* task, const b2_brfs_options* options, b2_brfs*
             throw std::invalid_argument("b2_brfs_create: null argument");
         if (!task->ctx)
             throw std::invalid_argument("a host-only task (created without a context) cannot run on the device");
-        if (options->max_states != ~uint64_t{0})
-            throw Error(B2_UNSUPPORTED, "b2_brfs: max_states is not supported by the device BrFS yet");
+        if (options->max_states != ~uint64_t{0} && options->comm)
+            throw Error(B2_UNSUPPORTED, "b2_brfs: max_states is not supported by the sharded search");
         if (options->comm)
         {
             if (options->comm->device != task->ctx->device)

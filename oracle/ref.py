@@ -36,7 +36,7 @@ def lib():
         L.ref_task_open.argtypes = [C.c_char_p, C.c_int, C.c_int]
         L.ref_task_close.argtypes = [P]
         for name in ("ref_task_info", "ref_initial_state", "ref_is_goal", "ref_brfs", "ref_brfs_states", "ref_expand",
-                     "ref_env_reset", "ref_env_step", "ref_pool_bench", "ref_astar", "ref_hmax", "ref_ground_stats"):
+                     "ref_env_reset", "ref_env_step", "ref_pool_bench", "ref_astar", "ref_hmax", "ref_ground_stats", "ref_brfs_limited"):
             getattr(L, name).restype = C.c_int64
         L.ref_task_info.argtypes = [P, P]
         L.ref_initial_state.argtypes = [P, P, C.c_uint32]
@@ -62,6 +62,7 @@ def lib():
         L.ref_astar.argtypes = [P, P, P]
         L.ref_hmax.argtypes = [P, P, C.c_uint64, C.c_uint32, P]
         L.ref_ground_stats.argtypes = [P, P]
+        L.ref_brfs_limited.argtypes = [P, C.c_uint64, C.c_uint32, C.c_int, C.c_int, C.c_int, P, P, C.c_uint32]
         _L = L
     return _L
 
@@ -127,6 +128,21 @@ class RefTask:
         r = {k: int(v) for k, v in zip(keys, out)}
         r["layer_counts"] = [tuple(int(x) for x in row) for row in lc[:n]]
         r["search_s"] = sec.value
+        return r
+
+    def brfs_limited(self, max_states, max_depth=None, stop_at_goal=True, witness_pruning=True, fingerprint=False):
+        """Single-threaded mymyr::brfs with max_states (status as SearchStatus: 0 solved, 1 exhausted, 2 out of
+        states, 6 unsolvable)."""
+        out = np.zeros(10, np.uint64)
+        cap = 4096
+        lc = np.zeros((cap, 3), np.uint64)
+        n = _check(lib().ref_brfs_limited(self.h, max_states, 0xFFFFFFFF if max_depth is None else max_depth,
+                                          int(stop_at_goal), int(witness_pruning), int(fingerprint), out.ctypes.data,
+                                          lc.ctypes.data, cap))
+        keys = ["states", "expanded", "generated", "num_goal_states", "layers", "exhausted", "solved", "fingerprint",
+                "plan_length", "status"]
+        r = {k: int(v) for k, v in zip(keys, out)}
+        r["layer_counts"] = [tuple(int(x) for x in row) for row in lc[:n]]
         return r
 
     def brfs_states(self, max_depth=None, witness_pruning=True, cap=1 << 22):

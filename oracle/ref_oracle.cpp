@@ -9,6 +9,7 @@
 //   ref_pool_bench     mymyr::rl::CpuEnvPool step               include/mymyr/rl/pool.hpp:114-172
 //   ref_astar          mymyr::search::astar_eager (h^max)       include/mymyr/search/best_first.hpp:191
 //   ref_hmax           heuristics::make_heuristic(Kind::Max)    include/mymyr/heuristics/heuristic.hpp:259
+//   ref_brfs_limited   mymyr::brfs with max_states               include/mymyr/search/brfs.hpp:79
 //   ref_ground_stats   heuristics::ground (GroundingStats)      include/mymyr/heuristics/heuristic.hpp:165
 //   ref_hash_state     mymyr::hash::state                       include/mymyr/core/hash.hpp:58
 //   ref_philox_bits64  mymyr::rl::rng::bits64                   include/mymyr/rl/rng.hpp:68
@@ -186,6 +187,38 @@ int64_t ref_brfs(void* h, uint32_t threads, uint32_t max_depth, int stop_at_goal
         out[8] = r.plan.size();
         out[9] = static_cast<uint64_t>(r.status);
         *seconds = r.search_s;
+        for (uint32_t i = 0; i < r.layer_counts.size() && i < layer_cap; ++i)
+            for (int k = 0; k < 3; ++k)
+                layer_counts[3 * i + k] = r.layer_counts[i][k];
+        return static_cast<int64_t>(r.layer_counts.size());
+    });
+}
+
+/// mymyr::brfs single-threaded (flat store) with a state budget: out as ref_brfs (status: SearchStatus).
+int64_t ref_brfs_limited(void* h, uint64_t max_states, uint32_t max_depth, int stop_at_goal, int witness,
+                         int fingerprint, uint64_t* out, uint64_t* layer_counts, uint32_t layer_cap)
+{
+    return guarded([&] {
+        BrfsOptions o;
+        o.threads = 1;
+        o.max_states = max_states;
+        o.max_depth = max_depth;
+        o.stop_at_goal = stop_at_goal != 0;
+        o.witness_pruning = witness != 0;
+        o.fingerprint = fingerprint != 0;
+        o.layer_stats = true;
+        o.store = BrfsOptions::Store::Flat;
+        const BrfsResult r = brfs(T(h), o);
+        out[0] = r.states;
+        out[1] = r.expanded;
+        out[2] = r.generated;
+        out[3] = r.num_goal_states;
+        out[4] = r.layers;
+        out[5] = r.exhausted;
+        out[6] = r.solved;
+        out[7] = r.fingerprint;
+        out[8] = r.plan.size();
+        out[9] = static_cast<uint64_t>(r.status);
         for (uint32_t i = 0; i < r.layer_counts.size() && i < layer_cap; ++i)
             for (int k = 0; k < 3; ++k)
                 layer_counts[3 * i + k] = r.layer_counts[i][k];

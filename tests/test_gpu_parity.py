@@ -263,3 +263,41 @@ def test_env_full_config_digest(ref):
         env.step()
         renv.step()
     _compare_env(env, renv)
+
+
+MAX_STATES_CASES = [
+    ("tower5", lambda: tasks.tower(5, 3), None),
+    ("tile3x3_d14", lambda: tasks.sliding_tile(3, 3, 30, 0), 14),
+    ("transport_2_4_2", lambda: tasks.transport(2, 4, 2, 1), None),
+]
+
+REF_STATUS = {0: "solved", 1: "exhausted", 2: "out_of_states", 6: "unsolvable"}
+
+
+@pytest.mark.parametrize("name,make,depth", MAX_STATES_CASES, ids=[c[0] for c in MAX_STATES_CASES])
+@pytest.mark.parametrize("matcher", MATCHERS)
+@pytest.mark.parametrize("stop", [False, True])
+def test_brfs_max_states_matches_reference(ref, name, make, depth, matcher, stop):
+    """max_states stops the search right after that many states are stored, inside the expansion that stores the
+    last one (run_flat): states, expanded, generated, per-layer counts, goal count, status, fingerprint and the kept
+    states' rows and node records equal the reference's."""
+    text = make()
+    rt = ref.RefTask(text)
+    t = Task.from_text(text, matcher=matcher)
+    full = rt.brfs(max_depth=depth, stop_at_goal=False)
+    rows, par, idx = rt.brfs_states(max_depth=depth)
+    n = full["states"]
+    for M in sorted({1, 2, 3, 7, n // 3, n // 2 + 1, n - 1, n, n + 3}):
+        exp = rt.brfs_limited(M, max_depth=depth, stop_at_goal=stop, fingerprint=True)
+        r = b2cuda.brfs(t, max_states=M, max_depth=depth, stop_at_goal=stop, fingerprint=True)
+        got = (r.states, r.expanded, r.generated, r.num_goal_states, r.layers, r.layer_counts, r.status,
+               r.fingerprint)
+        want = (exp["states"], exp["expanded"], exp["generated"], exp["num_goal_states"], exp["layers"],
+                exp["layer_counts"], REF_STATUS[exp["status"]], exp["fingerprint"])
+        assert got == want, (M, got, want)
+        k = r.states
+        np.testing.assert_array_equal(r.state_rows(), rows[:k])
+        p, i = r.nodes()
+        np.testing.assert_array_equal(p, par[:k])
+        np.testing.assert_array_equal(i, idx[:k])
+        r.close()
