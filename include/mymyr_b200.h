@@ -304,7 +304,10 @@ typedef struct b2_astar_options {
     void* stream;              /* NULL: a stream of its own */
     b2_heuristic* heuristic;   /* an h^max of the same task to share (NULL: the search grounds its own) */
     uint64_t chunk_candidates; /* successors staged at once: an f layer with more is expanded in chunks (bounded
-                                  memory; 0: 2^26; at least 2^16) */
+                                  memory; 0: 2^26; at least 2^16; one GPU) */
+    b2_comm* comm;             /* multi-GPU: states partitioned by state-hash owner over the communicator's ranks, every
+                                  rank calls create and run together and gets the same result (no plan; no counterpart
+                                  in the reference) */
 } b2_astar_options;
 
 void b2_astar_options_default(b2_astar_options* o);

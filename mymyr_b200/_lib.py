@@ -97,7 +97,7 @@ class HeuristicInfo(C.Structure):
 class AstarOptions(C.Structure):
     _fields_ = [("max_expansions", C.c_uint64), ("expected_states", C.c_uint64), ("witness_pruning", C.c_int32),
                 ("timings", C.c_int32), ("stream", C.c_void_p), ("heuristic", C.c_void_p),
-                ("chunk_candidates", C.c_uint64)]
+                ("chunk_candidates", C.c_uint64), ("comm", C.c_void_p)]
 
 
 class AstarResult(C.Structure):

@@ -25,6 +25,7 @@
 // record r that claimed the slot (rewritten to the new state's id by the id scan).
 
 #include "brfs.cuh"
+#include "comm.hpp"
 #include "relax.hpp"
 
 #include <array>
@@ -154,6 +155,11 @@ struct AstarMisc
     u64 fmin;       // smallest f of a valid open entry (bucket switch)
     u64 nkeep;      // open entries kept by the extraction
     u64 nfront;     // states extracted into the frontier
+    // sharded search: this rank's values and their reductions over the ranks
+    u64 gsum;       // the wave's successors (SUM)
+    u64 nnext_all;  // the next wave's states (SUM)
+    u64 goal_all;   // the best goal over the ranks, (g << 32 | rank << 27 | state) (MIN)
+    u64 stats[5];   // expanded, generated, states, evaluations, dead ends (SUM, at the end)
 };
 
 /// Chunks of a wave whose candidates exceed `chunk`: chunk k starts at the first frontier state whose first
@@ -175,13 +181,10 @@ __device__ __forceinline__ u32 key_g(u64 key) { return static_cast<u32>(key >> 4
 
 struct InsertArgs
 {
-    const u64* staging;
+    const u64* staging;  // records [row | hash | key]
     u64 G;
     u32 W;
     u32 wave;          // the chunk's stamp (unique per chunk): a state is listed touched once per chunk
-    const u32* frontier;
-    const u64* cand_base;
-    u64 nF;
     const u64* rows;   // states
     u64* best;         // per state
     const u8* flags;   // per state
@@ -203,25 +206,8 @@ __global__ void k_astar_insert(InsertArgs a)
     for (u64 r = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; r < a.G; r += static_cast<u64>(gridDim.x) * blockDim.x)
     {
         const u64* rec = a.staging + r * RW;
-        const u64 h = rec[W], c = rec[W + 1];
-        // the parent: the last frontier position p with cand_base[p] <= c
-        u64 lo = 0, hi = a.nF;
-        while (hi - lo > 1)
-        {
-            const u64 mid = (lo + hi) / 2;
-            if (a.cand_base[mid] <= c)
-                lo = mid;
-            else
-                hi = mid;
-        }
-        const u64 parent = a.frontier[lo], kid = c - a.cand_base[lo];
-        const u32 gnew = key_g(a.best[parent]) + 1;
-        if (kid > 0xFFFF || gnew > 0xFFFF)
-        {
-            atomicOr(&a.misc->lm.status, kStatusCapacity);  // a state with 2^16 successors, or a path of 2^16 steps
-            continue;
-        }
-        const u64 key = (static_cast<u64>(gnew) << 48) | (parent << 16) | kid;
+        const u64 h = rec[W], key = rec[W + 1];  // key = (g << 48 | parent << 16 | successor index), made by staging
+        const u32 gnew = key_g(key);
         const u64 tag = h & 0xFFFFFFFF00000000ull;
         u64 j = h & a.mask;
         bool done = false;
@@ -436,6 +422,35 @@ __global__ void k_rehash_entries(const u64* __restrict__ old, u64 old_slots, u64
     }
 }
 
+/// The key base of each frontier state: ((g + 1) << 48) | (parent id << 16), parent id = rank << kRankShift | state;
+/// the staging kernel adds the successor index (its records carry their key).
+constexpr u32 kRankShift = 27;  // a sharded search's local states stay below 2^27
+__global__ void k_key_base(const u32* __restrict__ frontier, u64 nF, const u64* __restrict__ best,
+                           const u32* __restrict__ counts, u64 rank_bits, u64* __restrict__ keys, AstarMisc* misc)
+{
+    for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < nF; i += static_cast<u64>(gridDim.x) * blockDim.x)
+    {
+        const u64 s = frontier[i];
+        const u64 g = key_g(best[s]) + 1;
+        if (g > 0xFFFF || counts[i] > 0x10000u)
+            atomicOr(&misc->lm.status, kStatusCapacity);  // a path of 2^16 steps or a state with 2^16 successors
+        keys[i] = (g << 48) | ((rank_bits | s) << 16);
+    }
+}
+
+/// Sharded search: this rank's best goal and next-wave size into the fields the ranks reduce (goal ids global).
+__global__ void k_astar_globalize(AstarMisc* misc, u64 rank_bits)
+{
+    const u64 b = misc->best_goal;  // this rank's, with a local state id
+    if (b != ~u64{0})
+    {
+        const u64 g = (b & 0xFFFFFFFF00000000ull) | rank_bits | (b & 0xFFFFFFFFull);
+        if (g < misc->goal_all)
+            misc->goal_all = g;
+    }
+    misc->nnext_all = misc->nnext;
+}
+
 __global__ void k_iota(u32* p, u64 n)
 {
     for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < n; i += static_cast<u64>(gridDim.x) * blockDim.x)
@@ -531,7 +546,7 @@ struct b2_astar
     DeviceBuffer table;
     u64 table_slots = 0;
     // per wave: frontier-sized and candidate-sized scratch
-    DeviceBuffer counts, cand_base, iota, sums;
+    DeviceBuffer counts, cand_base, keyb, iota, sums;
     u64 cap_front = 0, cap_iota = 0;
     DeviceBuffer staging, best_rec, slot_of, claimed, touched, fresh;
     u64 cap_wave = 0;
@@ -547,6 +562,9 @@ struct b2_astar
     u32 goal_state = 0;
     bool solved = false;
     u64 cost = 0;
+    b2_comm* comm = nullptr;  // sharded search
+    DeviceBuffer hist_m;      // sharded: per-owner counts and their all-gather [world + world * world]
+    DeviceBuffer sstage;      // sharded: this rank's staged records before the push
 };
 
 namespace
@@ -607,6 +625,7 @@ void ensure_front(b2_astar& A, u64 nF)
         const u64 cap = grow_to(nF, A.cap_front);
         A.counts.alloc(cap * 4, s);
         A.cand_base.alloc((cap + 1) * 8, s);
+        A.keyb.alloc(cap * 8, s);
         A.cap_front = cap;
     }
     if (nF > A.cap_iota)
@@ -647,6 +666,24 @@ void ensure_wave(b2_astar& A, u64 G, u64 nopen)
         A.keep.alloc(cap * 8, s);
         A.cap_open = cap;
     }
+}
+
+u32 dev_owner(u64 h, u32 world) { return static_cast<u32>(((h >> 32) * world) >> 32); }
+
+const AstarMisc& read_misc(b2_astar& A);
+
+/// read_misc for a sharded search: the wait polls the communicator (a rank that stopped taking part fails it).
+const AstarMisc& read_misc_sync(b2_astar& A)
+{
+    B2_CUDA(cudaMemcpyAsync(A.misc_host, A.misc.p, sizeof(AstarMisc), cudaMemcpyDeviceToHost, A.stream));
+    comm_sync(A.comm, A.stream);
+    if (A.misc_host->lm.status & kStatusProbeLimit)
+        throw Error(B2_DEVICE_FAULT, "b2_astar: a hash-set probe ran past its bound");
+    if (A.misc_host->lm.status & kStatusCapacity)
+        throw Error(B2_CAPACITY, "b2_astar: a state with 2^16 successors or a path of 2^16 steps");
+    if (A.misc_host->lm.status)
+        throw Error(B2_DEVICE_FAULT, "b2_astar: device status " + std::to_string(A.misc_host->lm.status));
+    return *A.misc_host;
 }
 
 const AstarMisc& read_misc(b2_astar& A)
@@ -769,6 +806,10 @@ void run_astar(b2_astar& A, b2_astar_result& R)
         A.launches += 4;
         if (A.opt.timings)
             B2_CUDA(cudaEventRecord(ev[1], s));
+        k_key_base<<<grid_for(nF, 256, sms * 16), 256, 0, s>>>(A.front.as<u32>(), nF, A.best.as<u64>(),
+                                                                A.counts.as<u32>(), 0, A.keyb.as<u64>(), misc);
+        B2_CUDA(cudaGetLastError());
+        ++A.launches;
         const u64 G = read_misc(A).lm.total_cand;
         // the wave's chunks: [first state, end state, first candidate, end candidate)
         std::vector<std::array<u64, 4>> chunks;
@@ -826,7 +867,7 @@ void run_astar(b2_astar& A, b2_astar_result& R)
             a.E = i1 - i0;
             a.layer_begin = 0;
             a.limit = ~u64{0};
-            a.gbase = A.cand_base.as<u64>() + i0;
+            a.gbase = A.keyb.as<u64>() + i0;  // the records' last word: key base + successor index
             a.local_base = A.cand_base.as<u64>() + i0;
             a.stage_base = c0;
             a.staging = A.staging.as<u64>();
@@ -843,9 +884,6 @@ void run_astar(b2_astar& A, b2_astar_result& R)
             in.G = Gc;
             in.W = W;
             in.wave = stamp;
-            in.frontier = A.front.as<u32>() + i0;
-            in.cand_base = A.cand_base.as<u64>() + i0;
-            in.nF = i1 - i0;
             in.rows = A.rows.as<u64>();
             in.best = A.best.as<u64>();
             in.flags = A.flags.as<u8>();
@@ -981,6 +1019,326 @@ void run_astar(b2_astar& A, b2_astar_result& R)
     R.kernel_launches = A.launches;
     R.search_s = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
 }
+
+/// A* sharded over the communicator's ranks by state-hash owner (HDA*-style, with the batched f layers of run_astar):
+/// every wave, each rank expands its part of the frontier into records [row | hash | key] (the key's parent is the
+/// global id rank << 27 | state), the records go to their owners through the peer-memory push of the sharded BrFS,
+/// and each owner inserts, evaluates and pushes its own. The ranks agree on every decision through reductions: the
+/// wave's successors, the next wave's size and the best goal (g << 32 | global id) after each wave, the smallest f of
+/// the open lists at a bucket switch.
+void run_astar_sharded(b2_astar& A, b2_astar_result& R)
+{
+    const auto t0 = std::chrono::steady_clock::now();
+    b2_task* task = A.task;
+    b2_comm* comm = A.comm;
+    const u32 me = comm->rank, world = comm->world;
+    const Program& P = task->prog;
+    const DevTask& T = task->dev;
+    const u32 pi = A.opt.witness_pruning ? 0 : 1;
+    const u32 W = A.W, RW = W + 2;
+    const unsigned sms = static_cast<unsigned>(task->ctx->sms);
+    cudaStream_t s = A.stream;
+    R.relaxed_ops = A.H->R.ops();
+    R.relaxed_atoms = A.H->R.reached;
+    if (P.goal_unsat)
+    {
+        R.status = B2_SEARCH_UNSOLVABLE;
+        return;
+    }
+    const u64 expect = std::max<u64>(A.opt.expected_states / world, 4096);
+    ensure_states(A, expect);
+    A.misc.alloc(sizeof(AstarMisc), s);
+    A.misc_host = static_cast<AstarMisc*>(task->ctx->pinned.take());
+    *A.misc_host = AstarMisc{};
+    A.misc_host->best_goal = ~u64{0};
+    A.misc_host->goal_all = ~u64{0};
+    B2_CUDA(cudaMemcpyAsync(A.misc.p, A.misc_host, sizeof(AstarMisc), cudaMemcpyHostToDevice, s));
+    ensure_table(A, expect);
+    AstarMisc* misc = A.misc.as<AstarMisc>();
+    A.hist_m.alloc((world + world * world) * 8, s);
+    u64* hist = A.hist_m.as<u64>();
+    u64* M = hist + world;
+    // the root: state 0 on every rank (row and hash), stored and expanded by its owner
+    B2_CUDA(cudaMemcpyAsync(A.rows.p, P.initial.data(), W * 8, cudaMemcpyHostToDevice, s));
+    k_astar_seed<<<1, 1, 0, s>>>(A.rows.as<u64>(), A.hash.as<u64>(), W, A.best.as<u64>(), A.flags.as<u8>(),
+                                 A.table.as<u64>(), A.table_slots - 1, max_probe(A.table_slots), misc);
+    B2_CUDA(cudaGetLastError());
+    ++A.launches;
+    u64 root_hash = 0;
+    B2_CUDA(cudaMemcpyAsync(&root_hash, A.hash.p, 8, cudaMemcpyDeviceToHost, s));
+    ensure_front(A, 1024);
+    ensure_wave(A, 1024, 0);
+    B2_CUDA(cudaMemsetAsync(A.front.p, 0, 4, s));
+    launch_hmax(*A.H, A.rows.as<u64>(), W, A.front.as<u32>(), nullptr, 1, A.hval.as<u32>(), true, A.flags.as<u8>(),
+                static_cast<int>(sms), s);
+    ++A.launches;
+    u32 h0 = 0;
+    u8 f0 = 0;
+    B2_CUDA(cudaMemcpyAsync(&h0, A.hval.p, 4, cudaMemcpyDeviceToHost, s));
+    B2_CUDA(cudaMemcpyAsync(&f0, A.flags.p, 1, cudaMemcpyDeviceToHost, s));
+    comm_sync(comm, s);
+    // the root's table entry and state stay only on its owner (the others keep row 0 as scratch)
+    const bool own_root = dev_owner(root_hash, world) == me;
+    if (!own_root)
+    {
+        B2_CUDA(cudaMemsetAsync(A.table.p, 0xFF, A.table_slots * 8, s));
+        A.n_states = 0;
+    }
+    else
+        A.n_states = 1;
+    R.evaluations = 1;
+    R.initial_h = h0 == kDeadEnd ? -1.0 : static_cast<double>(h0);
+    const bool dead_start = h0 == kDeadEnd && !(f0 & kGoal);
+    if (f0 & kGoal)
+    {
+        A.solved = true;
+        A.cost = 0;
+    }
+    else if (dead_start)
+        R.dead_ends = 1;
+    u64 fcur = h0, nF = own_root ? 1 : 0, nopen = 0, nnext_all = 1;
+    u64 expanded = 0, generated = 0, fresh_total = 0, dead = 0;
+    u32 wave = 0, f_layers = 1, stamp = 0;
+    bool exhausted = false;
+    if (A.n_states >= (u64{1} << kRankShift))
+        throw Error(B2_CAPACITY, "b2_astar: a rank of a sharded search holds at most 2^27 states");
+    while (!A.solved && !dead_start)
+    {
+        if (A.opt.max_expansions && expanded * world >= A.opt.max_expansions)
+            break;
+        ++wave;
+        ++stamp;
+        ensure_front(A, nF);
+        B2_CUDA(cudaMemsetAsync(misc, 0, offsetof(AstarMisc, nopen), s));
+        if (nF)
+        {
+            const unsigned grid = grid_for(nF, 128, sms * 64);
+            if (task->jit)
+            {
+                dev::BrfsArgs a{};
+                a.frontier = A.front.as<u32>();
+                a.E = nF;
+                a.counts = A.counts.as<u32>();
+                a.misc = &misc->lm;
+                a.S.rows = A.rows.as<u64>();
+                a.S.W = W;
+                a.pi = pi;
+                jit_launch(task->jit->brfs_count[pi], grid, 128, &a, s);
+            }
+            else
+                dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
+                    k_count<OW, WR><<<grid, 128, 0, s>>>(T, pi, A.rows.as<u64>(), W, A.front.as<u32>(), nF,
+                                                         A.counts.as<u32>(), &misc->lm);
+                });
+            ++A.launches;
+        }
+        if (A.sums.bytes < scan_scratch_bytes(nF))
+            A.sums.alloc(scan_scratch_bytes(grow_to(nF, 0)), s);
+        device_scan(CountIn{A.counts.as<u32>()}, BaseOut{A.cand_base.as<u64>()}, nF, &misc->lm.total_cand,
+                    A.sums.as<u64>(), s);
+        if (nF)
+            k_key_base<<<grid_for(nF, 256, sms * 16), 256, 0, s>>>(A.front.as<u32>(), nF, A.best.as<u64>(),
+                                                                    A.counts.as<u32>(), u64{me} << kRankShift,
+                                                                    A.keyb.as<u64>(), misc);
+        B2_CUDA(cudaMemcpyAsync(&misc->gsum, &misc->lm.total_cand, 8, cudaMemcpyDeviceToDevice, s));
+        comm_allreduce(comm, &misc->gsum, &misc->gsum, 1, CommType::U64, CommOp::Sum, s);
+        A.launches += 4;
+        const AstarMisc m1 = read_misc_sync(A);
+        const u64 Gl = m1.lm.total_cand, Gt = m1.gsum;
+        if (Gt > 0)
+        {
+            // stage this rank's successors by owner, then learn every rank's counts (the receive sizes)
+            if (A.sstage.bytes < Gl * RW * 8)
+                A.sstage.alloc(grow_to(Gl, A.sstage.bytes / (RW * 8)) * RW * 8, s);
+            B2_CUDA(cudaMemsetAsync(hist, 0, world * 8, s));
+            if (nF && Gl)
+            {
+                dev::DExpandArgs a{};
+                a.rows = A.rows.as<u64>();
+                a.frontier = A.front.as<u32>();
+                a.frontier_id = A.iota.as<u32>();
+                a.E = nF;
+                a.layer_begin = 0;
+                a.limit = ~u64{0};
+                a.gbase = A.keyb.as<u64>();
+                a.local_base = A.cand_base.as<u64>();
+                a.stage_base = 0;
+                a.staging = A.sstage.as<u64>();
+                a.hist = hist;
+                a.world = world;
+                a.W = W;
+                a.pi = pi;
+                const unsigned grid = grid_for(nF, 128, sms * 64);
+                if (task->jit)
+                    jit_launch(task->jit->dbrfs_expand[pi], grid, 128, &a, s);
+                else
+                    dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() { k_dexpand<OW, WR><<<grid, 128, 0, s>>>(T, a); });
+                ++A.launches;
+            }
+            comm_allgather(comm, hist, M, world, CommType::U64, s);
+            std::vector<u64> Mh(static_cast<std::size_t>(world) * world);
+            B2_CUDA(cudaMemcpyAsync(Mh.data(), M, Mh.size() * 8, cudaMemcpyDeviceToHost, s));
+            comm_sync(comm, s);
+            u64 recv = 0, most = 0;
+            for (u32 d = 0; d < world; ++d)
+            {
+                u64 col = 0;
+                for (u32 r = 0; r < world; ++r)
+                    col += Mh[static_cast<std::size_t>(r) * world + d];
+                most = std::max(most, col);
+                if (d == me)
+                    recv = col;
+            }
+            // the same decision on every rank: receive buffers for the largest owner's records
+            const u64 need = most * RW * 8;
+            if (need > comm->exchange.bytes)
+                peer_buffer_exchange(comm, comm->exchange, std::max<u64>(grow_to(need, comm->exchange.bytes / 2),
+                                                                         u64{1} << 20), s);
+            if (A.n_states + recv >= (u64{1} << kRankShift))
+                throw Error(B2_CAPACITY, "b2_astar: a rank of a sharded search holds at most 2^27 states");
+            ensure_wave(A, std::max<u64>(recv, 1), nopen);
+            if (A.next.bytes < (recv + 1) * 4)
+                A.next.alloc(grow_to(recv + 1, 0) * 4, s);
+            ensure_states(A, A.n_states + recv);
+            ensure_table(A, A.n_states + recv);
+            B2_CUDA(cudaMemsetAsync(misc, 0, offsetof(AstarMisc, nnext), s));  // the count pass's status was read
+            const u32 tile = std::min<u32>(kPushThreads, kPushSmemWords / RW);
+            u64* cursor = hist;  // the counts were gathered: reuse as this rank's per-owner cursors
+            B2_CUDA(cudaMemsetAsync(cursor, 0, world * 8, s));
+            k_push<<<grid_for(Gl, tile, sms * 8), kPushThreads, tile * RW * 8, s>>>(
+                A.sstage.as<u64>(), M, reinterpret_cast<u64* const*>(comm->exchange.table.p),
+                reinterpret_cast<unsigned long long*>(cursor), me, world, RW, tile);
+            B2_CUDA(cudaGetLastError());
+            comm_allreduce(comm, &misc->lm.ndeferred, &misc->lm.ndeferred, 1, CommType::U32, CommOp::Sum, s);
+            A.launches += 1;
+            if (recv)
+            {
+                const u64* in_rec = static_cast<const u64*>(comm->exchange.local.p);
+                B2_CUDA(cudaMemsetAsync(A.best_rec.p, 0xFF, recv * 8, s));
+                B2_CUDA(cudaMemsetAsync(A.claimed.p, 0, recv, s));
+                InsertArgs in{};
+                in.staging = in_rec;
+                in.G = recv;
+                in.W = W;
+                in.wave = stamp;
+                in.rows = A.rows.as<u64>();
+                in.best = A.best.as<u64>();
+                in.flags = A.flags.as<u8>();
+                in.stamp = A.stamp.as<u32>();
+                in.table = A.table.as<u64>();
+                in.mask = A.table_slots - 1;
+                in.max_probe = max_probe(A.table_slots);
+                in.best_rec = A.best_rec.as<u64>();
+                in.slot_of = A.slot_of.as<u64>();
+                in.claimed = A.claimed.as<u8>();
+                in.touched = A.touched.as<u32>();
+                in.misc = misc;
+                k_astar_insert<<<grid_for(recv, 256, sms * 16), 256, 0, s>>>(in);
+                B2_CUDA(cudaGetLastError());
+                ClaimOut co{in_rec, W, stamp, A.n_states, A.best_rec.as<u64>(), A.slot_of.as<u64>(),
+                            A.table.as<u64>(), A.rows.as<u64>(), A.hash.as<u64>(), A.best.as<u64>(), A.flags.as<u8>(),
+                            A.stamp.as<u32>(), A.fresh.as<u32>(), A.touched.as<u32>(), misc};
+                device_scan(ClaimIn{A.claimed.as<u8>()}, co, recv, &misc->nfresh, A.sums.as<u64>(), s);
+                launch_hmax(*A.H, A.rows.as<u64>(), W, A.fresh.as<u32>(), &misc->nfresh, recv, A.hval.as<u32>(), true,
+                            A.flags.as<u8>(), static_cast<int>(sms), s);
+                k_astar_push<<<grid_for(recv, 256, sms * 16), 256, 0, s>>>(A.touched.as<u32>(), misc, A.best.as<u64>(),
+                                                                            A.hval.as<u32>(), A.flags.as<u8>(),
+                                                                            static_cast<u32>(fcur), A.next.as<u32>(),
+                                                                            A.open.as<u64>());
+                B2_CUDA(cudaGetLastError());
+                A.launches += 6;
+            }
+        }
+        // the ranks' next waves and best goal (global ids: rank << 27 | state)
+        B2_CUDA(cudaMemsetAsync(&misc->nnext_all, 0, 8, s));
+        k_astar_globalize<<<1, 1, 0, s>>>(misc, u64{me} << kRankShift);
+        comm_group_begin();
+        comm_allreduce(comm, &misc->nnext_all, &misc->nnext_all, 1, CommType::U64, CommOp::Sum, s);
+        comm_allreduce(comm, &misc->goal_all, &misc->goal_all, 1, CommType::U64, CommOp::Min, s);
+        comm_group_end();
+        const AstarMisc m = read_misc_sync(A);
+        expanded += nF;
+        generated += Gl;
+        fresh_total += m.nfresh;
+        dead += m.ndead;
+        A.n_states += m.nfresh;
+        nopen = m.nopen;
+        nnext_all = m.nnext_all;
+        if (m.goal_all != ~u64{0} && (m.goal_all >> 32) <= fcur)
+        {
+            A.solved = true;
+            A.cost = m.goal_all >> 32;
+            break;
+        }
+        if (nnext_all > 0)
+        {
+            A.front.swap(A.next);
+            nF = m.nnext;
+            continue;
+        }
+        // the current f is done everywhere: the smallest f of the ranks' open lists is next
+        B2_CUDA(cudaMemsetAsync(&misc->fmin, 0xFF, 8, s));
+        if (nopen)
+            k_astar_fmin<<<grid_for(nopen, 256, sms * 16), 256, 0, s>>>(A.open.as<u64>(), nopen, A.best.as<u64>(),
+                                                                          A.hval.as<u32>(), A.flags.as<u8>(), misc);
+        comm_allreduce(comm, &misc->fmin, &misc->fmin, 1, CommType::U64, CommOp::Min, s);
+        ++A.launches;
+        const u64 fmin = read_misc_sync(A).fmin;
+        if (fmin == ~u64{0})
+        {
+            exhausted = true;
+            break;
+        }
+        if (m.goal_all != ~u64{0} && (m.goal_all >> 32) <= fmin)
+        {
+            A.solved = true;
+            A.cost = m.goal_all >> 32;
+            break;
+        }
+        fcur = fmin;
+        ++f_layers;
+        ensure_front(A, nopen);
+        B2_CUDA(cudaMemsetAsync(&misc->nkeep, 0, 16, s));
+        if (nopen)
+        {
+            k_astar_extract<<<grid_for(nopen, 256, sms * 16), 256, 0, s>>>(A.open.as<u64>(), nopen, A.best.as<u64>(),
+                                                                             A.hval.as<u32>(), A.flags.as<u8>(), fmin,
+                                                                             A.front.as<u32>(), A.keep.as<u64>(), misc);
+            B2_CUDA(cudaGetLastError());
+            ++A.launches;
+        }
+        const AstarMisc m4 = read_misc_sync(A);
+        if (nopen)
+            A.open.swap(A.keep);
+        nopen = m4.nkeep;
+        nF = m4.nfront;
+        A.misc_host->nopen = nopen;
+        B2_CUDA(cudaMemcpyAsync(&misc->nopen, &A.misc_host->nopen, 8, cudaMemcpyHostToDevice, s));
+    }
+    // the search's counters over all ranks
+    A.misc_host->stats[0] = expanded;
+    A.misc_host->stats[1] = generated;
+    A.misc_host->stats[2] = A.n_states;
+    A.misc_host->stats[3] = fresh_total;
+    A.misc_host->stats[4] = dead;
+    B2_CUDA(cudaMemcpyAsync(misc->stats, A.misc_host->stats, 5 * 8, cudaMemcpyHostToDevice, s));
+    comm_allreduce(comm, misc->stats, misc->stats, 5, CommType::U64, CommOp::Sum, s);
+    const AstarMisc mt = read_misc_sync(A);
+    R.status = A.solved ? B2_SEARCH_SOLVED
+                        : dead_start ? B2_SEARCH_UNSOLVABLE : exhausted ? B2_SEARCH_EXHAUSTED : B2_SEARCH_OUT_OF_STATES;
+    R.cost = A.solved ? static_cast<double>(A.cost) : 0.0;
+    R.expanded = mt.stats[0];
+    R.generated = mt.stats[1];
+    R.states = mt.stats[2];
+    R.evaluations += mt.stats[3];
+    R.dead_ends += mt.stats[4];
+    R.waves = wave;
+    R.f_layers = f_layers;
+    R.plan_length = A.solved ? static_cast<u32>(A.cost) : 0;
+    R.kernel_launches = A.launches;
+    R.search_s = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+}
+
 }  // namespace
 
 extern "C" {
@@ -1071,6 +1429,12 @@ b2_status b2_astar_create(b2_task* task, const b2_astar_options* options, b2_ast
             A->own_stream = true;
         }
         A->hist.alloc(64, A->stream);
+        if (options->comm)
+        {
+            if (options->comm->device != task->ctx->device)
+                throw std::invalid_argument("b2_astar_create: the communicator belongs to another device");
+            A->comm = options->comm;
+        }
         *out = A.release();
     });
 }
@@ -1085,7 +1449,10 @@ b2_status b2_astar_run(b2_astar* A, b2_astar_result* result)
         A->ran = true;
         B2_CUDA(cudaSetDevice(A->task->ctx->device));
         *result = b2_astar_result{};
-        run_astar(*A, *result);
+        if (A->comm)
+            run_astar_sharded(*A, *result);
+        else
+            run_astar(*A, *result);
     });
 }
 
@@ -1096,6 +1463,8 @@ b2_status b2_astar_plan(b2_astar* A, uint32_t* parent, uint32_t* index, uint32_t
             throw std::invalid_argument("b2_astar_plan: bad argument");
         if (!A->solved)
             throw std::invalid_argument("b2_astar_plan: the search found no plan");
+        if (A->comm)
+            throw Error(B2_UNSUPPORTED, "b2_astar_plan: a sharded search keeps no plan");
         const u32 n = static_cast<u32>(A->cost);
         *len = n;
         if (cap < n || !n)
@@ -1127,8 +1496,9 @@ void b2_astar_destroy(b2_astar* A)
         return;
     cudaSetDevice(A->task->ctx->device);
     for (DeviceBuffer* b : {&A->rows, &A->hash, &A->best, &A->hval, &A->flags, &A->stamp, &A->table, &A->counts,
-                            &A->cand_base, &A->iota, &A->sums, &A->staging, &A->best_rec, &A->slot_of, &A->claimed,
-                            &A->touched, &A->fresh, &A->front, &A->next, &A->open, &A->keep, &A->misc, &A->hist, &A->bounds})
+                            &A->cand_base, &A->keyb, &A->iota, &A->sums, &A->staging, &A->best_rec, &A->slot_of, &A->claimed,
+                            &A->touched, &A->fresh, &A->front, &A->next, &A->open, &A->keep, &A->misc, &A->hist, &A->bounds,
+                            &A->hist_m, &A->sstage})
         b->reset();
     if (A->stream)
     {

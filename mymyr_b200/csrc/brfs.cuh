@@ -104,6 +104,80 @@ __global__ void __launch_bounds__(128) k_dexpand(DevTask T, dev::DExpandArgs a)
             atomicAdd(reinterpret_cast<unsigned long long*>(a.hist + d), static_cast<unsigned long long>(hist[d]));
 }
 
+constexpr unsigned kPushThreads = 256;
+constexpr u32 kPushSmemWords = 5120;  // 40 KB of staged records per block (with the static arrays, under 48 KB)
+
+/// The exchange: each block loads a tile of staged records, orders it by owner rank in shared memory, reserves each
+/// owner's run in this rank's region of that owner's receive buffer, and writes the runs with consecutive threads on
+/// consecutive words (coalesced stores over NVLink for the other ranks). This rank's region of owner d starts after
+/// the records of ranks < this one for d (M[s][d]: records of rank s for owner d, all-gathered).
+__global__ void __launch_bounds__(kPushThreads) k_push(const u64* __restrict__ staging, const u64* __restrict__ M,
+                                                       u64* const* __restrict__ peers, unsigned long long* cursor,
+                                                       u32 me, u32 world, u32 RW, u32 tile)
+{
+    extern __shared__ u64 sm[];
+    __shared__ u32 cnt[dev::kMaxWorld], start[dev::kMaxWorld];
+    __shared__ u64 off[dev::kMaxWorld], base[dev::kMaxWorld];
+    __shared__ unsigned short order[kPushThreads];
+    __shared__ u8 dst[kPushThreads];
+    u64 n = 0;
+    for (u32 d = 0; d < world; ++d)
+        n += M[me * world + d];
+    for (u32 d = threadIdx.x; d < world; d += blockDim.x)
+    {
+        u64 o = 0;
+        for (u32 s = 0; s < me; ++s)
+            o += M[s * world + d];
+        off[d] = o;
+    }
+    for (u64 t0 = blockIdx.x * static_cast<u64>(tile); t0 < n; t0 += static_cast<u64>(gridDim.x) * tile)
+    {
+        const u32 m = static_cast<u32>(n - t0 < tile ? n - t0 : tile);
+        for (u32 d = threadIdx.x; d < world; d += blockDim.x)
+            cnt[d] = 0;
+        const u64* src = staging + t0 * RW;
+        for (u32 q = threadIdx.x; q < m * RW; q += blockDim.x)
+            sm[q] = src[q];
+        __syncthreads();
+        u32 d = 0, p = 0;
+        if (threadIdx.x < m)
+        {
+            d = dev::owner_of(sm[threadIdx.x * RW + RW - 2], world);
+            p = atomicAdd(&cnt[d], 1u);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0)
+        {
+            u32 acc = 0;
+            for (u32 x = 0; x < world; ++x)
+            {
+                start[x] = acc;
+                acc += cnt[x];
+            }
+        }
+        for (u32 x = threadIdx.x; x < world; x += blockDim.x)
+            base[x] = cnt[x] ? atomicAdd(cursor + x, static_cast<unsigned long long>(cnt[x])) : 0;
+        __syncthreads();
+        if (threadIdx.x < m)
+        {
+            order[start[d] + p] = static_cast<unsigned short>(threadIdx.x);
+            dst[threadIdx.x] = static_cast<u8>(d);
+        }
+        __syncthreads();
+        for (u32 q = threadIdx.x; q < m * RW; q += blockDim.x)
+        {
+            const u32 sp = q / RW, w = q - sp * RW;
+            const u32 rec = order[sp], dd = dst[rec];
+            const u64 slot = off[dd] + base[dd] + (sp - start[dd]);
+            peers[dd][slot * RW + w] = sm[rec * RW + w];
+        }
+        __syncthreads();
+    }
+    // the records are visible to every rank before this kernel completes; the ranks' next collective orders them
+    // before the owners' inserts
+    __threadfence_system();
+}
+
 /// Reinserts the states `state_g[0, n)` (arena indices) into an empty table.
 __global__ void k_rehash(u64* __restrict__ table, u64 mask, u32 max_probe, const u32* __restrict__ state_g, u64 n,
                          const u64* __restrict__ hash, u32* status)

@@ -314,10 +314,12 @@ class AstarResult:
 
 def astar(task: Task, ctx: Context | None = None, heuristic="max", *, witness_pruning: bool = False,
           max_expansions: int | None = None, expected_states: int | None = None, timings: bool = False,
-          stream=None, chunk_candidates: int | None = None) -> AstarResult:
+          stream=None, chunk_candidates: int | None = None, comm=None) -> AstarResult:
     """Eager A* with h^max and unit costs on the device (mymyr.cuda.astar / search::astar_eager): the optimal plan
     cost. ``heuristic`` is "max" or a ``Heuristic`` of the same task (to share its grounding). ``chunk_candidates``
-    bounds the successors staged at once (an f layer with more is expanded in chunks; default 2^26)."""
+    bounds the successors staged at once (an f layer with more is expanded in chunks; default 2^26). ``comm`` (a
+    ``mymyr_b200.dist.Communicator``) partitions the states over its ranks by state-hash owner: every rank calls astar
+    together and gets the same result (no plan)."""
     if ctx is not None and task.ctx is not None and ctx.device != task.ctx.device:
         raise ValueError("mymyr_b200 astar: the task lives on another device than ctx")
     o = _lib.AstarOptions()
@@ -332,6 +334,8 @@ def astar(task: Task, ctx: Context | None = None, heuristic="max", *, witness_pr
         o.stream = stream
     if chunk_candidates is not None:
         o.chunk_candidates = int(chunk_candidates)
+    if comm is not None:
+        o.comm = comm.handle
     if isinstance(heuristic, Heuristic):
         o.heuristic = heuristic.handle
     elif heuristic != "max":
@@ -349,4 +353,4 @@ def astar(task: Task, ctx: Context | None = None, heuristic="max", *, witness_pr
     return AstarResult(status=ASTAR_STATUS.get(r.status, str(r.status)), cost=r.cost, plan_length=r.plan_length,
                        expanded=r.expanded, generated=r.generated, states=r.states, evaluations=r.evaluations,
                        dead_ends=r.dead_ends, initial_h=r.initial_h, waves=r.waves, f_layers=r.f_layers,
-                       search_s=r.search_s, stats=stats, _search=h, _owners=(task, heuristic))
+                       search_s=r.search_s, stats=stats, _search=h, _owners=(task, heuristic, comm))

@@ -108,3 +108,62 @@ def test_sharded_brfs_matches_reference(ref, world, matcher):
             np.testing.assert_array_equal(got["index"], idx, err_msg=name)
             assert [int(h) for h in got["hashes"]] == [oref.hash_state(r) for r in rows], name
             assert sum(p[1] for p in per_rank) > 0, name  # successors crossed between ranks
+
+
+ASTAR_CASES = [
+    ("tower5", tasks.tower(5, 3)),
+    ("tile3x3", tasks.sliding_tile(3, 3, 30, 0)),
+    ("logistics_small", tasks.logistics(3, 3, 2, 1, 3, 5)),
+    ("logistics_2pk", tasks.logistics(8, 4, 6, 2, 2, 0)),
+]
+
+
+def _astar_worker(rank, world, port, matcher, out):
+    import torch.distributed as td
+
+    from mymyr_b200 import Context, Task, cuda
+    from mymyr_b200 import dist as bdist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    td.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                          timeout=datetime.timedelta(seconds=120))
+    try:
+        ctx = Context(rank)
+        comm = bdist.Communicator(ctx, timeout_s=60)
+        for name, text in ASTAR_CASES:
+            task = Task.from_text(text, ctx, matcher=matcher)
+            r = cuda.astar(task, comm=comm)
+            out[(name, rank)] = (r.status, r.cost, r.expanded, r.generated, r.states)
+            r.close()
+        comm.close()
+        td.barrier()
+    finally:
+        td.destroy_process_group()
+
+
+@pytest.mark.parametrize("matcher", ["compiled", "interpreted"])
+@pytest.mark.parametrize("world", _worlds())
+def test_sharded_astar_optimal_cost(ref, world, matcher):
+    """A* with its states partitioned by state-hash owner finds the reference's optimal cost; every rank reports the
+    same result, and it expands exactly the states of the one-GPU search (the same f layers)."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+
+    from mymyr_b200 import Task, cuda
+
+    mgr = mp.get_context("spawn").Manager()
+    out = mgr.dict()
+    mp.start_processes(_astar_worker, args=(world, _free_port(), matcher, out), nprocs=world, join=True,
+                       start_method="spawn")
+    for name, text in ASTAR_CASES:
+        per_rank = [out[(name, r)] for r in range(world)]
+        assert len(set(per_rank)) == 1, (name, per_rank)
+        status, cost, expanded, generated, states = per_rank[0]
+        exp = ref.RefTask(text).astar()
+        assert status == "solved" and cost == exp["cost"], (name, cost, exp["cost"])
+        one = cuda.astar(Task.from_text(text, matcher=matcher))
+        assert (expanded, generated, states) == (one.expanded, one.generated, one.states), name
+        one.close()
