@@ -239,10 +239,11 @@ def env_secondary(args, device, world=1, rank=0, pg=None):
             "parallelism": f"env ids sharded over {world} GPUs" if world > 1 else "single"}
 
 
-def astar_secondary(args, device, with_cpu: bool):
+def astar_secondary(args, device, with_cpu: bool, comm=None, pg=None):
     """A* with h^max on config [5] (logistics, 8 cities x 4 locations, 6 trucks, 2 airplanes, 2 packages): the time
-    to the optimal plan and the expansions/s, on one GPU (device events around each search), next to the reference's
-    CPU A* (search::astar_eager, one thread: it has no thread option) on the same task."""
+    to the optimal plan and the expansions/s (device events around each search; at N > 1 the states are partitioned
+    over the ranks by state-hash owner and the time is the slowest rank's), next to the reference's CPU A*
+    (search::astar_eager, one thread: it has no thread option) on the same task."""
     import torch
 
     from mymyr_b200 import cuda as b2cuda
@@ -251,26 +252,35 @@ def astar_secondary(args, device, with_cpu: bool):
 
     cfg = (8, 4, 6, 2, 2, 0)
     text = tasks.logistics(*cfg)
-    t = Task.from_text(text)
+    from mymyr_b200.task import default_context
+
+    t = Task.from_text(text, default_context(device.index))
     H = b2cuda.Heuristic(t)
     stream = torch.cuda.Stream(device)
-    r = b2cuda.astar(t, heuristic=H, stream=stream.cuda_stream)
+    r = b2cuda.astar(t, heuristic=H, stream=stream.cuda_stream, comm=comm)
     expected = r.states
     r.close()
     runs = []
     for _ in range(3):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
-        r = b2cuda.astar(t, heuristic=H, stream=stream.cuda_stream, expected_states=expected, timings=True)
+        r = b2cuda.astar(t, heuristic=H, stream=stream.cuda_stream, expected_states=expected, timings=True,
+                         comm=comm)
         b.record(stream)
         stream.synchronize()
-        runs.append((a.elapsed_time(b), r.expanded, r.generated, r.cost, r.stats))
+        runs.append((a.elapsed_time(b), r.expanded, r.generated, r.cost, r.stats, r.search_s))
         r.close()
     ms = statistics.median(x[0] for x in runs)
+    if pg is not None:
+        x = torch.tensor([ms], dtype=torch.float64, device=device)
+        pg.all_reduce(x, op=pg.ReduceOp.MAX)
+        ms = float(x.item())
     out = {"metric": "A* expansions/sec (h^max, logistics 8x4 cities/locations, 6 trucks, 2 airplanes, 2 packages)",
            "value": runs[-1][1] / (ms / 1000.0), "unit": "expansions/s", "ms_per_search": ms,
            "cost": runs[-1][3], "expanded": runs[-1][1], "generated": runs[-1][2],
            "phases_ms": {k: runs[-1][4][k] for k in ("count_ms", "expand_ms", "eval_ms")},
+           "host_ms_per_search": statistics.median(x[5] for x in runs) * 1000,
+           "parallelism": f"states sharded by hash owner over {comm.world} GPUs" if comm is not None else "single",
            "note": "each device step expands a whole f layer, so it expands more states than the one-at-a-time "
                    "reference; the time to the optimal plan compares the two"}
     if with_cpu:
@@ -304,8 +314,16 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
         pg = dist
     if args.leg != "all":
-        out = astar_secondary(args, device, with_cpu=False) if args.leg == "astar" else \
+        leg_comm = None
+        if world > 1 and args.leg == "astar":
+            from mymyr_b200.dist import Communicator
+            from mymyr_b200.task import default_context
+
+            leg_comm = Communicator(default_context(local))
+        out = astar_secondary(args, device, with_cpu=False, comm=leg_comm, pg=pg) if args.leg == "astar" else \
             env_secondary(args, device, world, rank, pg)
+        if leg_comm is not None:
+            leg_comm.close()
         if rank == 0:
             print(json.dumps(out), flush=True)
         if pg is not None:
@@ -410,7 +428,7 @@ def main():
     e2e_value = expanded * args.steps / e2e_s
 
     secondary = None if args.no_secondary else env_secondary(args, device, world, rank, pg)
-    astar_line = None if (args.no_astar or rank != 0) else astar_secondary(args, device, with_cpu=world == 1)
+    astar_line = None if args.no_astar else astar_secondary(args, device, with_cpu=world == 1, comm=comm, pg=pg)
     base = cpu_baseline() if rank == 0 and world == 1 else None
     if rank == 0:
         line = {
