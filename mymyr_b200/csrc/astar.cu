@@ -461,6 +461,19 @@ __global__ void k_iota(u32* p, u64 n)
 
 using namespace b2;
 
+namespace b2
+{
+constexpr int kAstarBuffers = 27, kAstarCaps = 6;
+/// An A* search's device buffers, kept by a shared heuristic between the searches that use it (one at a time): a
+/// search grows its buffers to its waves, and the next search reuses them instead of allocating gigabytes again.
+struct AstarCache
+{
+    DeviceBuffer bufs[kAstarBuffers];
+    u64 caps[kAstarCaps] = {};
+    bool busy = false;
+};
+}  // namespace b2
+
 struct b2_heuristic
 {
     b2_task* task = nullptr;
@@ -468,6 +481,7 @@ struct b2_heuristic
     DeviceBuffer blob;  // u32: pre_begin | pre | add_begin | add | goal
     DeviceBuffer goal_masks;  // u64: goal_pos | goal_neg
     HmaxArgs args{};
+    AstarCache cache;
 };
 
 namespace
@@ -565,6 +579,15 @@ struct b2_astar
     b2_comm* comm = nullptr;  // sharded search
     DeviceBuffer hist_m;      // sharded: per-owner counts and their all-gather [world + world * world]
     DeviceBuffer sstage;      // sharded: this rank's staged records before the push
+    bool borrowed = false;    // the buffers came from the shared heuristic's cache and go back to it
+
+    std::array<DeviceBuffer*, kAstarBuffers> buffers()
+    {
+        return {&rows, &hash, &best, &hval, &flags, &stamp, &table, &counts, &cand_base, &keyb, &iota, &sums,
+                &staging, &best_rec, &slot_of, &claimed, &touched, &fresh, &bounds, &front, &next, &open, &keep,
+                &misc, &hist, &hist_m, &sstage};
+    }
+    std::array<u64*, kAstarCaps> caps() { return {&cap_states, &table_slots, &cap_front, &cap_iota, &cap_wave, &cap_open}; }
 };
 
 namespace
@@ -730,6 +753,8 @@ void run_astar(b2_astar& A, b2_astar_result& R)
     }
     const u64 expect = std::max<u64>(A.opt.expected_states, 4096);
     const u64 chunk = A.opt.chunk_candidates ? std::max<u64>(A.opt.chunk_candidates, u64{1} << 16) : u64{1} << 26;
+    if (A.table_slots)  // reused buffers: an empty table
+        B2_CUDA(cudaMemsetAsync(A.table.p, 0xFF, A.table_slots * 8, s));
     ensure_states(A, expect);
     A.misc.alloc(sizeof(AstarMisc), s);
     static_assert(sizeof(AstarMisc) <= PinnedPool::kBlock);
@@ -1046,6 +1071,8 @@ void run_astar_sharded(b2_astar& A, b2_astar_result& R)
         return;
     }
     const u64 expect = std::max<u64>(A.opt.expected_states / world, 4096);
+    if (A.table_slots)  // reused buffers: an empty table
+        B2_CUDA(cudaMemsetAsync(A.table.p, 0xFF, A.table_slots * 8, s));
     ensure_states(A, expect);
     A.misc.alloc(sizeof(AstarMisc), s);
     A.misc_host = static_cast<AstarMisc*>(task->ctx->pinned.take());
@@ -1387,7 +1414,12 @@ b2_status b2_heuristic_evaluate(b2_heuristic* h, const uint64_t* rows, uint64_t 
     });
 }
 
-void b2_heuristic_destroy(b2_heuristic* h) { delete h; }
+void b2_heuristic_destroy(b2_heuristic* h)
+{
+    if (h && h->task && h->task->ctx)
+        cudaSetDevice(h->task->ctx->device);  // the cached search buffers are this device's
+    delete h;
+}
 
 void b2_astar_options_default(b2_astar_options* o)
 {
@@ -1428,7 +1460,22 @@ b2_status b2_astar_create(b2_task* task, const b2_astar_options* options, b2_ast
             B2_CUDA(cudaStreamCreateWithFlags(&A->stream, cudaStreamNonBlocking));
             A->own_stream = true;
         }
-        A->hist.alloc(64, A->stream);
+        if (options->heuristic && !options->heuristic->cache.busy)
+        {
+            // reuse the buffers the heuristic's previous search left (their contents are stale: the search clears
+            // what it reads)
+            AstarCache& c = options->heuristic->cache;
+            auto bufs = A->buffers();
+            auto caps = A->caps();
+            for (int i = 0; i < kAstarBuffers; ++i)
+                bufs[i]->swap(c.bufs[i]);
+            for (int i = 0; i < kAstarCaps; ++i)
+                *caps[i] = c.caps[i];
+            c.busy = true;
+            A->borrowed = true;
+        }
+        if (A->hist.bytes < 64)
+            A->hist.alloc(64, A->stream);
         if (options->comm)
         {
             if (options->comm->device != task->ctx->device)
@@ -1495,10 +1542,25 @@ void b2_astar_destroy(b2_astar* A)
     if (!A)
         return;
     cudaSetDevice(A->task->ctx->device);
-    for (DeviceBuffer* b : {&A->rows, &A->hash, &A->best, &A->hval, &A->flags, &A->stamp, &A->table, &A->counts,
-                            &A->cand_base, &A->keyb, &A->iota, &A->sums, &A->staging, &A->best_rec, &A->slot_of, &A->claimed,
-                            &A->touched, &A->fresh, &A->front, &A->next, &A->open, &A->keep, &A->misc, &A->hist, &A->bounds,
-                            &A->hist_m, &A->sstage})
+    if (A->borrowed)
+    {
+        // the buffers go back to the heuristic's cache, usable from any stream once this search's work is done
+        // (a later release frees them on the default stream)
+        if (A->stream)
+            stream_drain(A->stream);
+        AstarCache& c = A->H->cache;
+        auto bufs = A->buffers();
+        auto caps = A->caps();
+        for (int i = 0; i < kAstarBuffers; ++i)
+        {
+            bufs[i]->stream = nullptr;
+            bufs[i]->swap(c.bufs[i]);
+        }
+        for (int i = 0; i < kAstarCaps; ++i)
+            c.caps[i] = *caps[i];
+        c.busy = false;
+    }
+    for (DeviceBuffer* b : A->buffers())
         b->reset();
     if (A->stream)
     {

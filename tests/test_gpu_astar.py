@@ -131,3 +131,19 @@ def test_astar_shared_heuristic(ref):
     r2 = b2cuda.astar(t)
     assert r1.cost == r2.cost == ref.RefTask(text).astar()["cost"]
     assert r1.expanded == r2.expanded
+
+
+def test_astar_reuses_heuristic_buffers(ref):
+    """Searches sharing a heuristic reuse its cached device buffers (the table, states and wave scratch of the previous
+    search): every search reproduces the first one exactly, with and without chunked waves in between."""
+    text = tasks.logistics(8, 4, 6, 2, 2, 0)
+    t = Task.from_text(text)
+    H = b2cuda.Heuristic(t)
+    runs = []
+    for chunk in (None, None, 1 << 16, None):
+        r = b2cuda.astar(t, heuristic=H, chunk_candidates=chunk)
+        runs.append((r.status, r.cost, r.expanded, r.generated, r.states, r.dead_ends))
+        if len(runs) == 1:
+            _check_plan(ref.RefTask(text), t, r)
+        r.close()
+    assert len(set(runs)) == 1, runs
