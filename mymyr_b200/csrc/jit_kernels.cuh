@@ -103,8 +103,8 @@ struct QEntry
     u64 g;
     u32 i, k;
 };
-/// Queue entries per warp: about 25 KB per 128-thread block.
-constexpr u32 kQueue = W <= 4 ? 112u : W <= 6 ? 96u : 80u;
+/// Queue entries per warp: about 21 KB per 128-thread block (ten blocks per SM).
+constexpr u32 kQueue = W <= 4 ? 96u : W <= 6 ? 80u : 64u;
 
 /// The expansion with warp-cooperative inserts (rows in registers): each lane runs its parent's matcher and queues
 /// every successor (row, hash, candidate index) in shared memory; after the round all 32 lanes insert the queued
@@ -459,8 +459,8 @@ B2_DI void expand_write(const ExpandArgs& a)
 
 extern "C" __global__ void __launch_bounds__(128) b2j_brfs_count_w(b2::dev::BrfsArgs a) { b2::gen::brfs_count<0>(a); }
 extern "C" __global__ void __launch_bounds__(128) b2j_brfs_count_nw(b2::dev::BrfsArgs a) { b2::gen::brfs_count<1>(a); }
-extern "C" __global__ void __launch_bounds__(128) b2j_brfs_expand_w(b2::dev::BrfsArgs a) { b2::gen::brfs_expand<0>(a); }
-extern "C" __global__ void __launch_bounds__(128) b2j_brfs_expand_nw(b2::dev::BrfsArgs a) { b2::gen::brfs_expand<1>(a); }
+extern "C" __global__ void __launch_bounds__(128, 10) b2j_brfs_expand_w(b2::dev::BrfsArgs a) { b2::gen::brfs_expand<0>(a); }
+extern "C" __global__ void __launch_bounds__(128, 10) b2j_brfs_expand_nw(b2::dev::BrfsArgs a) { b2::gen::brfs_expand<1>(a); }
 extern "C" __global__ void __launch_bounds__(128) b2j_dbrfs_expand_w(b2::dev::DExpandArgs a) { b2::gen::dbrfs_expand<0>(a); }
 extern "C" __global__ void __launch_bounds__(128) b2j_dbrfs_expand_nw(b2::dev::DExpandArgs a) { b2::gen::dbrfs_expand<1>(a); }
 extern "C" __global__ void b2j_env_init_w(b2::dev::EnvArgs a) { b2::gen::env_init<0>(a); }
