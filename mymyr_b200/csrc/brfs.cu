@@ -135,6 +135,9 @@ __global__ void k_count_goals(DevTask T, const u64* __restrict__ rows, u32 W, co
             atomicAdd(out, 1u);
 }
 
+/// Resets a layer's counters (its slot of the two that alternate between layers).
+__global__ void k_layer_init(LayerMisc* m) { *m = LayerMisc{0, 0, 0, 0, 0xFFFFFFFFu, 0, 0}; }
+
 __global__ void k_seed_root(Store S, u32* state_g)
 {
     const GlobalRow r{S.rows, S.W};
@@ -238,6 +241,9 @@ using namespace b2;
 
 namespace
 {
+/// Layer counters: two slots, so that the next layer's count can run before the host reads this layer's.
+LayerMisc* misc_at(b2_brfs& B, unsigned slot) { return B.misc.as<LayerMisc>() + slot; }
+
 void ensure_cand(b2_brfs& B, u64 need, u64 used)
 {
     if (need <= B.cap_cand)
@@ -294,7 +300,7 @@ void ensure_table(b2_brfs& B, u64 states)
     B2_CUDA(cudaMemsetAsync(B.table.p, 0xFF, slots * 8, B.stream));
     if (B.n_states)
     {
-        LayerMisc* misc = B.misc.as<LayerMisc>();
+        LayerMisc* misc = misc_at(B, B.slot);
         k_rehash<<<grid_for(B.n_states, 256), 256, 0, B.stream>>>(B.table.as<u64>(), slots - 1, max_probe(slots),
                                                                     B.state_g.as<u32>(), B.n_states, B.hash.as<u64>(),
                                                                     &misc->status);
@@ -318,22 +324,28 @@ Store make_store(b2_brfs& B, u64 layer_cand_begin)
     S.claimed = B.flags.as<u8>();
     S.lost = B.flags.as<u8>() + B.cap_flags;
     S.layer_cand_begin = layer_cand_begin;
-    S.status = &B.misc.as<LayerMisc>()->status;
+    S.status = &misc_at(B, B.slot)->status;
     S.deferred = B.deferred.as<u64>();
-    S.ndeferred = &B.misc.as<LayerMisc>()->ndeferred;
+    S.ndeferred = &misc_at(B, B.slot)->ndeferred;
     return S;
 }
 
-LayerMisc read_misc(b2_brfs& B)
+/// Waits for the stream and reads both counter slots: returns the current layer's, the other one into *other.
+LayerMisc read_misc(b2_brfs& B, LayerMisc* other = nullptr)
 {
-    B2_CUDA(cudaMemcpyAsync(B.misc_host, B.misc.p, sizeof(LayerMisc), cudaMemcpyDeviceToHost, B.stream));
+    B2_CUDA(cudaMemcpyAsync(B.misc_host, B.misc.p, 2 * sizeof(LayerMisc), cudaMemcpyDeviceToHost, B.stream));
     stream_wait(B.stream);
-    const LayerMisc m = *B.misc_host;
-    if (m.status & kStatusProbeLimit)
-        throw Error(B2_DEVICE_FAULT, "b2_brfs: a hash-set probe ran past its bound");
-    if (m.status)
-        throw Error(B2_DEVICE_FAULT, "b2_brfs: device status " + std::to_string(m.status));
-    return m;
+    for (int k = 0; k < 2; ++k)
+    {
+        const u32 st = B.misc_host[k].status;
+        if (st & kStatusProbeLimit)
+            throw Error(B2_DEVICE_FAULT, "b2_brfs: a hash-set probe ran past its bound");
+        if (st)
+            throw Error(B2_DEVICE_FAULT, "b2_brfs: device status " + std::to_string(st));
+    }
+    if (other)
+        *other = B.misc_host[B.slot ^ 1];
+    return B.misc_host[B.slot];
 }
 
 void run_search(b2_brfs& B, b2_brfs_result& R)
@@ -372,11 +384,12 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
     ensure_states(B, expect);
     if (o.expected_states)
         ensure_layer(B, expect / 2, expect);  // a layer holds at most the states, and about twice as many candidates
-    B.misc.alloc(sizeof(LayerMisc), s);
-    static_assert(sizeof(LayerMisc) <= PinnedPool::kBlock);
+    B.misc.alloc(2 * sizeof(LayerMisc), s);
+    static_assert(2 * sizeof(LayerMisc) <= PinnedPool::kBlock);
     if (!B.misc_host)
         B.misc_host = static_cast<LayerMisc*>(B.task->ctx->pinned.take());
-    B2_CUDA(cudaMemsetAsync(B.misc.p, 0, sizeof(LayerMisc), s));
+    B2_CUDA(cudaMemsetAsync(B.misc.p, 0, 2 * sizeof(LayerMisc), s));
+    B.slot = 0;
     ensure_table(B, expect);
     B2_CUDA(cudaMemcpyAsync(B.rows.p, P.initial.data(), W * 8, cudaMemcpyHostToDevice, s));
     k_seed_root<<<1, 1, 0, s>>>(make_store(B, 0), B.state_g.as<u32>());
@@ -391,6 +404,45 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
     u64 expanded = 0, generated = 0, goals = 0, goal_id = 0, fingerprint = 0;
     double count_ms = 0, gen_ms = 0, dedup_ms = 0;
     std::vector<std::array<u64, 3>> counts;
+    // The count pass of a layer: successors per parent, their offsets and total, goals among the parents, into the
+    // counter slot `misc`. The parents are E, or, when E_dev is non-null, a count still on the device that is at most
+    // E_max (the next layer's, launched before the host has read it).
+    const auto launch_count = [&](const u32* frontier, u64 E, const u64* E_dev, u64 E_max, LayerMisc* misc,
+                                  u64 cand_begin) {
+        const unsigned grid = grid_for(E_max, 128, static_cast<unsigned>(B.task->ctx->sms) * 64);
+        k_layer_init<<<1, 1, 0, s>>>(misc);
+        if (o.timings)
+            B2_CUDA(cudaEventRecord(ev[0], s));
+        if (B.task->jit)
+        {
+            dev::BrfsArgs a{};
+            a.frontier = frontier;
+            a.E = E;
+            a.E_dev = E_dev;
+            a.counts = B.counts.as<u32>();
+            a.misc = misc;
+            a.S = make_store(B, cand_begin);
+            a.pi = pi;
+            jit_launch(B.task->jit->brfs_count[pi], grid, 128, &a, s);
+        }
+        else
+            dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
+                k_count<OW, WR><<<grid, 128, 0, s>>>(T, pi, B.rows.as<u64>(), W, frontier, E, B.counts.as<u32>(), misc,
+                                                     E_dev);
+            });
+        if (E_dev)
+            device_scan_dev(CountIn{B.counts.as<u32>()}, BaseOut{B.cand_base.as<u64>()}, E_dev, E_max,
+                            &misc->total_cand, B.sums.as<u64>(), s);
+        else
+            device_scan(CountIn{B.counts.as<u32>()}, BaseOut{B.cand_base.as<u64>()}, E, &misc->total_cand,
+                        B.sums.as<u64>(), s);
+        B2_CUDA(cudaGetLastError());
+        B.launches += 5;
+        if (o.timings)
+            B2_CUDA(cudaEventRecord(ev[1], s));
+    };
+    bool counted = false;  // this layer's count already ran (launched with the previous layer), its counters in `next`
+    LayerMisc next{};
     for (;;)
     {
         const u64 E = layer_end - layer_begin;
@@ -407,34 +459,23 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
             break;
         }
         ++layers;
-        ensure_layer(B, E, 0);
-        LayerMisc* misc = B.misc.as<LayerMisc>();
-        *B.misc_host = LayerMisc{0, 0, 0, 0, 0xFFFFFFFFu, 0, 0};
-        B2_CUDA(cudaMemcpyAsync(misc, B.misc_host, sizeof(LayerMisc), cudaMemcpyHostToDevice, s));
-        const u32* frontier = B.state_g.as<u32>() + layer_begin;
-        const unsigned grid = grid_for(E, 128, static_cast<unsigned>(B.task->ctx->sms) * 64);
-        if (o.timings)
-            B2_CUDA(cudaEventRecord(ev[0], s));
-        if (B.task->jit)
-        {
-            dev::BrfsArgs a{};
-            a.frontier = frontier;
-            a.E = E;
-            a.counts = B.counts.as<u32>();
-            a.misc = misc;
-            a.S = make_store(B, cand_next);
-            a.pi = pi;
-            jit_launch(B.task->jit->brfs_count[pi], grid, 128, &a, s);
-        }
+        LayerMisc* misc = misc_at(B, B.slot);
+        LayerMisc m;
+        if (counted)
+            m = next;
         else
-            dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
-                k_count<OW, WR><<<grid, 128, 0, s>>>(T, pi, B.rows.as<u64>(), W, frontier, E, B.counts.as<u32>(), misc);
-            });
-        device_scan(CountIn{B.counts.as<u32>()}, BaseOut{B.cand_base.as<u64>()}, E, &misc->total_cand, B.sums.as<u64>(), s);
-        B.launches += 4;
+        {
+            ensure_layer(B, E, 0);
+            launch_count(B.state_g.as<u32>() + layer_begin, E, nullptr, E, misc, cand_next);
+            m = read_misc(B);
+        }
+        counted = false;
         if (o.timings)
-            B2_CUDA(cudaEventRecord(ev[1], s));
-        LayerMisc m = read_misc(B);
+        {
+            float a = 0;
+            B2_CUDA(cudaEventElapsedTime(&a, ev[0], ev[1]));
+            count_ms += a;
+        }
         u64 E_exp = E, G = m.total_cand;
         bool stop = false;
         const u32 layer_goals = m.goals, first_goal = m.first_goal;
@@ -460,7 +501,7 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
             if (o.timings)
                 B2_CUDA(cudaEventRecord(ev[2], s));
             const Store S = make_store(B, cand_next);
-            frontier = B.state_g.as<u32>() + layer_begin;
+            const u32* frontier = B.state_g.as<u32>() + layer_begin;
             const unsigned grid_e = grid_for(E_exp, 128, static_cast<unsigned>(B.task->ctx->sms) * 64);
             if (B.task->jit)
             {
@@ -487,15 +528,23 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
             B.launches += 4;
             if (o.timings)
                 B2_CUDA(cudaEventRecord(ev[4], s));
-            m = read_misc(B);
+            // The next layer's count, launched now over this layer's new states (at most G, their number still on
+            // the device), so that one wait returns both. Skipped where this layer may be the last: a goal stop, the
+            // depth bound, or a store that this layer can fill (max_states stops inside the layer).
+            if (!stop && layers < o.max_depth && B.n_states + G < o.max_states)
+            {
+                ensure_layer(B, G, 0);
+                launch_count(B.state_g.as<u32>() + B.n_states, 0, &misc->total_new, G, misc_at(B, B.slot ^ 1),
+                             cand_next + G);
+                counted = true;
+            }
+            m = read_misc(B, &next);
             N = m.total_new;
             if (o.timings)
             {
-                float a = 0, b = 0, c = 0;
-                B2_CUDA(cudaEventElapsedTime(&a, ev[0], ev[1]));
+                float b = 0, c = 0;
                 B2_CUDA(cudaEventElapsedTime(&b, ev[2], ev[3]));
                 B2_CUDA(cudaEventElapsedTime(&c, ev[3], ev[4]));
-                count_ms += a;
                 gen_ms += b;
                 dedup_ms += c;
             }
@@ -525,7 +574,6 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
             }
             else
             {
-                LayerMisc* misc = B.misc.as<LayerMisc>();
                 B2_CUDA(cudaMemsetAsync(&misc->goals, 0, 4, s));
                 k_count_goals<<<grid_for(E_exp, 256), 256, 0, s>>>(T, B.rows.as<u64>(), W,
                                                                      B.state_g.as<u32>() + layer_begin, E_exp,
@@ -552,11 +600,13 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
         B.layer_begin.push_back(layer_begin);
         if (stop)
             break;
+        if (counted)
+            B.slot ^= 1;
     }
     B.layer_begin.push_back(B.n_states);
     if (o.fingerprint)
     {
-        u64* acc = &B.misc.as<LayerMisc>()->fingerprint;
+        u64* acc = &misc_at(B, B.slot)->fingerprint;
         B2_CUDA(cudaMemsetAsync(acc, 0, 8, s));
         k_fingerprint<<<grid_for(B.n_states, 256, static_cast<unsigned>(B.task->ctx->sms) * 8), 256, 0, s>>>(
             B.state_g.as<u32>(), 0, B.n_states, B.rows.as<u64>(), W, acc);

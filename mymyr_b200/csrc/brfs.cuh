@@ -18,9 +18,10 @@ using dev::Store;
 
 template<int OW, int WR>
 __global__ void __launch_bounds__(128) k_count(DevTask T, u32 pi, const u64* __restrict__ rows, u32 W,
-                                               const u32* __restrict__ frontier, u64 E, u32* __restrict__ counts,
-                                               LayerMisc* misc)
+                                               const u32* __restrict__ frontier, u64 E_in, u32* __restrict__ counts,
+                                               LayerMisc* misc, const u64* E_dev = nullptr)
 {
+    const u64 E = E_dev ? *E_dev : E_in;  // a non-null E_dev: the parents are a count still on the device
     for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < E; i += static_cast<u64>(gridDim.x) * blockDim.x)
     {
         const u64 g = frontier[i];
@@ -233,7 +234,8 @@ struct b2_brfs
     // per layer scratch
     b2::DeviceBuffer counts, cand_base, flags, deferred, sums, misc;
     b2::u64 cap_layer = 0, cap_flags = 0;
-    b2::dev::LayerMisc* misc_host = nullptr;  // pinned mirror of `misc`
+    b2::dev::LayerMisc* misc_host = nullptr;  // pinned mirror of `misc` (two counter slots)
+    unsigned slot = 0;                         // the current layer's counter slot
     // results
     std::vector<b2::u64> layer_begin;  // id of each layer's first state (+ the end)
     b2::u64 n_states = 0;

@@ -331,6 +331,7 @@ struct BrfsArgs
     LayerMisc* misc;
     Store S;
     u32 pi;               // 0: witness pruning, 1: off
+    const u64* E_dev;     // count pass: when non-null, the parents are *E_dev (a count still on the device), not E
 };
 
 // ------------------------------------------------------------------------------------------------ sharded BrFS

@@ -82,7 +82,8 @@ B2_DI u32 count_all(const Row& st)
 template<int PI>
 B2_DI void brfs_count(const BrfsArgs& a)
 {
-    for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < a.E; i += static_cast<u64>(gridDim.x) * blockDim.x)
+    const u64 E = a.E_dev ? *a.E_dev : a.E;
+    for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < E; i += static_cast<u64>(gridDim.x) * blockDim.x)
     {
         const u64 g = a.frontier[i];
         const Row st = RowSel<WR>::load(a.S.rows + g * W);
