@@ -243,6 +243,8 @@ typedef struct b2_brfs_result {
     uint32_t words;
     uint64_t local_states;     /* out: states this rank stores (all of them on one GPU) */
     uint64_t exchanged;        /* out: successors this rank received from other ranks (sharded search) */
+    double exchange_ms;        /* out: sharded search: device time of the successor exchange (per-owner counts,
+                                  push, barrier; options.timings), part of gen_ms */
 } b2_brfs_result;
 
 b2_status b2_brfs_create(b2_task* task, const b2_brfs_options* options, b2_brfs** out);

@@ -57,7 +57,7 @@ __global__ void __launch_bounds__(128) k_dexpand(DevTask T, dev::DExpandArgs a)
         if (id >= a.limit)
             continue;
         const auto st = load_row<WR>(a.rows + static_cast<u64>(a.frontier[i]) * W, W);
-        const u64 c0 = a.gbase[id - a.layer_begin];
+        const u64 c0 = a.gbase ? a.gbase[id - a.layer_begin] : id << 32;
         u64* out = a.staging + (a.local_base[i] - a.stage_base) * (W + 2);
         u32 k = 0;
         u32 bind[kMaxLevels] = {};
@@ -170,6 +170,73 @@ __global__ void __launch_bounds__(kPushThreads) k_push(const u64* __restrict__ s
             const u32 sp = q / RW, w = q - sp * RW;
             const u32 rec = order[sp], dd = dst[rec];
             const u64 slot = off[dd] + base[dd] + (sp - start[dd]);
+            peers[dd][slot * RW + w] = sm[rec * RW + w];
+        }
+        __syncthreads();
+    }
+    // the records are visible to every rank before this kernel completes; the ranks' next collective orders them
+    // before the owners' inserts
+    __threadfence_system();
+}
+
+/// The exchange without a prior all-gather of the per-owner counts: like k_push, but each block reserves each owner's
+/// run by an atomic on that owner's fill cursor (in the owner's memory, over NVLink for the other ranks), so the
+/// records of all senders interleave in the owner's buffer in an order of no meaning (the records carry their keys).
+/// The staged records are the first sum(hist) of the staging area.
+__global__ void __launch_bounds__(kPushThreads) k_push_reserve(const u64* __restrict__ staging,
+                                                               const u64* __restrict__ hist, u64* const* __restrict__ peers,
+                                                               u64* const* __restrict__ cursors, u32 world, u32 RW,
+                                                               u32 tile)
+{
+    extern __shared__ u64 sm[];
+    __shared__ u32 cnt[dev::kMaxWorld], start[dev::kMaxWorld];
+    __shared__ u64 base[dev::kMaxWorld];
+    __shared__ unsigned short order[kPushThreads];
+    __shared__ u8 dst[kPushThreads];
+    u64 n = 0;
+    for (u32 d = 0; d < world; ++d)
+        n += hist[d];
+    for (u64 t0 = blockIdx.x * static_cast<u64>(tile); t0 < n; t0 += static_cast<u64>(gridDim.x) * tile)
+    {
+        const u32 m = static_cast<u32>(n - t0 < tile ? n - t0 : tile);
+        for (u32 d = threadIdx.x; d < world; d += blockDim.x)
+            cnt[d] = 0;
+        const u64* src = staging + t0 * RW;
+        for (u32 q = threadIdx.x; q < m * RW; q += blockDim.x)
+            sm[q] = src[q];
+        __syncthreads();
+        u32 d = 0, p = 0;
+        if (threadIdx.x < m)
+        {
+            d = dev::owner_of(sm[threadIdx.x * RW + RW - 2], world);
+            p = atomicAdd(&cnt[d], 1u);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0)
+        {
+            u32 acc = 0;
+            for (u32 x = 0; x < world; ++x)
+            {
+                start[x] = acc;
+                acc += cnt[x];
+            }
+        }
+        for (u32 x = threadIdx.x; x < world; x += blockDim.x)
+            base[x] = cnt[x] ? atomicAdd_system(reinterpret_cast<unsigned long long*>(cursors[x]),
+                                                static_cast<unsigned long long>(cnt[x]))
+                             : 0;
+        __syncthreads();
+        if (threadIdx.x < m)
+        {
+            order[start[d] + p] = static_cast<unsigned short>(threadIdx.x);
+            dst[threadIdx.x] = static_cast<u8>(d);
+        }
+        __syncthreads();
+        for (u32 q = threadIdx.x; q < m * RW; q += blockDim.x)
+        {
+            const u32 sp = q / RW, w = q - sp * RW;
+            const u32 rec = order[sp], dd = dst[rec];
+            const u64 slot = base[dd] + (sp - start[dd]);
             peers[dd][slot * RW + w] = sm[rec * RW + w];
         }
         __syncthreads();

@@ -178,7 +178,7 @@ void PeerBuffer::close()
     bytes = 0;
 }
 
-void peer_buffer_exchange(b2_comm* c, PeerBuffer& b, size_t bytes, cudaStream_t s)
+void peer_buffer_exchange(b2_comm* c, PeerBuffer& b, size_t bytes, cudaStream_t s, bool zero)
 {
     const u32 world = c->world, me = c->rank;
     comm_sync(c, s);
@@ -195,6 +195,8 @@ void peer_buffer_exchange(b2_comm* c, PeerBuffer& b, size_t bytes, cudaStream_t 
     comm_allreduce(c, word, word, 1, CommType::U32, CommOp::Sum, s);
     comm_sync(c, s);
     b.local.alloc(bytes);
+    if (zero)
+        B2_CUDA(cudaMemset(b.local.p, 0, bytes));  // complete before the handle allgather below
     cudaIpcMemHandle_t h;
     B2_CUDA(cudaIpcGetMemHandle(&h, b.local.p));
     B2_CUDA(cudaMemcpyAsync(scratch.p, &h, hs, cudaMemcpyHostToDevice, s));
@@ -266,6 +268,7 @@ void b2_comm_destroy(b2_comm* comm)
         return;
     cudaSetDevice(comm->device);
     comm->exchange.close();
+    comm->cursors.close();
     if (comm->nccl)
         nccl().destroy(static_cast<ncclComm_t>(comm->nccl));
     delete comm;

@@ -34,6 +34,9 @@ struct b2_comm
     // the sharded search's receive buffers (one search at a time per communicator); kept between searches so that
     // their IPC mappings are made once, not per search
     b2::PeerBuffer exchange;
+    // per rank one 256-byte block in its own memory, mapped by all: word 0 is the fill cursor of its receive buffer,
+    // advanced by the senders' atomics (zeroed before the mappings are shared)
+    b2::PeerBuffer cursors;
 };
 
 namespace b2
@@ -59,6 +62,7 @@ void comm_group_end();
 /// stopped taking part) the communicator is aborted and an error thrown, so that no rank waits for good.
 void comm_sync(b2_comm* c, cudaStream_t s);
 
-/// Collective: every rank reallocates its buffer to `bytes` and maps the others'.
-void peer_buffer_exchange(b2_comm* c, PeerBuffer& b, size_t bytes, cudaStream_t s);
+/// Collective: every rank reallocates its buffer to `bytes` (zeroed if `zero`, before any rank can reach it) and maps
+/// the others'.
+void peer_buffer_exchange(b2_comm* c, PeerBuffer& b, size_t bytes, cudaStream_t s, bool zero = false);
 }  // namespace b2

@@ -349,12 +349,17 @@ struct DistMisc
     u64 new_packed;   // new states of the layer: all ranks | this rank's << 32
     u64 recv;         // candidates this rank received
     u64 fingerprint;
+    u64 next_all;     // new states of the layer over all ranks (the next layer's parents), unpacked on the device
+    u64 next_local;   // new states of the layer on this rank (its next local parents)
     u32 goals_all;    // goal parents of the layer over all ranks
+    u32 overflow_all; // parents over all ranks whose successor count did not fit the count lanes
     u32 barrier;      // reduced by all ranks between the exchange and the inserts
+    u32 pad;
 };
 
-/// Arguments of the sharded expansion: each local parent's successors are staged as records [row | hash | c], c the
-/// successor's candidate index within the layer in canonical order (parent id, successor index) over all ranks.
+/// Arguments of the sharded expansion: each local parent's successors are staged as records [row | hash | key], key =
+/// the parent's key base + successor index. With gbase null the key base is id << 32, so that keys order successors in
+/// canonical order (parent id, successor index) over all ranks.
 struct DExpandArgs
 {
     const u64* rows;         // the rank's arena rows (parents)
@@ -363,7 +368,7 @@ struct DExpandArgs
     u64 E;                   // local parents
     u64 layer_begin;         // id of the layer's first state
     u64 limit;               // expand the parents with id < limit
-    const u64* gbase;        // [layer states] candidate offset of each parent of the layer (all ranks)
+    const u64* gbase;        // [layer states] key base of each parent of the layer, or null (id << 32)
     const u64* local_base;   // [E] staging record of each local parent's first successor (minus stage_base)
     u64 stage_base;          // subtracted from local_base (a chunk of a larger batch stages from 0)
     u64* staging;            // [local candidates, W + 2]

@@ -7,28 +7,32 @@
 // and node record sit in that rank's arena, its slot in that rank's hash set, and that rank expands it.
 //
 // Per layer (parents: the layer's states, ids [layer_begin, layer_end), each on its owner):
-//   1. count: each rank counts the successors of its parents (and tests the goal); the counts are scattered to a
-//      layer-wide array by parent id and summed over ranks (NCCL all-reduce), whose exclusive scan gives every
-//      successor its candidate index c in canonical order (parent id, successor index) over the whole layer;
-//   2. expand: each rank regenerates its parents' successors into a staging area as records [row | hash | c] and
-//      counts them per owner; the ranks all-gather the per-owner counts, so every rank knows where its records go in
-//      every owner's receive buffer;
+//   1. count: each rank counts the successors of its parents (and tests the goal); the counts go into a layer-wide
+//      array of byte lanes by parent id (each lane written by the parent's owner alone; word lanes for the rest of the
+//      search once a parent has more than 255 successors) and are summed over ranks (NCCL all-reduce), whose
+//      exclusive scan gives every parent the candidate index of its first successor in canonical order;
+//   2. expand: each rank regenerates its parents' successors into a staging area as records [row | hash | key], key =
+//      parent id << 32 | successor index (the canonical order);
 //   3. push: one kernel writes the records straight into the owners' receive buffers in peer memory (NVLink stores
-//      through CUDA IPC mappings; no library copy), then a one-word all-reduce orders the exchange before the inserts;
+//      through CUDA IPC mappings; no library copy), each block reserving its run in an owner's buffer by an atomic on
+//      that owner's fill cursor; then a one-word all-reduce orders the exchange before the inserts;
 //   4. insert: each owner inserts its received records into its hash set: a record that takes an empty slot is a new
-//      state; an equal record of the same layer keeps the smallest c at that slot's entry (atomicMin), an equal state
-//      of an earlier layer drops it. The smallest c of a state is its first discovery in canonical order;
-//   5. ids: each owner flags its new states' c in a layer-wide byte array; the all-reduced flags' exclusive scan gives
-//      every new state its id (the one-GPU id), and the scan of the rank's own flags gives its local order, so each
-//      rank keeps its states in id order. The node record (parent id, successor index) comes from c by a binary search
-//      of the layer's candidate offsets.
+//      state; an equal record of the same layer keeps the smallest key at that slot's entry (atomicMin), an equal
+//      state of an earlier layer drops it. The smallest key of a state is its first discovery in canonical order;
+//   5. ids: each owner sets the bit of its new states' candidate index c (the parent's offset + successor index) in a
+//      layer-wide bitmap; the all-reduced bitmap's exclusive popcount scan gives every new state its id (the one-GPU
+//      id), and the scan of the rank's own bits its local order, so each rank keeps its states in id order. The node
+//      record (parent id, successor index) is the key.
 // Every decision the host takes (stop, capacities, buffer growth) uses values that all ranks share, so the ranks take
-// the same collective steps in the same order.
+// the same collective steps in the same order. The next layer's count (step 1) is launched right after step 5, over
+// parents whose number is still on the device, so that one wait per layer returns both: the counters alternate
+// between two slots.
 
 #include "brfs.cuh"
 
 #include <array>
 #include <chrono>
+#include <cstddef>
 #include <cstring>
 
 namespace b2
@@ -65,40 +69,66 @@ __global__ void k_dseed(u64* __restrict__ rows, u64* __restrict__ hash, u32 W, u
     misc->new_packed = 1 | (u64{1} << 32);
 }
 
-/// The local successor counts into the layer-wide array (by parent id), and the rank's goal count and first goal id.
-__global__ void k_dscatter(const u32* __restrict__ counts, const u32* __restrict__ ids, u64 E, u64 layer_begin,
-                           u32* __restrict__ cg, u64 n_layer, DistMisc* misc)
+/// The local successor counts into the layer-wide lane array (by parent id: bytes for lane 1, words for lane 4), then
+/// the rank's goal parents and its parents whose count does not fit a byte lane (saturated, counted) after the lanes,
+/// and the rank's first goal id. A parent's lane is written by its owner alone, so the all-reduce sums without carries.
+__global__ void k_dscatter(const u32* __restrict__ counts, const u32* __restrict__ ids, u64 E_in, const u64* E_dev,
+                           u64 layer_begin, u32* __restrict__ cg, u64 lane_words, u32 lane, DistMisc* misc)
 {
+    const u64 E = E_dev ? *E_dev : E_in;  // the local parents (a count still on the device when E_dev is set)
+    u32* tail = cg + lane_words;  // [goals, overflow]
     for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < E; i += static_cast<u64>(gridDim.x) * blockDim.x)
-        cg[ids[i] - layer_begin] = counts[i];
+    {
+        const u64 j = ids[i] - layer_begin;
+        const u32 c = counts[i];
+        if (lane == 4)
+            cg[j] = c;
+        else
+        {
+            if (c > 0xFFu)
+                atomicAdd(tail + 1, 1u);
+            reinterpret_cast<u8*>(cg)[j] = static_cast<u8>(c > 0xFFu ? 0xFFu : c);
+        }
+    }
     if (blockIdx.x == 0 && threadIdx.x == 0)
     {
-        cg[n_layer] = misc->lm.goals;
+        tail[0] = misc->lm.goals;
         misc->goal_id = misc->lm.first_goal != 0xFFFFFFFFu ? ids[misc->lm.first_goal] : ~u64{0};
     }
 }
 
+/// The count of parent i from the summed lanes.
+struct LaneIn
+{
+    const u32* cg;
+    u32 lane;
+    __device__ __forceinline__ u32 operator()(u64 i) const
+    {
+        return lane == 4 ? cg[i] : static_cast<u32>(reinterpret_cast<const u8*>(cg)[i]);
+    }
+};
+
 /// The owner's inserts of its received records (all of them in memory before this kernel, so rows are compared in
 /// place with no ordering within the kernel). Table entries are (hash >> 32) << 32 | arena index; the arena index of
-/// received record r is cand_begin + r, and its row stays in the receive buffer during the layer.
-__global__ void k_dinsert(const u64* __restrict__ recv, const u64* __restrict__ M, u32 me, u32 world,
+/// received record r is cand_begin + r, and its row stays in the receive buffer during the layer. gmin[r] ends as the
+/// smallest key of record r's state if r took a slot, and stays all ones otherwise. The received records are the
+/// first *fill of the buffer (its cursor, advanced by all senders).
+__global__ void k_dinsert(const u64* __restrict__ recv, const u64* fill, const u64* __restrict__ hist, u32 me,
                           u64* __restrict__ rows, u64* __restrict__ hash, u64* table, u64 mask, u32 max_probe,
-                          u64 cand_begin, u32 W, u32* gmin, u8* __restrict__ claimed, DistMisc* misc)
+                          u64 cand_begin, u32 W, unsigned long long* gmin, DistMisc* misc)
 {
-    u64 n = 0;
-    for (u32 s = 0; s < world; ++s)
-        n += M[s * world + me];
+    const u64 n = *fill;
     if (blockIdx.x == 0 && threadIdx.x == 0)
     {
         misc->recv = n;
-        misc->lm.ndeferred = static_cast<u32>(n - M[me * world + me]);  // received from other ranks
+        misc->lm.ndeferred = static_cast<u32>(n - hist[me]);  // received from other ranks
     }
     const u32 RW = W + 2;
     for (u64 r = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; r < n; r += static_cast<u64>(gridDim.x) * blockDim.x)
     {
         const u64* rec = recv + r * RW;
         const u64 h = rec[W];
-        const u32 c = static_cast<u32>(rec[W + 1]);
+        const u64 key = rec[W + 1];
         const u64 lc = cand_begin + r;
         const u64 mine = (h & 0xFFFFFFFF00000000ull) | lc;
         u64 j = h & mask;
@@ -115,8 +145,7 @@ __global__ void k_dinsert(const u64* __restrict__ recv, const u64* __restrict__ 
                     for (u32 q = 0; q < W; ++q)
                         dst[q] = rec[q];
                     hash[lc] = h;
-                    claimed[r] = 1;
-                    atomicMin(gmin + r, c);
+                    atomicMin(gmin + r, static_cast<unsigned long long>(key));
                     done = true;
                     break;
                 }
@@ -133,7 +162,7 @@ __global__ void k_dinsert(const u64* __restrict__ recv, const u64* __restrict__ 
             if (!eq)
                 continue;
             if (this_layer)
-                atomicMin(gmin + (o - cand_begin), c);
+                atomicMin(gmin + (o - cand_begin), static_cast<unsigned long long>(key));
             done = true;
             break;
         }
@@ -142,60 +171,79 @@ __global__ void k_dinsert(const u64* __restrict__ recv, const u64* __restrict__ 
     }
 }
 
-/// Flags the candidate index of each new state of this rank (its smallest discovery) and remembers its arena index.
-__global__ void k_dmark(const u64* __restrict__ M, u32 me, u32 world, const u8* __restrict__ claimed,
-                        const u32* __restrict__ gmin, u64 cand_begin, u8* __restrict__ fm, u32* __restrict__ mark)
+/// Sets the bit of the candidate index c of each new state of this rank (its first discovery: parent offset +
+/// successor index) and remembers c. Resets the receive buffer's fill cursor (no sender advances it before the next
+/// layer's collectives, which follow this kernel on this rank).
+__global__ void k_dmark(const DistMisc* misc, u64* fill, const u64* __restrict__ gmin, const u64* __restrict__ gbase,
+                        u64 layer_begin, u32* __restrict__ fm, u32* __restrict__ cw)
 {
-    u64 n = 0;
-    for (u32 s = 0; s < world; ++s)
-        n += M[s * world + me];
+    const u64 n = misc->recv;
+    if (blockIdx.x == 0 && threadIdx.x == 0)
+        *fill = 0;
     for (u64 r = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; r < n; r += static_cast<u64>(gridDim.x) * blockDim.x)
-        if (claimed[r])
-        {
-            const u32 c = gmin[r];
-            fm[c] = 1;
-            mark[c] = static_cast<u32>(cand_begin + r);
-        }
+    {
+        const u64 key = gmin[r];
+        if (key == ~u64{0})
+            continue;
+        const u64 c = gbase[(key >> 32) - layer_begin] + (key & 0xFFFFFFFFull);
+        atomicOr(fm + (c >> 5), 1u << (c & 31));
+        cw[r] = static_cast<u32>(c);
+    }
 }
 
-/// Packed flags of candidate c: new state of any rank (low half) | new state of this rank (high half).
-struct PackIn
+/// Per bitmap word: new states of any rank (low half) | new states of this rank (high half).
+struct WordIn
 {
-    const u8* f;
-    const u8* fm;
-    __device__ __forceinline__ u64 operator()(u64 c) const { return f[c] | (static_cast<u64>(fm[c]) << 32); }
-};
-struct PackOut
-{
-    const u32* mark;
-    const u64* gbase;  // candidate offsets of the layer's expanded parents
-    u64 parents;
-    u64 layer_begin, layer_end, n_local;
-    u32* state_lc;
-    u32* state_id;
-    u32* state_par;
-    u32* state_kid;
-    __device__ __forceinline__ void operator()(u64 c, u64 e, u64 v) const
+    const u32* f;
+    const u32* fm;
+    __device__ __forceinline__ u64 operator()(u64 w) const
     {
-        if (!(v >> 32))
-            return;
-        const u64 lp = n_local + (e >> 32);
-        state_lc[lp] = mark[c];
-        state_id[lp] = static_cast<u32>(layer_end + (e & 0xFFFFFFFFull));
-        // the parent: the last p with gbase[p] <= c (it has successors, since c < gbase[p + 1])
-        u64 lo = 0, hi = parents;
-        while (hi - lo > 1)
-        {
-            const u64 mid = (lo + hi) / 2;
-            if (gbase[mid] <= c)
-                lo = mid;
-            else
-                hi = mid;
-        }
-        state_par[lp] = static_cast<u32>(layer_begin + lo);
-        state_kid[lp] = static_cast<u32>(c - gbase[lo]);
+        return static_cast<u64>(__popc(f[w])) | (static_cast<u64>(__popc(fm[w])) << 32);
     }
 };
+struct WordOut
+{
+    u64* wpre;
+    __device__ __forceinline__ void operator()(u64 w, u64 e, u64) const { wpre[w] = e; }
+};
+
+/// Each new state of this rank: its id (layer_end + the new states of all ranks before its candidate index), its place
+/// in the rank's id-ordered lists (after the rank's states before it), its arena index and node record (the key).
+/// Resets gmin to all ones for the next layer, and unpacks the layer's new-state counts for the next layer's count.
+__global__ void k_dassign(DistMisc* misc, u64* __restrict__ gmin, const u32* __restrict__ cw, const u32* __restrict__ f,
+                          const u32* __restrict__ fm, const u64* __restrict__ wpre, u64 layer_end, u64 n_local,
+                          u64 cand_begin, u32* __restrict__ state_lc, u32* __restrict__ state_id,
+                          u32* __restrict__ state_par, u32* __restrict__ state_kid)
+{
+    const u64 n = misc->recv;
+    if (blockIdx.x == 0 && threadIdx.x == 0)
+    {
+        misc->next_all = misc->new_packed & 0xFFFFFFFFull;
+        misc->next_local = misc->new_packed >> 32;
+    }
+    for (u64 r = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; r < n; r += static_cast<u64>(gridDim.x) * blockDim.x)
+    {
+        const u64 key = gmin[r];
+        if (key == ~u64{0})
+            continue;
+        gmin[r] = ~u64{0};
+        const u32 c = cw[r];
+        const u32 w = c >> 5, below = (1u << (c & 31)) - 1u;
+        const u64 e = wpre[w];
+        const u64 lp = n_local + (e >> 32) + __popc(fm[w] & below);
+        state_lc[lp] = static_cast<u32>(cand_begin + r);
+        state_id[lp] = static_cast<u32>(layer_end + (e & 0xFFFFFFFFull) + __popc(f[w] & below));
+        state_par[lp] = static_cast<u32>(key >> 32);
+        state_kid[lp] = static_cast<u32>(key);
+    }
+}
+
+/// Resets a layer's counter slot.
+__global__ void k_dmisc_init(DistMisc* m)
+{
+    *m = DistMisc{};
+    m->lm.first_goal = 0xFFFFFFFFu;
+}
 
 __global__ void k_dfingerprint(const u32* __restrict__ state_lc, const u32* __restrict__ state_id, u64 n,
                                const u64* __restrict__ rows, u32 W, u64* acc)
@@ -259,20 +307,23 @@ struct ShardState
     // staged records
     DeviceBuffer staging;
     u64 cap_staging = 0;
-    // per candidate of the layer (all ranks): flags, the all-reduced flags, arena index; per received record: its
-    // state's smallest candidate index, whether it took a slot
-    DeviceBuffer fm, f, mark, gmin, claimed;
+    // per candidate of the layer (all ranks), one bit each: this rank's new states, all ranks' (all-reduced); per
+    // bitmap word: the exclusive prefix of both; per received record: its state's smallest key (all ones unless the
+    // record took a slot: kept all ones between layers), its candidate index
+    DeviceBuffer fm, f, wpre, gmin, cw;
     u64 cap_g = 0;
-    DeviceBuffer small;  // hist[world] | M[world, world] | cursor[world] | fingerprints[world]
-    DeviceBuffer misc, sums;
-    DistMisc* misc_host = nullptr;
+    bool gmin_clean = false;  // gmin all ones (false after an interrupted layer)
+    u32 lane = 1;             // bytes per count lane (1, or 4 once a parent had more than 255 successors)
+    DeviceBuffer small;  // hist[world] | fingerprints[world]
+    DeviceBuffer misc, sums;  // misc: two counter slots, alternating between layers
+    DistMisc* misc_host = nullptr;  // pinned mirror of both slots
+    unsigned slot = 0;              // the current layer's slot
     std::vector<u64> layer_begin;
     u64 n_total = 0;
     u64 exchanged = 0;  // records received from other ranks
     u64* hist() { return small.as<u64>(); }
-    u64* matrix() { return small.as<u64>() + world; }
-    u64* cursor() { return small.as<u64>() + world + world * world; }
-    u64* prints() { return small.as<u64>() + 2 * world + world * world; }
+    u64* prints() { return small.as<u64>() + world; }
+    DistMisc* misc_at(unsigned k) { return misc.as<DistMisc>() + k; }
 };
 
 namespace
@@ -322,7 +373,7 @@ void ensure_layer(ShardState& S, u64 n, cudaStream_t s)
     if (n > S.cap_layer)
     {
         const u64 cap = grown(n, S.cap_layer);
-        S.cg.alloc((cap + 1) * 4, s);
+        S.cg.alloc((cap + 2) * 4, s);  // word lanes, goals, overflow
         S.gbase.alloc((cap + 1) * 8, s);
         S.cap_layer = cap;
     }
@@ -334,19 +385,29 @@ void ensure_g(ShardState& S, u64 G, cudaStream_t s)
     if (G > S.cap_g)
     {
         const u64 cap = grown(G, S.cap_g);
-        S.fm.alloc(cap, s);
-        S.f.alloc(cap, s);
-        S.mark.alloc(cap * 4, s);
-        S.gmin.alloc(cap * 4, s);
-        S.claimed.alloc(cap, s);
+        const u64 nw = (cap + 31) / 32;
+        S.fm.alloc(nw * 4, s);
+        S.f.alloc(nw * 4, s);
+        S.wpre.alloc(nw * 8, s);
+        S.gmin.alloc(cap * 8, s);
+        S.cw.alloc(cap * 4, s);
         S.cap_g = cap;
+        S.gmin_clean = false;
     }
-    ensure_scan(S, G, s);
+    if (!S.gmin_clean)
+    {
+        B2_CUDA(cudaMemsetAsync(S.gmin.p, 0xFF, S.cap_g * 8, s));
+        S.gmin_clean = true;
+    }
+    ensure_scan(S, (G + 31) / 32, s);
 }
 
-/// Collective (every rank passes the same G and W): the communicator's receive buffers hold G records.
+/// Collective (every rank passes the same G and W): the communicator's receive buffers hold G records, and their
+/// fill cursors are mapped.
 void ensure_recv(b2_comm* comm, u32 W, u64 G, cudaStream_t s)
 {
+    if (!comm->cursors.bytes)
+        peer_buffer_exchange(comm, comm->cursors, 256, s, true);
     const u64 need = G * (W + 2) * 8;
     if (need <= comm->exchange.bytes)
         return;
@@ -374,16 +435,22 @@ void ensure_table(ShardState& S, u64 bound, DistMisc* misc, cudaStream_t s, u64&
     }
 }
 
-const DistMisc& read_misc(ShardState& S, b2_comm* comm, cudaStream_t s)
+/// Waits for the stream and reads both counter slots: returns the current layer's, the other one into *other.
+DistMisc read_misc(ShardState& S, b2_comm* comm, cudaStream_t s, DistMisc* other = nullptr)
 {
-    B2_CUDA(cudaMemcpyAsync(S.misc_host, S.misc.p, sizeof(DistMisc), cudaMemcpyDeviceToHost, s));
+    B2_CUDA(cudaMemcpyAsync(S.misc_host, S.misc.p, 2 * sizeof(DistMisc), cudaMemcpyDeviceToHost, s));
     comm_sync(comm, s);
-    const DistMisc& m = *S.misc_host;
-    if (m.lm.status & kStatusProbeLimit)
-        throw Error(B2_DEVICE_FAULT, "b2_brfs: a hash-set probe ran past its bound");
-    if (m.lm.status)
-        throw Error(B2_DEVICE_FAULT, "b2_brfs: device status " + std::to_string(m.lm.status));
-    return m;
+    for (int k = 0; k < 2; ++k)
+    {
+        const u32 st = S.misc_host[k].lm.status;
+        if (st & kStatusProbeLimit)
+            throw Error(B2_DEVICE_FAULT, "b2_brfs: a hash-set probe ran past its bound");
+        if (st)
+            throw Error(B2_DEVICE_FAULT, "b2_brfs: device status " + std::to_string(st));
+    }
+    if (other)
+        *other = S.misc_host[S.slot ^ 1];
+    return S.misc_host[S.slot];
 }
 }  // namespace
 
@@ -404,7 +471,7 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
     const u32 W = B.W, RW = W + 2;
     const unsigned sms = static_cast<unsigned>(B.task->ctx->sms);
     cudaStream_t s = B.stream;
-    cudaEvent_t ev[5];
+    cudaEvent_t ev[7];
     for (auto& e : ev)
         B2_CUDA(cudaEventCreate(&e));
     struct EvGuard
@@ -412,7 +479,7 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
         cudaEvent_t* e;
         ~EvGuard()
         {
-            for (int i = 0; i < 5; ++i)
+            for (int i = 0; i < 7; ++i)
                 cudaEventDestroy(e[i]);
         }
     } guard{ev};
@@ -422,19 +489,21 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
     const u64 expect = std::max<u64>(o.expected_states / world + o.expected_states / (4 * world), 1024);
     ensure_cand(S, W, expect * 2, s);
     ensure_states(S, expect, s);
-    S.misc.alloc(sizeof(DistMisc), s);
-    static_assert(sizeof(DistMisc) <= PinnedPool::kBlock);
+    S.misc.alloc(2 * sizeof(DistMisc), s);
+    static_assert(2 * sizeof(DistMisc) <= PinnedPool::kBlock);
     if (!S.misc_host)
         S.misc_host = static_cast<DistMisc*>(B.task->ctx->pinned.take());
-    S.small.alloc((3 * world + world * world) * 8, s);
-    B2_CUDA(cudaMemsetAsync(S.misc.p, 0, sizeof(DistMisc), s));
-    DistMisc* misc = S.misc.as<DistMisc>();
-    ensure_table(S, expect, misc, s, B.launches);
+    S.small.alloc(2 * world * 8, s);
+    B2_CUDA(cudaMemsetAsync(S.misc.p, 0, 2 * sizeof(DistMisc), s));
+    S.slot = 0;
+    if (comm->cursors.bytes)  // a search that ended early may have left it advanced; no rank pushes before the
+        B2_CUDA(cudaMemsetAsync(comm->cursors.local.p, 0, 8, s));  // first layer's collectives
+    ensure_table(S, expect, S.misc_at(0), s, B.launches);
     // the root: arena index 0 on every rank, stored by its owner
     B2_CUDA(cudaMemcpyAsync(S.rows.p, P.initial.data(), W * 8, cudaMemcpyHostToDevice, s));
     k_dseed<<<1, 1, 0, s>>>(S.rows.as<u64>(), S.hash.as<u64>(), W, S.table.as<u64>(), S.table_slots - 1,
                             max_probe(S.table_slots), me, world, S.state_lc.as<u32>(), S.state_id.as<u32>(),
-                            S.state_par.as<u32>(), S.state_kid.as<u32>(), misc);
+                            S.state_par.as<u32>(), S.state_kid.as<u32>(), S.misc_at(0));
     B2_CUDA(cudaGetLastError());
     ++B.launches;
     S.n_local = read_misc(S, comm, s).new_packed >> 32;
@@ -452,8 +521,75 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
     u32 layers = 0;
     bool exhausted = false, solved = false;
     u64 expanded = 0, generated = 0, goals = 0, goal_id = 0;
-    double count_ms = 0, gen_ms = 0, dedup_ms = 0;
+    double count_ms = 0, gen_ms = 0, dedup_ms = 0, exchange_ms = 0;
+    S.lane = 1;
     std::vector<std::array<u64, 3>> counts;
+    u64* fill = nullptr;  // this rank's receive-buffer cursor (mapped on the first exchange)
+    // The count pass of a layer into counter slot `misc`: the local parents' successor counts and goals, their local
+    // offsets (staging), and the layer's counts by parent id summed over the ranks and their offsets. The local
+    // parents are El (host) or *El_dev and the layer's parents E or *E_dev (counts still on the device, launched with
+    // the previous layer), at most El_max and E_max.
+    const auto launch_count = [&](DistMisc* misc, u64 lb, u64 layer_first, u64 El, const u64* El_dev, u64 El_max,
+                                  u64 E, const u64* E_dev, u64 E_max) {
+        const u32* frontier = S.state_lc.as<u32>() + lb;
+        const u32* frontier_id = S.state_id.as<u32>() + lb;
+        k_dmisc_init<<<1, 1, 0, s>>>(misc);
+        if (o.timings)
+            B2_CUDA(cudaEventRecord(ev[0], s));
+        if (El_max)
+        {
+            const unsigned grid = grid_for(El_max, 128, sms * 64);
+            if (B.task->jit)
+            {
+                dev::BrfsArgs a{};
+                a.frontier = frontier;
+                a.E = El;
+                a.E_dev = El_dev;
+                a.counts = S.counts.as<u32>();
+                a.misc = &misc->lm;
+                a.S.rows = S.rows.as<u64>();
+                a.S.W = W;
+                a.pi = pi;
+                jit_launch(B.task->jit->brfs_count[pi], grid, 128, &a, s);
+            }
+            else
+                dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
+                    k_count<OW, WR><<<grid, 128, 0, s>>>(T, pi, S.rows.as<u64>(), W, frontier, El,
+                                                         S.counts.as<u32>(), &misc->lm, El_dev);
+                });
+            ++B.launches;
+        }
+        const u64 lane_words = S.lane == 4 ? E_max : (E_max + 3) / 4;
+        B2_CUDA(cudaMemsetAsync(S.cg.p, 0, (lane_words + 2) * 4, s));
+        k_dscatter<<<grid_for(El_max, 256, sms * 8), 256, 0, s>>>(S.counts.as<u32>(), frontier_id, El, El_dev,
+                                                                  layer_first, S.cg.as<u32>(), lane_words, S.lane, misc);
+        B2_CUDA(cudaGetLastError());
+        comm_group_begin();
+        comm_allreduce(comm, S.cg.p, S.cg.p, lane_words + 2, CommType::U32, CommOp::Sum, s);
+        comm_allreduce(comm, &misc->goal_id, &misc->goal_id, 1, CommType::U64, CommOp::Min, s);
+        comm_group_end();
+        static_assert(offsetof(DistMisc, overflow_all) == offsetof(DistMisc, goals_all) + 4);
+        B2_CUDA(cudaMemcpyAsync(&misc->goals_all, S.cg.as<u32>() + lane_words, 8, cudaMemcpyDeviceToDevice, s));
+        if (E_dev)
+        {
+            device_scan_dev(LaneIn{S.cg.as<u32>(), S.lane}, BaseOut{S.gbase.as<u64>()}, E_dev, E_max,
+                            &misc->lm.total_cand, S.sums.as<u64>(), s);
+            device_scan_dev(CountIn{S.counts.as<u32>()}, BaseOut{S.local_base.as<u64>()}, El_dev, El_max,
+                            &misc->total_local, S.sums.as<u64>(), s);
+        }
+        else
+        {
+            device_scan(LaneIn{S.cg.as<u32>(), S.lane}, BaseOut{S.gbase.as<u64>()}, E, &misc->lm.total_cand,
+                        S.sums.as<u64>(), s);
+            device_scan(CountIn{S.counts.as<u32>()}, BaseOut{S.local_base.as<u64>()}, El, &misc->total_local,
+                        S.sums.as<u64>(), s);
+        }
+        B.launches += 10;
+        if (o.timings)
+            B2_CUDA(cudaEventRecord(ev[1], s));
+    };
+    bool counted = false;  // this layer's count ran with the previous layer; its counters are in `next`
+    DistMisc next{};
     for (;;)
     {
         const u64 E = layer_end - layer_begin, El = le_local - lb_local;
@@ -465,53 +601,34 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
         if (layers == o.max_depth)
             break;
         ++layers;
-        ensure_local(S, El, s);
-        ensure_layer(S, E, s);
-        *S.misc_host = DistMisc{};
-        S.misc_host->lm.first_goal = 0xFFFFFFFFu;
-        B2_CUDA(cudaMemcpyAsync(misc, S.misc_host, sizeof(DistMisc), cudaMemcpyHostToDevice, s));
-        B2_CUDA(cudaMemsetAsync(S.cg.p, 0, (E + 1) * 4, s));
-        const u32* frontier = S.state_lc.as<u32>() + lb_local;
-        const u32* frontier_id = S.state_id.as<u32>() + lb_local;
-        if (o.timings)
-            B2_CUDA(cudaEventRecord(ev[0], s));
-        if (El)
+        DistMisc* misc = S.misc_at(S.slot);
+        DistMisc m1;
+        if (counted)
+            m1 = next;
+        else
         {
-            const unsigned grid = grid_for(El, 128, sms * 64);
-            if (B.task->jit)
-            {
-                dev::BrfsArgs a{};
-                a.frontier = frontier;
-                a.E = El;
-                a.counts = S.counts.as<u32>();
-                a.misc = &misc->lm;
-                a.S.rows = S.rows.as<u64>();
-                a.S.W = W;
-                a.pi = pi;
-                jit_launch(B.task->jit->brfs_count[pi], grid, 128, &a, s);
-            }
-            else
-                dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
-                    k_count<OW, WR><<<grid, 128, 0, s>>>(T, pi, S.rows.as<u64>(), W, frontier, El,
-                                                         S.counts.as<u32>(), &misc->lm);
-                });
-            ++B.launches;
+            ensure_local(S, El, s);
+            ensure_layer(S, E, s);
+            launch_count(misc, lb_local, layer_begin, El, nullptr, El, E, nullptr, E);
+            m1 = read_misc(S, comm, s);
         }
-        k_dscatter<<<grid_for(El, 256, sms * 8), 256, 0, s>>>(S.counts.as<u32>(), frontier_id, El, layer_begin,
-                                                              S.cg.as<u32>(), E, misc);
-        B2_CUDA(cudaGetLastError());
-        comm_group_begin();
-        comm_allreduce(comm, S.cg.p, S.cg.p, E + 1, CommType::U32, CommOp::Sum, s);
-        comm_allreduce(comm, &misc->goal_id, &misc->goal_id, 1, CommType::U64, CommOp::Min, s);
-        comm_group_end();
-        B2_CUDA(cudaMemcpyAsync(&misc->goals_all, S.cg.as<u32>() + E, 4, cudaMemcpyDeviceToDevice, s));
-        device_scan(CountIn{S.cg.as<u32>()}, BaseOut{S.gbase.as<u64>()}, E, &misc->lm.total_cand, S.sums.as<u64>(), s);
-        device_scan(CountIn{S.counts.as<u32>()}, BaseOut{S.local_base.as<u64>()}, El, &misc->total_local,
-                    S.sums.as<u64>(), s);
-        B.launches += 7;
+        counted = false;
+        if (m1.overflow_all)
+        {
+            // a parent has more than 255 successors: word lanes from here on (every rank sees the same sum); the
+            // count pass again, over the known parents
+            S.lane = 4;
+            ensure_local(S, El, s);
+            ensure_layer(S, E, s);
+            launch_count(misc, lb_local, layer_begin, El, nullptr, El, E, nullptr, E);
+            m1 = read_misc(S, comm, s);
+        }
         if (o.timings)
-            B2_CUDA(cudaEventRecord(ev[1], s));
-        const DistMisc m1 = read_misc(S, comm, s);
+        {
+            float a = 0;
+            B2_CUDA(cudaEventElapsedTime(&a, ev[0], ev[1]));
+            count_ms += a;
+        }
         u64 limit = layer_end, G = m1.lm.total_cand;
         bool stop = false;
         if (m1.goals_all)
@@ -543,6 +660,7 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
         {
             ensure_g(S, G, s);
             ensure_recv(comm, W, G, s);
+            fill = static_cast<u64*>(comm->cursors.local.p);
             if (S.cap_staging < m1.total_local)
             {
                 S.cap_staging = grown(m1.total_local, S.cap_staging);
@@ -551,25 +669,22 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
             ensure_cand(S, W, S.cand_next + G, s);
             ensure_states(S, S.n_local + G, s);
             ensure_table(S, S.n_local + G, misc, s, B.launches);
-            B2_CUDA(cudaMemsetAsync(S.small.p, 0, (3 * world + world * world) * 8, s));
-            B2_CUDA(cudaMemsetAsync(S.fm.p, 0, G, s));
-            B2_CUDA(cudaMemsetAsync(S.claimed.p, 0, G, s));
-            B2_CUDA(cudaMemsetAsync(S.gmin.p, 0xFF, G * 4, s));
+            const u64 nw = (G + 31) / 32;
+            B2_CUDA(cudaMemsetAsync(S.small.p, 0, world * 8, s));
+            B2_CUDA(cudaMemsetAsync(S.fm.p, 0, nw * 4, s));
             if (o.timings)
                 B2_CUDA(cudaEventRecord(ev[2], s));
-            // the state arrays may have moved (ensure_states)
-            frontier = S.state_lc.as<u32>() + lb_local;
-            frontier_id = S.state_id.as<u32>() + lb_local;
             if (El)
             {
+                // the state arrays may have moved (ensure_states)
                 DExpandArgs a{};
                 a.rows = S.rows.as<u64>();
-                a.frontier = frontier;
-                a.frontier_id = frontier_id;
+                a.frontier = S.state_lc.as<u32>() + lb_local;
+                a.frontier_id = S.state_id.as<u32>() + lb_local;
                 a.E = El;
                 a.layer_begin = layer_begin;
                 a.limit = limit;
-                a.gbase = S.gbase.as<u64>();
+                a.gbase = nullptr;  // keys id << 32 | successor index
                 a.local_base = S.local_base.as<u64>();
                 a.staging = S.staging.as<u64>();
                 a.hist = S.hist();
@@ -585,44 +700,63 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
                     });
                 ++B.launches;
             }
-            comm_allgather(comm, S.hist(), S.matrix(), world, CommType::U64, s);
+            if (o.timings)
+                B2_CUDA(cudaEventRecord(ev[5], s));
             const u32 tile = std::min<u32>(kPushThreads, kPushSmemWords / RW);
-            k_push<<<grid_for(m1.total_local, tile, sms * 8), kPushThreads, tile * RW * 8, s>>>(
-                S.staging.as<u64>(), S.matrix(), reinterpret_cast<u64* const*>(comm->exchange.table.p),
-                reinterpret_cast<unsigned long long*>(S.cursor()), me, world, RW, tile);
+            k_push_reserve<<<grid_for(m1.total_local, tile, sms * 8), kPushThreads, tile * RW * 8, s>>>(
+                S.staging.as<u64>(), S.hist(), reinterpret_cast<u64* const*>(comm->exchange.table.p),
+                reinterpret_cast<u64* const*>(comm->cursors.table.p), world, RW, tile);
             B2_CUDA(cudaGetLastError());
             comm_allreduce(comm, &misc->barrier, &misc->barrier, 1, CommType::U32, CommOp::Sum, s);
-            k_dinsert<<<sms * 8, 256, 0, s>>>(static_cast<const u64*>(comm->exchange.local.p), S.matrix(), me, world,
+            if (o.timings)
+                B2_CUDA(cudaEventRecord(ev[6], s));
+            S.gmin_clean = false;
+            k_dinsert<<<sms * 8, 256, 0, s>>>(static_cast<const u64*>(comm->exchange.local.p), fill, S.hist(), me,
                                               S.rows.as<u64>(), S.hash.as<u64>(), S.table.as<u64>(), S.table_slots - 1,
-                                              max_probe(S.table_slots), S.cand_next, W, S.gmin.as<u32>(),
-                                              S.claimed.as<u8>(), misc);
+                                              max_probe(S.table_slots), S.cand_next, W,
+                                              S.gmin.as<unsigned long long>(), misc);
             B2_CUDA(cudaGetLastError());
             if (o.timings)
                 B2_CUDA(cudaEventRecord(ev[3], s));
-            k_dmark<<<sms * 8, 256, 0, s>>>(S.matrix(), me, world, S.claimed.as<u8>(), S.gmin.as<u32>(), S.cand_next,
-                                            S.fm.as<u8>(), S.mark.as<u32>());
+            k_dmark<<<sms * 8, 256, 0, s>>>(misc, fill, S.gmin.as<u64>(), S.gbase.as<u64>(), layer_begin,
+                                            S.fm.as<u32>(), S.cw.as<u32>());
             B2_CUDA(cudaGetLastError());
-            comm_allreduce(comm, S.fm.p, S.f.p, G, CommType::U8, CommOp::Sum, s);
-            PackOut out{S.mark.as<u32>(), S.gbase.as<u64>(), E_exp, layer_begin, layer_end, S.n_local,
-                        S.state_lc.as<u32>(), S.state_id.as<u32>(), S.state_par.as<u32>(), S.state_kid.as<u32>()};
-            device_scan(PackIn{S.f.as<u8>(), S.fm.as<u8>()}, out, G, &misc->new_packed, S.sums.as<u64>(), s);
-            B.launches += 6;
+            comm_allreduce(comm, S.fm.p, S.f.p, nw, CommType::U32, CommOp::Sum, s);
+            device_scan(WordIn{S.f.as<u32>(), S.fm.as<u32>()}, WordOut{S.wpre.as<u64>()}, nw, &misc->new_packed,
+                        S.sums.as<u64>(), s);
+            k_dassign<<<sms * 8, 256, 0, s>>>(misc, S.gmin.as<u64>(), S.cw.as<u32>(), S.f.as<u32>(), S.fm.as<u32>(),
+                                              S.wpre.as<u64>(), layer_end, S.n_local, S.cand_next,
+                                              S.state_lc.as<u32>(), S.state_id.as<u32>(), S.state_par.as<u32>(),
+                                              S.state_kid.as<u32>());
+            B2_CUDA(cudaGetLastError());
+            S.gmin_clean = true;
+            B.launches += 7;
             if (o.timings)
                 B2_CUDA(cudaEventRecord(ev[4], s));
-            const DistMisc& m3 = read_misc(S, comm, s);
+            // the next layer's count, over this layer's new states (at most G on all ranks together), so that one
+            // wait returns both; skipped where this layer is the last (a goal stop or the depth bound)
+            if (!stop && layers < o.max_depth)
+            {
+                ensure_local(S, G, s);
+                ensure_layer(S, G, s);
+                launch_count(S.misc_at(S.slot ^ 1), S.n_local, layer_end, 0, &misc->next_local, G, 0,
+                             &misc->next_all, G);
+                counted = true;
+            }
+            const DistMisc m3 = read_misc(S, comm, s, &next);
             N = m3.new_packed & 0xFFFFFFFFull;
             N_local = m3.new_packed >> 32;
             S.cand_next += m3.recv;
             S.exchanged += m3.lm.ndeferred;
             if (o.timings)
             {
-                float a = 0, b = 0, c = 0;
-                B2_CUDA(cudaEventElapsedTime(&a, ev[0], ev[1]));
+                float b = 0, c = 0, x = 0;
                 B2_CUDA(cudaEventElapsedTime(&b, ev[2], ev[3]));
                 B2_CUDA(cudaEventElapsedTime(&c, ev[3], ev[4]));
-                count_ms += a;
+                B2_CUDA(cudaEventElapsedTime(&x, ev[5], ev[6]));
                 gen_ms += b;
                 dedup_ms += c;
+                exchange_ms += x;
             }
         }
         expanded += E_exp;
@@ -637,10 +771,13 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
         S.layer_begin.push_back(layer_begin);
         if (stop)
             break;
+        if (counted)
+            S.slot ^= 1;
     }
     S.layer_begin.push_back(S.n_total);
     B.n_states = S.n_total;
     u64 fingerprint = 0;
+    DistMisc* misc = S.misc_at(S.slot);
     if (o.fingerprint)
     {
         B2_CUDA(cudaMemsetAsync(&misc->fingerprint, 0, 8, s));
@@ -669,6 +806,7 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
     R.count_ms = count_ms;
     R.gen_ms = gen_ms;
     R.dedup_ms = dedup_ms;
+    R.exchange_ms = exchange_ms;
     R.kernel_launches = B.launches;
     R.status = solved ? B2_SEARCH_SOLVED
                       : (exhausted || layers >= o.max_depth ? B2_SEARCH_EXHAUSTED : B2_SEARCH_OUT_OF_STATES);
@@ -734,8 +872,8 @@ void shard_free(b2_brfs& B)
         return;
     ShardState& S = *B.shard;
     for (DeviceBuffer* b : {&S.rows, &S.hash, &S.state_lc, &S.state_id, &S.state_par, &S.state_kid, &S.table,
-                            &S.counts, &S.local_base, &S.cg, &S.gbase, &S.staging, &S.fm, &S.f, &S.mark, &S.gmin,
-                            &S.claimed, &S.small, &S.misc, &S.sums})
+                            &S.counts, &S.local_base, &S.cg, &S.gbase, &S.staging, &S.fm, &S.f, &S.wpre, &S.gmin,
+                            &S.cw, &S.small, &S.misc, &S.sums})
         b->reset();
     B.task->ctx->pinned.give(S.misc_host);
     delete B.shard;

@@ -212,7 +212,7 @@ B2_DI void dbrfs_expand(const DExpandArgs& a)
         if (id >= a.limit)
             continue;
         const Row st = RowSel<WR>::load(a.rows + static_cast<u64>(a.frontier[i]) * W);
-        const u64 c0 = a.gbase[id - a.layer_begin];
+        const u64 c0 = a.gbase ? a.gbase[id - a.layer_begin] : id << 32;
         u64* out = a.staging + (a.local_base[i] - a.stage_base) * (W + 2);
         u32 k = 0;
         for_each_schema([&]<int S>() {

@@ -29,6 +29,7 @@ class DeviceBrfsStats:
     kernel_launches: int = 0
     local_states: int = 0  # states this rank stores (all of them on one GPU)
     exchanged: int = 0     # successors this rank received from other ranks (sharded search)
+    exchange_ms: float = 0.0  # sharded search: device time of the successor exchange (part of gen_ms)
 
 
 @dataclass
@@ -184,7 +185,8 @@ def brfs(task: Task, ctx: Context | None = None, witness_pruning: bool = True, c
                      solved=bool(r.solved), goal_id=r.goal_id, fingerprint=r.fingerprint, search_s=r.search_s,
                      words=r.words,
                      stats=DeviceBrfsStats(r.count_ms, r.gen_ms, r.dedup_ms, r.rehashes, 1 << r.table_log2,
-                                           r.kernel_launches, r.local_states, r.exchanged), _search=s)
+                                           r.kernel_launches, r.local_states, r.exchanged, r.exchange_ms),
+                     _search=s)
     return res
 
 

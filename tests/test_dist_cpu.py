@@ -2,9 +2,11 @@
 step, with the reference's own successor generator, and must reproduce the reference's deterministic ids, node
 records and layer counts; the NCCL id broadcast and the gathering of the ranks' shards run over gloo as well.
 
-The protocol model here is test infrastructure: it mirrors the device kernels' decisions (owner by hash, candidate
-index by the all-reduced count scan, smallest candidate index per state at its owner, ids by the all-reduced flag
-scan, parent by a binary search of the candidate offsets) so that a flaw in the partition logic shows without a GPU.
+The protocol model here is test infrastructure: it mirrors the device kernels' decisions (owner by hash; per-parent
+successor counts in byte lanes, widened to word lanes once a count overflows, all-reduced and scanned into candidate
+offsets; records keyed parent id << 32 | successor index; the smallest key per state at its owner; ids by popcount
+prefixes of the all-reduced candidate bitmap; node records from the key) so that a flaw in the partition logic shows
+without a GPU.
 """
 
 from __future__ import annotations
@@ -54,53 +56,72 @@ def sharded_brfs_model(text: str, rank: int, world: int, max_depth: int | None, 
     layer_begin, layer_end, n_total, lb_local = 0, 1, 1, 0
     counts = []
     layers = 0
+    lane = 1
     while layer_end > layer_begin and (max_depth is None or layers < max_depth):
         layers += 1
         E = layer_end - layer_begin
         frontier = mine[lb_local:]
         rows = np.array([r for _, r, _, _ in frontier], np.uint64).reshape(-1, t.words)
         ex = t.expand(rows, witness_pruning=witness, succ=True) if len(frontier) else None
-        cg = torch.zeros(E, dtype=torch.int64)
-        for i, (pid, _, _, _) in enumerate(frontier):
-            cg[pid - layer_begin] = int(ex["offsets"][i + 1] - ex["offsets"][i])
-        td.all_reduce(cg)
-        gbase = np.concatenate([[0], np.cumsum(cg.numpy())]).astype(np.int64)
+        # k_dscatter: byte lanes by parent id (saturated at 255 and counted), or word lanes once a layer overflowed
+        local_counts = [int(ex["offsets"][i + 1] - ex["offsets"][i]) for i in range(len(frontier))]
+        while True:
+            cg = torch.zeros(E + 1, dtype=torch.int64)  # lanes, then the overflow count
+            for i, (pid, _, _, _) in enumerate(frontier):
+                c = local_counts[i]
+                if lane == 1 and c > 255:
+                    cg[E] += 1
+                    c = 255
+                cg[pid - layer_begin] = c
+            td.all_reduce(cg)
+            if lane == 1 and int(cg[E]):
+                lane = 4  # every rank sees the same sum, so all of them redo the layer with word lanes
+                continue
+            break
+        gbase = np.concatenate([[0], np.cumsum(cg.numpy()[:E])]).astype(np.int64)
         G = int(gbase[-1])
-        # stage [row | hash | c] per local successor, bucketed by owner; the exchange (a peer-memory push on the
-        # device) is an all-gather here, each owner keeping its bucket
+        # stage [row | hash | key] per local successor, key = parent id << 32 | successor index; the exchange (a
+        # peer-memory push on the device) is an all-gather here, each owner keeping its bucket
         records = []
         for i, (pid, _, _, _) in enumerate(frontier):
-            c0 = gbase[pid - layer_begin]
             for k in range(int(ex["offsets"][i]), int(ex["offsets"][i + 1])):
                 h = int(ex["succ_hash"][k])
-                records.append((owner_of(h, world), ex["succ"][k].tobytes(), int(c0 + k - ex["offsets"][i])))
+                records.append((owner_of(h, world), ex["succ"][k].tobytes(), (pid << 32) | (k - int(ex["offsets"][i]))))
         everyone: list = [None] * world
         td.all_gather_object(everyone, records)
-        best: dict[bytes, int] = {}
+        best: dict[bytes, int] = {}  # k_dinsert: the smallest key of each new state of this owner
         for recs in everyone:
-            for d, row, c in recs:
+            for d, row, key in recs:
                 if d != rank or row in store:
                     continue
-                if row not in best or c < best[row]:
-                    best[row] = c
-        fm = torch.zeros(G, dtype=torch.int64)
-        for c in best.values():
-            fm[c] = 1
+                if row not in best or key < best[row]:
+                    best[row] = key
+        # k_dmark: bit c = gbase[parent] + successor index of each new state, in 32-bit words
+        nw = (G + 31) // 32
+        fm = torch.zeros(max(nw, 1), dtype=torch.int64)
+        cand = {}
+        for row, key in best.items():
+            c = int(gbase[(key >> 32) - layer_begin] + (key & 0xFFFFFFFF))
+            assert not (int(fm[c >> 5]) >> (c & 31)) & 1, "two states share a candidate index"
+            fm[c >> 5] += 1 << (c & 31)
+            cand[row] = c
         f = fm.clone()
         td.all_reduce(f)
-        assert G == 0 or int(f.max()) <= 1, "two owners flagged the same candidate"
-        prefix = np.concatenate([[0], np.cumsum(f.numpy())]).astype(np.int64)
+        assert all(int(x) < (1 << 32) for x in f), "two owners set the same candidate bit"
+        popc = [bin(int(x)).count("1") for x in f]
+        wpre = np.concatenate([[0], np.cumsum(popc)]).astype(np.int64)
         new = []
-        for row, c in best.items():
-            p = int(np.searchsorted(gbase, c, side="right") - 1)
-            new.append((int(layer_end + prefix[c]), np.frombuffer(row, np.uint64).copy(), layer_begin + p,
-                        int(c - gbase[p])))
+        for row, key in best.items():  # k_dassign
+            c = cand[row]
+            below = (1 << (c & 31)) - 1
+            sid = layer_end + int(wpre[c >> 5]) + bin(int(f[c >> 5]) & below).count("1")
+            new.append((sid, np.frombuffer(row, np.uint64).copy(), key >> 32, key & 0xFFFFFFFF))
         new.sort(key=lambda x: x[0])
         for sid, row, _, _ in new:
             store[row.tobytes()] = sid
         lb_local = len(mine)
         mine.extend(new)
-        N = int(prefix[-1])
+        N = int(wpre[-1])
         counts.append((E, G, N))
         n_total += N
         layer_begin, layer_end = layer_end, n_total
@@ -135,7 +156,9 @@ def test_sharded_protocol_matches_reference_ids(ref, world):
     from oracle import ref as oref
 
     cases = [("tower5", tasks.tower(5, 3), None), ("transport", tasks.transport(2, 6, 2, 0), None),
-             ("tile3x3", tasks.sliding_tile(3, 3, 30, 0), 10)]
+             ("tile3x3", tasks.sliding_tile(3, 3, 30, 0), 10),
+             # the root has more than 255 successors: word lanes from the first layer on
+             ("transport200", tasks.transport(2, 200, 3, 0), 2)]
     mgr = mp.get_context("spawn").Manager()
     out = mgr.dict()
     mp.start_processes(_protocol_worker, args=(world, _free_port(), cases, out), nprocs=world, join=True,
@@ -152,6 +175,7 @@ def test_sharded_protocol_matches_reference_ids(ref, world):
         assert got["parent"] == [int(x) for x in par], name
         assert got["index"] == [int(x) for x in idx], name
         assert min(got["sizes"]) > 0, f"{name}: a rank owns no state"
+    assert out["transport200"]["layer_counts"][0][1] > 255
 
 
 def _comm_id_worker(rank, world, port, out):

@@ -25,6 +25,8 @@ CASES = [
     ("tile4x4_d12", tasks.sliding_tile(4, 4, 60, 0), 12, True, False),
     ("tower7_goal", tasks.tower(7, 0), None, True, True),
     ("tile3x3_goal", tasks.sliding_tile(3, 3, 30, 0), None, True, True),
+    # the root has more than 255 successors: the count lanes widen to words from the first layer on
+    ("transport_2_200_3_d2", tasks.transport(2, 200, 3, 0), 2, True, False),
 ]
 
 
