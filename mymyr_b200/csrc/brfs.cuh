@@ -185,7 +185,8 @@ __global__ void __launch_bounds__(kPushThreads) k_push(const u64* __restrict__ s
 /// The staged records are the first sum(hist) of the staging area.
 __global__ void __launch_bounds__(kPushThreads) k_push_reserve(const u64* __restrict__ staging,
                                                                const u64* __restrict__ hist, u64* const* __restrict__ peers,
-                                                               u64* const* __restrict__ cursors, u32 world, u32 RW,
+                                                               u64* const* __restrict__ cursors,
+                                                               unsigned long long* sent_self, u32 me, u32 world, u32 RW,
                                                                u32 tile)
 {
     extern __shared__ u64 sm[];
@@ -225,6 +226,8 @@ __global__ void __launch_bounds__(kPushThreads) k_push_reserve(const u64* __rest
             base[x] = cnt[x] ? atomicAdd_system(reinterpret_cast<unsigned long long*>(cursors[x]),
                                                 static_cast<unsigned long long>(cnt[x]))
                              : 0;
+        if (threadIdx.x == 0 && cnt[me])
+            atomicAdd(sent_self, static_cast<unsigned long long>(cnt[me]));
         __syncthreads();
         if (threadIdx.x < m)
         {

@@ -349,6 +349,7 @@ struct DistMisc
     u64 new_packed;   // new states of the layer: all ranks | this rank's << 32
     u64 recv;         // candidates this rank received
     u64 fingerprint;
+    u64 sent_self;    // records this rank pushed to itself (the rest of those received came over NVLink)
     u64 next_all;     // new states of the layer over all ranks (the next layer's parents), unpacked on the device
     u64 next_local;   // new states of the layer on this rank (its next local parents)
     u32 goals_all;    // goal parents of the layer over all ranks
@@ -376,6 +377,10 @@ struct DExpandArgs
     u32 world;
     u32 W;
     u32 pi;                  // 0: witness pruning, 1: off
+    u32 me;                  // fused push (b2j_dbrfs_push): this rank
+    u64* const* peers;       // fused push: each rank's receive buffer (peer memory)
+    u64* const* cursors;     // fused push: each rank's fill cursor (peer memory)
+    unsigned long long* sent_self;  // fused push: records pushed to this rank
 };
 
 /// Arguments of the env kernels (b2_env_batch and b2_step_out, flattened).

@@ -113,15 +113,15 @@ struct LaneIn
 /// received record r is cand_begin + r, and its row stays in the receive buffer during the layer. gmin[r] ends as the
 /// smallest key of record r's state if r took a slot, and stays all ones otherwise. The received records are the
 /// first *fill of the buffer (its cursor, advanced by all senders).
-__global__ void k_dinsert(const u64* __restrict__ recv, const u64* fill, const u64* __restrict__ hist, u32 me,
-                          u64* __restrict__ rows, u64* __restrict__ hash, u64* table, u64 mask, u32 max_probe,
-                          u64 cand_begin, u32 W, unsigned long long* gmin, DistMisc* misc)
+__global__ void k_dinsert(const u64* __restrict__ recv, const u64* fill, u64* __restrict__ rows, u64* __restrict__ hash,
+                          u64* table, u64 mask, u32 max_probe, u64 cand_begin, u32 W, unsigned long long* gmin,
+                          DistMisc* misc)
 {
     const u64 n = *fill;
     if (blockIdx.x == 0 && threadIdx.x == 0)
     {
         misc->recv = n;
-        misc->lm.ndeferred = static_cast<u32>(n - hist[me]);  // received from other ranks
+        misc->lm.ndeferred = static_cast<u32>(n - misc->sent_self);  // received from other ranks
     }
     const u32 RW = W + 2;
     for (u64 r = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; r < n; r += static_cast<u64>(gridDim.x) * blockDim.x)
@@ -661,7 +661,7 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
             ensure_g(S, G, s);
             ensure_recv(comm, W, G, s);
             fill = static_cast<u64*>(comm->cursors.local.p);
-            if (S.cap_staging < m1.total_local)
+            if (!B.task->jit && S.cap_staging < m1.total_local)
             {
                 S.cap_staging = grown(m1.total_local, S.cap_staging);
                 S.staging.alloc(S.cap_staging * RW * 8, s);
@@ -674,6 +674,9 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
             B2_CUDA(cudaMemsetAsync(S.fm.p, 0, nw * 4, s));
             if (o.timings)
                 B2_CUDA(cudaEventRecord(ev[2], s));
+            // the compiled matcher pushes its records to their owners as it generates them; the interpreted one
+            // stages them and pushes them after
+            const bool fused = B.task->jit != nullptr;
             if (El)
             {
                 // the state arrays may have moved (ensure_states)
@@ -691,9 +694,13 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
                 a.world = world;
                 a.W = W;
                 a.pi = pi;
+                a.me = me;
+                a.peers = reinterpret_cast<u64* const*>(comm->exchange.table.p);
+                a.cursors = reinterpret_cast<u64* const*>(comm->cursors.table.p);
+                a.sent_self = reinterpret_cast<unsigned long long*>(&misc->sent_self);
                 const unsigned grid = grid_for(El, 128, sms * 64);
-                if (B.task->jit)
-                    jit_launch(B.task->jit->dbrfs_expand[pi], grid, 128, &a, s);
+                if (fused)
+                    jit_launch(B.task->jit->dbrfs_push[pi], grid, 128, &a, s);
                 else
                     dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
                         k_dexpand<OW, WR><<<grid, 128, 0, s>>>(T, a);
@@ -702,17 +709,22 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
             }
             if (o.timings)
                 B2_CUDA(cudaEventRecord(ev[5], s));
-            const u32 tile = std::min<u32>(kPushThreads, kPushSmemWords / RW);
-            k_push_reserve<<<grid_for(m1.total_local, tile, sms * 8), kPushThreads, tile * RW * 8, s>>>(
-                S.staging.as<u64>(), S.hist(), reinterpret_cast<u64* const*>(comm->exchange.table.p),
-                reinterpret_cast<u64* const*>(comm->cursors.table.p), world, RW, tile);
-            B2_CUDA(cudaGetLastError());
+            if (!fused)
+            {
+                const u32 tile = std::min<u32>(kPushThreads, kPushSmemWords / RW);
+                k_push_reserve<<<grid_for(m1.total_local, tile, sms * 8), kPushThreads, tile * RW * 8, s>>>(
+                    S.staging.as<u64>(), S.hist(), reinterpret_cast<u64* const*>(comm->exchange.table.p),
+                    reinterpret_cast<u64* const*>(comm->cursors.table.p),
+                    reinterpret_cast<unsigned long long*>(&misc->sent_self), me, world, RW, tile);
+                B2_CUDA(cudaGetLastError());
+                ++B.launches;
+            }
             comm_allreduce(comm, &misc->barrier, &misc->barrier, 1, CommType::U32, CommOp::Sum, s);
             if (o.timings)
                 B2_CUDA(cudaEventRecord(ev[6], s));
             S.gmin_clean = false;
-            k_dinsert<<<sms * 8, 256, 0, s>>>(static_cast<const u64*>(comm->exchange.local.p), fill, S.hist(), me,
-                                              S.rows.as<u64>(), S.hash.as<u64>(), S.table.as<u64>(), S.table_slots - 1,
+            k_dinsert<<<sms * 8, 256, 0, s>>>(static_cast<const u64*>(comm->exchange.local.p), fill, S.rows.as<u64>(),
+                                              S.hash.as<u64>(), S.table.as<u64>(), S.table_slots - 1,
                                               max_probe(S.table_slots), S.cand_next, W,
                                               S.gmin.as<unsigned long long>(), misc);
             B2_CUDA(cudaGetLastError());
@@ -730,7 +742,7 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
                                               S.state_kid.as<u32>());
             B2_CUDA(cudaGetLastError());
             S.gmin_clean = true;
-            B.launches += 7;
+            B.launches += 6;
             if (o.timings)
                 B2_CUDA(cudaEventRecord(ev[4], s));
             // the next layer's count, over this layer's new states (at most G on all ranks together), so that one

@@ -237,6 +237,117 @@ B2_DI void dbrfs_expand(const DExpandArgs& a)
             atomicAdd(reinterpret_cast<unsigned long long*>(a.hist + d), static_cast<unsigned long long>(hist[d]));
 }
 
+/// Words of an exchange record [row | hash | key], and records per warp queue of the fused expansion + push (at most
+/// 1024 words a warp: about 32 KB of queue per 128-thread block).
+constexpr u32 kRW = W + 2;
+constexpr u32 kPushQ = 1024u / kRW < 128u ? 1024u / kRW : 128u;
+
+/// The sharded expansion fused with the exchange: each lane runs its parent's matcher and queues every successor's
+/// record [row | hash | parent id << 32 | successor index] in its warp's shared-memory queue; after the round the warp
+/// orders the queue by owner rank, reserves each owner's run by one atomic on that owner's fill cursor (in the owner's
+/// memory, over NVLink for the other ranks), and writes the runs with consecutive lanes on consecutive words
+/// (coalesced NVLink stores). A record that finds the queue full reserves its own slot. No staging area: the records
+/// cross NVLink while the matchers run.
+template<int PI>
+B2_DI void dbrfs_expand_push(const DExpandArgs& a)
+{
+    __shared__ u64 q[4][kPushQ * kRW];  // blockDim.x = 128: four warps
+    __shared__ u32 qn[4];
+    __shared__ u32 cnt[4][kMaxWorld], start[4][kMaxWorld];
+    __shared__ u64 base[4][kMaxWorld];
+    __shared__ unsigned short order[4][kPushQ], pos[4][kPushQ];
+    __shared__ u8 dst[4][kPushQ];
+    const u32 wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    u64* Q = q[wid];
+    if (lane == 0)
+        qn[wid] = 0;
+    __syncwarp();
+    const u64 stride = static_cast<u64>(gridDim.x) * blockDim.x;
+    for (u64 first = blockIdx.x * static_cast<u64>(blockDim.x) + wid * 32; first < a.E; first += stride)
+    {
+        const u64 i = first + lane;
+        const u64 id = i < a.E ? a.frontier_id[i] : a.limit;
+        if (id < a.limit)
+        {
+            const Row st = RowSel<WR>::load(a.rows + static_cast<u64>(a.frontier[i]) * W);
+            const u64 key0 = id << 32;
+            u32 k = 0;
+            for_each_schema([&]<int S>() {
+                Run<S, PI>::go(st, [&](const u32* b) {
+                    with_successor<S>(st, b, [&](const auto& nx, u64 h) {
+                        const u32 s = atomicAdd(&qn[wid], 1u);
+                        u64* r;
+                        if (s < kPushQ)
+                            r = Q + s * kRW;
+                        else
+                        {
+                            const u32 d = owner_of(h, a.world);
+                            const u64 slot = atomicAdd_system(reinterpret_cast<unsigned long long*>(a.cursors[d]), 1ull);
+                            if (d == a.me)
+                                atomicAdd(a.sent_self, 1ull);
+                            r = a.peers[d] + slot * kRW;
+                        }
+#pragma unroll
+                        for (u32 x = 0; x < W; ++x)
+                            r[x] = nx.word(x);
+                        r[W] = h;
+                        r[W + 1] = key0 + k;
+                    });
+                    ++k;
+                    return true;
+                });
+            });
+        }
+        __syncwarp();
+        const u32 n = min(qn[wid], kPushQ);
+        if (n)
+        {
+            for (u32 d = lane; d < a.world; d += 32)
+                cnt[wid][d] = 0;
+            __syncwarp();
+            for (u32 s = lane; s < n; s += 32)
+            {
+                const u32 d = owner_of(Q[s * kRW + W], a.world);
+                dst[wid][s] = static_cast<u8>(d);
+                pos[wid][s] = static_cast<unsigned short>(atomicAdd(&cnt[wid][d], 1u));
+            }
+            __syncwarp();
+            if (lane == 0)
+            {
+                u32 acc = 0;
+                for (u32 d = 0; d < a.world; ++d)
+                {
+                    start[wid][d] = acc;
+                    acc += cnt[wid][d];
+                }
+                if (cnt[wid][a.me])
+                    atomicAdd(a.sent_self, static_cast<unsigned long long>(cnt[wid][a.me]));
+            }
+            for (u32 d = lane; d < a.world; d += 32)
+                base[wid][d] = cnt[wid][d] ? atomicAdd_system(reinterpret_cast<unsigned long long*>(a.cursors[d]),
+                                                              static_cast<unsigned long long>(cnt[wid][d]))
+                                           : 0;
+            __syncwarp();
+            for (u32 s = lane; s < n; s += 32)
+                order[wid][start[wid][dst[wid][s]] + pos[wid][s]] = static_cast<unsigned short>(s);
+            __syncwarp();
+            for (u32 x = lane; x < n * kRW; x += 32)
+            {
+                const u32 sp = x / kRW, w = x - sp * kRW;
+                const u32 s = order[wid][sp], d = dst[wid][s];
+                a.peers[d][(base[wid][d] + (sp - start[wid][d])) * kRW + w] = Q[s * kRW + w];
+            }
+            __syncwarp();
+            if (lane == 0)
+                qn[wid] = 0;
+            __syncwarp();
+        }
+    }
+    // the records are visible to every rank before this kernel completes; the ranks' next collective orders them
+    // before the owners' inserts
+    __threadfence_system();
+}
+
 // ------------------------------------------------------------------------------------------------ env
 template<int PI>
 B2_DI void env_init(const EnvArgs& a)
@@ -464,6 +575,8 @@ extern "C" __global__ void __launch_bounds__(128, 10) b2j_brfs_expand_w(b2::dev:
 extern "C" __global__ void __launch_bounds__(128, 10) b2j_brfs_expand_nw(b2::dev::BrfsArgs a) { b2::gen::brfs_expand<1>(a); }
 extern "C" __global__ void __launch_bounds__(128) b2j_dbrfs_expand_w(b2::dev::DExpandArgs a) { b2::gen::dbrfs_expand<0>(a); }
 extern "C" __global__ void __launch_bounds__(128) b2j_dbrfs_expand_nw(b2::dev::DExpandArgs a) { b2::gen::dbrfs_expand<1>(a); }
+extern "C" __global__ void __launch_bounds__(128) b2j_dbrfs_push_w(b2::dev::DExpandArgs a) { b2::gen::dbrfs_expand_push<0>(a); }
+extern "C" __global__ void __launch_bounds__(128) b2j_dbrfs_push_nw(b2::dev::DExpandArgs a) { b2::gen::dbrfs_expand_push<1>(a); }
 extern "C" __global__ void b2j_env_init_w(b2::dev::EnvArgs a) { b2::gen::env_init<0>(a); }
 extern "C" __global__ void b2j_env_init_nw(b2::dev::EnvArgs a) { b2::gen::env_init<1>(a); }
 extern "C" __global__ void __launch_bounds__(128) b2j_env_step_w(b2::dev::EnvArgs a) { b2::gen::env_step<0>(a); }

@@ -60,6 +60,15 @@ def test_generators_are_deterministic_and_pinned():
     assert digests == want
 
 
+@pytest.mark.parametrize("name", ["tile4x4", "transport_2_200_3"])
+def test_compiled_matcher_kernels_build_on_the_host(name):
+    """The task's generated matcher and the kernels over it (count, expand, fused expand + push, env, batched expand)
+    compile for sm_100a with NVRTC without a device."""
+    text = {"tile4x4": tasks.sliding_tile(4, 4, 60, 0), "transport_2_200_3": tasks.transport(2, 200, 3, 0)}[name]
+    src = Task.from_text(text, host_only=True).compile()
+    assert "b2::gen" in src or "namespace" in src
+
+
 def test_bench_config_shapes():
     t = Task.from_text(tasks.sliding_tile(4, 4, 60, 0), host_only=True)
     assert (t.words, t.fluent_slots, t.num_objects) == (4, 256, 31)
