@@ -22,7 +22,7 @@ LIB_DIR = ROOT / "lib"
 LIB = LIB_DIR / "libmymyr_b200.so"
 OBJ_DIR = REPO / "_build" / "mymyr_b200"
 
-CU_SOURCES = ["api.cu", "scan.cu", "expand.cu", "brfs.cu", "dbrfs.cu", "comm.cu", "astar.cu", "env.cu", "jit.cu"]
+CU_SOURCES = ["api.cu", "expand.cu", "brfs.cu", "dbrfs.cu", "comm.cu", "astar.cu", "env.cu", "jit.cu"]
 CPP_SOURCES = ["compile.cpp", "codegen.cpp", "relax.cpp"]
 # device sources compiled at run time (NVRTC), embedded into the library as strings
 EMBEDDED = {"b2_jit_core_source": "core.cuh", "b2_jit_kernels_source": "jit_kernels.cuh"}

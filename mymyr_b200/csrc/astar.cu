@@ -827,8 +827,8 @@ void run_astar(b2_astar& A, b2_astar_result& R)
         if (A.sums.bytes < scan_scratch_bytes(nF))
             A.sums.alloc(scan_scratch_bytes(grow_to(nF, 0)), s);
         device_scan(CountIn{A.counts.as<u32>()}, BaseOut{A.cand_base.as<u64>()}, nF, &misc->lm.total_cand,
-                    A.sums.as<u64>(), s);
-        A.launches += 4;
+                    A.sums.as<u64>(), s, &misc->lm.status);
+        A.launches += 2;
         if (A.opt.timings)
             B2_CUDA(cudaEventRecord(ev[1], s));
         k_key_base<<<grid_for(nF, 256, sms * 16), 256, 0, s>>>(A.front.as<u32>(), nF, A.best.as<u64>(),
@@ -926,7 +926,7 @@ void run_astar(b2_astar& A, b2_astar_result& R)
             ClaimOut co{A.staging.as<u64>(), W, stamp, A.n_states, A.best_rec.as<u64>(), A.slot_of.as<u64>(),
                         A.table.as<u64>(), A.rows.as<u64>(), A.hash.as<u64>(), A.best.as<u64>(), A.flags.as<u8>(),
                         A.stamp.as<u32>(), A.fresh.as<u32>(), A.touched.as<u32>(), misc};
-            device_scan(ClaimIn{A.claimed.as<u8>()}, co, Gc, &misc->nfresh, A.sums.as<u64>(), s);
+            device_scan(ClaimIn{A.claimed.as<u8>()}, co, Gc, &misc->nfresh, A.sums.as<u64>(), s, &misc->lm.status);
             if (A.opt.timings)
                 B2_CUDA(cudaEventRecord(ev[3], s));
             launch_hmax(*A.H, A.rows.as<u64>(), W, A.fresh.as<u32>(), &misc->nfresh, Gc, A.hval.as<u32>(), true,
@@ -938,7 +938,7 @@ void run_astar(b2_astar& A, b2_astar_result& R)
                                                                        static_cast<u32>(fcur), A.next.as<u32>(),
                                                                        A.open.as<u64>());
             B2_CUDA(cudaGetLastError());
-            A.launches += 7;
+            A.launches += 5;
             if (A.opt.timings)
                 B2_CUDA(cudaEventRecord(ev[5], s));
             const AstarMisc mc = read_misc(A);
@@ -1162,14 +1162,14 @@ void run_astar_sharded(b2_astar& A, b2_astar_result& R)
         if (A.sums.bytes < scan_scratch_bytes(nF))
             A.sums.alloc(scan_scratch_bytes(grow_to(nF, 0)), s);
         device_scan(CountIn{A.counts.as<u32>()}, BaseOut{A.cand_base.as<u64>()}, nF, &misc->lm.total_cand,
-                    A.sums.as<u64>(), s);
+                    A.sums.as<u64>(), s, &misc->lm.status);
         if (nF)
             k_key_base<<<grid_for(nF, 256, sms * 16), 256, 0, s>>>(A.front.as<u32>(), nF, A.best.as<u64>(),
                                                                     A.counts.as<u32>(), u64{me} << kRankShift,
                                                                     A.keyb.as<u64>(), misc);
         B2_CUDA(cudaMemcpyAsync(&misc->gsum, &misc->lm.total_cand, 8, cudaMemcpyDeviceToDevice, s));
         comm_allreduce(comm, &misc->gsum, &misc->gsum, 1, CommType::U64, CommOp::Sum, s);
-        A.launches += 4;
+        A.launches += 2;
         const AstarMisc m1 = read_misc_sync(A);
         const u64 Gl = m1.lm.total_cand, Gt = m1.gsum;
         if (Gt > 0)
@@ -1265,7 +1265,8 @@ void run_astar_sharded(b2_astar& A, b2_astar_result& R)
                 ClaimOut co{in_rec, W, stamp, A.n_states, A.best_rec.as<u64>(), A.slot_of.as<u64>(),
                             A.table.as<u64>(), A.rows.as<u64>(), A.hash.as<u64>(), A.best.as<u64>(), A.flags.as<u8>(),
                             A.stamp.as<u32>(), A.fresh.as<u32>(), A.touched.as<u32>(), misc};
-                device_scan(ClaimIn{A.claimed.as<u8>()}, co, recv, &misc->nfresh, A.sums.as<u64>(), s);
+                device_scan(ClaimIn{A.claimed.as<u8>()}, co, recv, &misc->nfresh, A.sums.as<u64>(), s,
+                            &misc->lm.status);
                 launch_hmax(*A.H, A.rows.as<u64>(), W, A.fresh.as<u32>(), &misc->nfresh, recv, A.hval.as<u32>(), true,
                             A.flags.as<u8>(), static_cast<int>(sms), s);
                 k_astar_push<<<grid_for(recv, 256, sms * 16), 256, 0, s>>>(A.touched.as<u32>(), misc, A.best.as<u64>(),
@@ -1273,7 +1274,7 @@ void run_astar_sharded(b2_astar& A, b2_astar_result& R)
                                                                             static_cast<u32>(fcur), A.next.as<u32>(),
                                                                             A.open.as<u64>());
                 B2_CUDA(cudaGetLastError());
-                A.launches += 6;
+                A.launches += 4;
             }
         }
         // the ranks' next waves and best goal (global ids: rank << 27 | state)

@@ -340,6 +340,8 @@ LayerMisc read_misc(b2_brfs& B, LayerMisc* other = nullptr)
         const u32 st = B.misc_host[k].status;
         if (st & kStatusProbeLimit)
             throw Error(B2_DEVICE_FAULT, "b2_brfs: a hash-set probe ran past its bound");
+        if (st & kStatusScanStall)
+            throw Error(B2_DEVICE_FAULT, "b2_brfs: a prefix scan gave up waiting for a tile");
         if (st)
             throw Error(B2_DEVICE_FAULT, "b2_brfs: device status " + std::to_string(st));
     }
@@ -432,12 +434,12 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
             });
         if (E_dev)
             device_scan_dev(CountIn{B.counts.as<u32>()}, BaseOut{B.cand_base.as<u64>()}, E_dev, E_max,
-                            &misc->total_cand, B.sums.as<u64>(), s);
+                            &misc->total_cand, B.sums.as<u64>(), s, &misc->status);
         else
             device_scan(CountIn{B.counts.as<u32>()}, BaseOut{B.cand_base.as<u64>()}, E, &misc->total_cand,
-                        B.sums.as<u64>(), s);
+                        B.sums.as<u64>(), s, &misc->status);
         B2_CUDA(cudaGetLastError());
-        B.launches += 5;
+        B.launches += 3;
         if (o.timings)
             B2_CUDA(cudaEventRecord(ev[1], s));
     };
@@ -524,8 +526,8 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
             if (o.timings)
                 B2_CUDA(cudaEventRecord(ev[3], s));
             device_scan(WinIn{S.claimed, S.lost}, WinOut{B.state_g.as<u32>() + B.n_states, cand_next}, G,
-                        &misc->total_new, B.sums.as<u64>(), s);
-            B.launches += 4;
+                        &misc->total_new, B.sums.as<u64>(), s, &misc->status);
+            B.launches += 2;
             if (o.timings)
                 B2_CUDA(cudaEventRecord(ev[4], s));
             // The next layer's count, launched now over this layer's new states (at most G, their number still on

@@ -445,6 +445,8 @@ DistMisc read_misc(ShardState& S, b2_comm* comm, cudaStream_t s, DistMisc* other
         const u32 st = S.misc_host[k].lm.status;
         if (st & kStatusProbeLimit)
             throw Error(B2_DEVICE_FAULT, "b2_brfs: a hash-set probe ran past its bound");
+        if (st & kStatusScanStall)
+            throw Error(B2_DEVICE_FAULT, "b2_brfs: a prefix scan gave up waiting for a tile");
         if (st)
             throw Error(B2_DEVICE_FAULT, "b2_brfs: device status " + std::to_string(st));
     }
@@ -573,18 +575,18 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
         if (E_dev)
         {
             device_scan_dev(LaneIn{S.cg.as<u32>(), S.lane}, BaseOut{S.gbase.as<u64>()}, E_dev, E_max,
-                            &misc->lm.total_cand, S.sums.as<u64>(), s);
+                            &misc->lm.total_cand, S.sums.as<u64>(), s, &misc->lm.status);
             device_scan_dev(CountIn{S.counts.as<u32>()}, BaseOut{S.local_base.as<u64>()}, El_dev, El_max,
-                            &misc->total_local, S.sums.as<u64>(), s);
+                            &misc->total_local, S.sums.as<u64>(), s, &misc->lm.status);
         }
         else
         {
             device_scan(LaneIn{S.cg.as<u32>(), S.lane}, BaseOut{S.gbase.as<u64>()}, E, &misc->lm.total_cand,
-                        S.sums.as<u64>(), s);
+                        S.sums.as<u64>(), s, &misc->lm.status);
             device_scan(CountIn{S.counts.as<u32>()}, BaseOut{S.local_base.as<u64>()}, El, &misc->total_local,
-                        S.sums.as<u64>(), s);
+                        S.sums.as<u64>(), s, &misc->lm.status);
         }
-        B.launches += 10;
+        B.launches += 4;
         if (o.timings)
             B2_CUDA(cudaEventRecord(ev[1], s));
     };
@@ -735,14 +737,14 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
             B2_CUDA(cudaGetLastError());
             comm_allreduce(comm, S.fm.p, S.f.p, nw, CommType::U32, CommOp::Sum, s);
             device_scan(WordIn{S.f.as<u32>(), S.fm.as<u32>()}, WordOut{S.wpre.as<u64>()}, nw, &misc->new_packed,
-                        S.sums.as<u64>(), s);
+                        S.sums.as<u64>(), s, &misc->lm.status);
             k_dassign<<<sms * 8, 256, 0, s>>>(misc, S.gmin.as<u64>(), S.cw.as<u32>(), S.f.as<u32>(), S.fm.as<u32>(),
                                               S.wpre.as<u64>(), layer_end, S.n_local, S.cand_next,
                                               S.state_lc.as<u32>(), S.state_id.as<u32>(), S.state_par.as<u32>(),
                                               S.state_kid.as<u32>());
             B2_CUDA(cudaGetLastError());
             S.gmin_clean = true;
-            B.launches += 6;
+            B.launches += 4;
             if (o.timings)
                 B2_CUDA(cudaEventRecord(ev[4], s));
             // the next layer's count, over this layer's new states (at most G on all ranks together), so that one

@@ -158,7 +158,7 @@ extern "C" b2_status b2_expand(b2_task* task, const uint64_t* states, uint64_t r
             dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
                 k_expand_count<OW, WR><<<grid, 128, 0, s>>>(task->dev, states, rows, words, pi, counts);
             });
-        device_scan(SegCountIn{counts}, SegCountOut{seg_off}, nseg, total, sums, s);
+        device_scan(SegCountIn{counts}, SegCountOut{seg_off}, nseg, total, sums, s, status);
         if (nseg && task->jit)
             jit_launch(task->jit->expand_write[pi], grid, 128, &a, s);
         else if (nseg)
@@ -197,7 +197,7 @@ namespace
 constexpr u64 kNoAllocMaxSegments = u64{1} << 18;
 constexpr size_t kNoAllocCounts = kNoAllocMaxSegments * 4;
 constexpr size_t kNoAllocOffsets = kNoAllocMaxSegments * 8;
-constexpr size_t kNoAllocSums = ((kNoAllocMaxSegments + kScanTile - 1) / kScanTile + 1) * 8;
+constexpr size_t kNoAllocSums = scan_scratch_bytes(kNoAllocMaxSegments);
 constexpr size_t kNoAllocScratchBytes = kNoAllocCounts + kNoAllocOffsets + 256 + kNoAllocSums;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
@@ -282,7 +282,7 @@ extern "C" b2_status b2_expand_noalloc(b2_task* task, const uint64_t* states, ui
             dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
                 k_expand_count<OW, WR><<<grid, 128, 0, s>>>(task->dev, states, rows, words, pi, counts);
             });
-        device_scan(SegCountIn{counts}, SegCountOut{seg_off}, nseg, total, sums, s);
+        device_scan(SegCountIn{counts}, SegCountOut{seg_off}, nseg, total, sums, s, status);
         if (nseg && task->jit)
             jit_launch(task->jit->expand_write[pi], grid, 128, &a, s);
         else if (nseg)
