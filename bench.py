@@ -403,7 +403,8 @@ def main():
               "expand": statistics.mean(r.stats.gen_ms for r in phased),
               "rank": statistics.mean(r.stats.dedup_ms for r in phased),
               "source": "the warm-up searches, with per-layer events",
-              "wall": statistics.mean(r.search_s * 1000 for r in results)}
+              "wall": statistics.mean(r.search_s * 1000 for r in results),
+              "host_wait": statistics.mean(r.stats.wait_ms for r in results)}
     if world > 1:
         phases["exchange"] = statistics.mean(r.stats.exchange_ms for r in phased)  # part of "expand"
     if args.quick:

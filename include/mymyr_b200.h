@@ -245,6 +245,7 @@ typedef struct b2_brfs_result {
     uint64_t exchanged;        /* out: successors this rank received from other ranks (sharded search) */
     double exchange_ms;        /* out: sharded search: device time of the successor exchange (per-owner counts,
                                   push, barrier; options.timings), part of gen_ms */
+    double wait_ms;            /* out: host time spent waiting for the device's per-layer results (of search_s) */
 } b2_brfs_result;
 
 b2_status b2_brfs_create(b2_task* task, const b2_brfs_options* options, b2_brfs** out);

@@ -86,7 +86,8 @@ class BrfsResult(C.Structure):
                 ("dedup_ms", C.c_double), ("kernel_launches", C.c_uint64),
                 ("layer_counts", C.POINTER(C.c_uint64)), ("layer_capacity", C.c_uint32),
                 ("table_log2", C.c_uint32), ("rehashes", C.c_uint32), ("words", C.c_uint32),
-                ("local_states", C.c_uint64), ("exchanged", C.c_uint64), ("exchange_ms", C.c_double)]
+                ("local_states", C.c_uint64), ("exchanged", C.c_uint64), ("exchange_ms", C.c_double),
+                ("wait_ms", C.c_double)]
 
 
 class HeuristicInfo(C.Structure):

@@ -334,7 +334,9 @@ Store make_store(b2_brfs& B, u64 layer_cand_begin)
 LayerMisc read_misc(b2_brfs& B, LayerMisc* other = nullptr)
 {
     B2_CUDA(cudaMemcpyAsync(B.misc_host, B.misc.p, 2 * sizeof(LayerMisc), cudaMemcpyDeviceToHost, B.stream));
+    const auto t0 = std::chrono::steady_clock::now();
     stream_wait(B.stream);
+    B.wait_s += std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
     for (int k = 0; k < 2; ++k)
     {
         const u32 st = B.misc_host[k].status;
@@ -392,6 +394,7 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
         B.misc_host = static_cast<LayerMisc*>(B.task->ctx->pinned.take());
     B2_CUDA(cudaMemsetAsync(B.misc.p, 0, 2 * sizeof(LayerMisc), s));
     B.slot = 0;
+    B.wait_s = 0;
     ensure_table(B, expect);
     B2_CUDA(cudaMemcpyAsync(B.rows.p, P.initial.data(), W * 8, cudaMemcpyHostToDevice, s));
     k_seed_root<<<1, 1, 0, s>>>(make_store(B, 0), B.state_g.as<u32>());
@@ -629,6 +632,7 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
     R.count_ms = count_ms;
     R.gen_ms = gen_ms;
     R.dedup_ms = dedup_ms;
+    R.wait_ms = B.wait_s * 1000;
     R.kernel_launches = B.launches;
     R.status = solved ? B2_SEARCH_SOLVED
                       : full ? B2_SEARCH_OUT_OF_STATES

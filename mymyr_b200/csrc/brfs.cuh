@@ -42,6 +42,33 @@ __global__ void __launch_bounds__(128) k_count(DevTask T, u32 pi, const u64* __r
     }
 }
 
+/// Interpreted matcher: calls f(successor accessor, hash) for the successor of `st` under schema sc's binding b.
+template<int WR, class Row, class F>
+__device__ __forceinline__ void with_successor_interp(const DevTask& T, const DSchema& sc, const Row& st, const u32* b,
+                                                      u32 W, F&& f)
+{
+    if constexpr (WR > 0)
+    {
+        RegRow<WR> nx = st;
+        for (u32 q = sc.del_begin; q < sc.del_end; ++q)
+        {
+            const u64 key = pattern_key(T, T.lits[q], b);
+            if (key < T.fluent_count)
+                nx.clear(static_cast<u32>(key));
+        }
+        for (u32 q = sc.add_begin; q < sc.add_end; ++q)
+            nx.set(static_cast<u32>(pattern_key(T, T.lits[q], b)));
+        f(nx, hash_words([&](u32 q) { return nx.word(q); }, W));
+    }
+    else
+    {
+        Effects e;
+        collect_effects(T, sc, b, e);
+        const SuccRow<Row> nx{st, e};
+        f(nx, hash_words([&](u32 q) { return nx.word(q); }, W));
+    }
+}
+
 /// Interpreted matcher: the records of the local parents' successors (the compiled twin is b2j_dbrfs_expand).
 template<int OW, int WR>
 __global__ void __launch_bounds__(128) k_dexpand(DevTask T, dev::DExpandArgs a)
@@ -65,35 +92,14 @@ __global__ void __launch_bounds__(128) k_dexpand(DevTask T, dev::DExpandArgs a)
         {
             const DSchema& sc = T.schemas[s];
             enumerate<OW>(T, sc.prog[a.pi], st, bind, [&](const u32* b) {
-                u64* r = out + static_cast<u64>(k) * (W + 2);
-                u64 h;
-                if constexpr (WR > 0)
-                {
-                    RegRow<WR> nx = st;
-                    for (u32 q = sc.del_begin; q < sc.del_end; ++q)
-                    {
-                        const u64 key = pattern_key(T, T.lits[q], b);
-                        if (key < T.fluent_count)
-                            nx.clear(static_cast<u32>(key));
-                    }
-                    for (u32 q = sc.add_begin; q < sc.add_end; ++q)
-                        nx.set(static_cast<u32>(pattern_key(T, T.lits[q], b)));
-                    h = hash_words([&](u32 q) { return nx.word(q); }, W);
+                with_successor_interp<WR>(T, sc, st, b, W, [&](const auto& nx, u64 h) {
+                    u64* r = out + static_cast<u64>(k) * (W + 2);
                     for (u32 q = 0; q < W; ++q)
                         r[q] = nx.word(q);
-                }
-                else
-                {
-                    Effects e;
-                    collect_effects(T, sc, b, e);
-                    const SuccRow<decltype(st)> nx{st, e};
-                    h = hash_words([&](u32 q) { return nx.word(q); }, W);
-                    for (u32 q = 0; q < W; ++q)
-                        r[q] = nx.word(q);
-                }
-                r[W] = h;
-                r[W + 1] = c0 + k;
-                atomicAdd(&hist[dev::owner_of(h, a.world)], 1u);
+                    r[W] = h;
+                    r[W + 1] = c0 + k;
+                    atomicAdd(&hist[dev::owner_of(h, a.world)], 1u);
+                });
                 ++k;
                 return true;
             });
@@ -103,6 +109,46 @@ __global__ void __launch_bounds__(128) k_dexpand(DevTask T, dev::DExpandArgs a)
     for (u32 d = threadIdx.x; d < a.world; d += blockDim.x)
         if (hist[d])
             atomicAdd(reinterpret_cast<unsigned long long*>(a.hist + d), static_cast<unsigned long long>(hist[d]));
+}
+
+/// Interpreted matcher, sharded count pass: k_count plus the successors per owner rank (the compiled twin is
+/// b2j_dbrfs_count).
+template<int OW, int WR>
+__global__ void __launch_bounds__(128) k_dcount(DevTask T, u32 pi, const u64* __restrict__ rows, u32 W,
+                                                const u32* __restrict__ frontier, u64 E_in, const u64* E_dev,
+                                                u32* __restrict__ counts, LayerMisc* misc, u64* hist_out, u32 world)
+{
+    __shared__ u32 hist[dev::kMaxWorld];
+    for (u32 d = threadIdx.x; d < world; d += blockDim.x)
+        hist[d] = 0;
+    __syncthreads();
+    const u64 E = E_dev ? *E_dev : E_in;
+    for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < E; i += static_cast<u64>(gridDim.x) * blockDim.x)
+    {
+        const auto st = load_row<WR>(rows + static_cast<u64>(frontier[i]) * W, W);
+        if (goal_holds(T, st))
+        {
+            atomicAdd(&misc->goals, 1u);
+            atomicMin(&misc->first_goal, static_cast<u32>(i));
+        }
+        u32 k = 0;
+        u32 bind[kMaxLevels] = {};
+        for (u32 s = 0; s < T.nschemas; ++s)
+        {
+            const DSchema& sc = T.schemas[s];
+            enumerate<OW>(T, sc.prog[pi], st, bind, [&](const u32* b) {
+                with_successor_interp<WR>(T, sc, st, b, W,
+                                          [&](const auto&, u64 h) { atomicAdd(&hist[dev::owner_of(h, world)], 1u); });
+                ++k;
+                return true;
+            });
+        }
+        counts[i] = k;
+    }
+    __syncthreads();
+    for (u32 d = threadIdx.x; d < world; d += blockDim.x)
+        if (hist[d])
+            atomicAdd(reinterpret_cast<unsigned long long*>(hist_out + d), static_cast<unsigned long long>(hist[d]));
 }
 
 constexpr unsigned kPushThreads = 256;
@@ -310,6 +356,7 @@ struct b2_brfs
     std::vector<b2::u64> layer_begin;  // id of each layer's first state (+ the end)
     b2::u64 n_states = 0;
     b2::u64 launches = 0;
+    double wait_s = 0;  // host time spent waiting for the device's layer results (this search)
     bool ran = false;
     bool own_stream = false;
     // sharded search (options.comm set)

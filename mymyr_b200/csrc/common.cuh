@@ -165,7 +165,7 @@ namespace b2
 /// more than the search's own host work, and freeing pinned memory synchronizes the device.
 struct PinnedPool
 {
-    static constexpr size_t kBlock = 256;
+    static constexpr size_t kBlock = 512;
     std::mutex mu;
     std::vector<void*> blocks;
     void* take()

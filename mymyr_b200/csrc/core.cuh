@@ -332,6 +332,8 @@ struct BrfsArgs
     Store S;
     u32 pi;               // 0: witness pruning, 1: off
     const u64* E_dev;     // count pass: when non-null, the parents are *E_dev (a count still on the device), not E
+    u64* hist;            // sharded count pass: successors per owner rank (added to)
+    u32 world;            // sharded count pass: ranks
 };
 
 // ------------------------------------------------------------------------------------------------ sharded BrFS
@@ -350,6 +352,8 @@ struct DistMisc
     u64 recv;         // candidates this rank received
     u64 fingerprint;
     u64 sent_self;    // records this rank pushed to itself (the rest of those received came over NVLink)
+    u64 recv_me;      // successors of the layer owned by this rank (from the all-reduced per-owner counts)
+    u64 recv_max;     // the most successors of the layer any rank owns
     u64 next_all;     // new states of the layer over all ranks (the next layer's parents), unpacked on the device
     u64 next_local;   // new states of the layer on this rank (its next local parents)
     u32 goals_all;    // goal parents of the layer over all ranks

@@ -70,13 +70,18 @@ __global__ void k_dseed(u64* __restrict__ rows, u64* __restrict__ hash, u32 W, u
 }
 
 /// The local successor counts into the layer-wide lane array (by parent id: bytes for lane 1, words for lane 4), then
-/// the rank's goal parents and its parents whose count does not fit a byte lane (saturated, counted) after the lanes,
-/// and the rank's first goal id. A parent's lane is written by its owner alone, so the all-reduce sums without carries.
+/// after the lanes: the rank's goal parents, its parents whose count does not fit a byte lane (saturated, counted), and
+/// its row of the per-owner successor counts M[rank][owner]; and the rank's first goal id. A parent's lane and a rank's
+/// row are written by one rank alone, so the all-reduce sums without carries.
 __global__ void k_dscatter(const u32* __restrict__ counts, const u32* __restrict__ ids, u64 E_in, const u64* E_dev,
-                           u64 layer_begin, u32* __restrict__ cg, u64 lane_words, u32 lane, DistMisc* misc)
+                           u64 layer_begin, u32* __restrict__ cg, u64 lane_words, u32 lane, const u64* __restrict__ hist,
+                           u32 me, u32 world, DistMisc* misc)
 {
     const u64 E = E_dev ? *E_dev : E_in;  // the local parents (a count still on the device when E_dev is set)
-    u32* tail = cg + lane_words;  // [goals, overflow]
+    u32* tail = cg + lane_words;  // [goals, overflow, M[world][world]]
+    if (blockIdx.x == 0)
+        for (u32 d = threadIdx.x; d < world; d += blockDim.x)
+            tail[2 + me * world + d] = static_cast<u32>(hist[d]);
     for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < E; i += static_cast<u64>(gridDim.x) * blockDim.x)
     {
         const u64 j = ids[i] - layer_begin;
@@ -95,6 +100,27 @@ __global__ void k_dscatter(const u32* __restrict__ counts, const u32* __restrict
         tail[0] = misc->lm.goals;
         misc->goal_id = misc->lm.first_goal != 0xFFFFFFFFu ? ids[misc->lm.first_goal] : ~u64{0};
     }
+}
+
+/// From the summed tail: the layer's goal parents and overflowing parents over all ranks, the successors this rank
+/// owns and the most any rank owns.
+__global__ void k_dtail(const u32* __restrict__ tail, u32 me, u32 world, DistMisc* misc)
+{
+    if (threadIdx.x != 0)
+        return;
+    misc->goals_all = tail[0];
+    misc->overflow_all = tail[1];
+    u64 most = 0;
+    for (u32 d = 0; d < world; ++d)
+    {
+        u64 n = 0;
+        for (u32 s = 0; s < world; ++s)
+            n += tail[2 + s * world + d];
+        if (d == me)
+            misc->recv_me = n;
+        most = n > most ? n : most;
+    }
+    misc->recv_max = most;
 }
 
 /// The count of parent i from the summed lanes.
@@ -311,13 +337,14 @@ struct ShardState
     // bitmap word: the exclusive prefix of both; per received record: its state's smallest key (all ones unless the
     // record took a slot: kept all ones between layers), its candidate index
     DeviceBuffer fm, f, wpre, gmin, cw;
-    u64 cap_g = 0;
+    u64 cap_g = 0, cap_recv = 0;
     bool gmin_clean = false;  // gmin all ones (false after an interrupted layer)
     u32 lane = 1;             // bytes per count lane (1, or 4 once a parent had more than 255 successors)
     DeviceBuffer small;  // hist[world] | fingerprints[world]
     DeviceBuffer misc, sums;  // misc: two counter slots, alternating between layers
     DistMisc* misc_host = nullptr;  // pinned mirror of both slots
     unsigned slot = 0;              // the current layer's slot
+    double wait_s = 0;              // host time spent waiting for the layers' results (this search)
     std::vector<u64> layer_begin;
     u64 n_total = 0;
     u64 exchanged = 0;  // records received from other ranks
@@ -373,14 +400,15 @@ void ensure_layer(ShardState& S, u64 n, cudaStream_t s)
     if (n > S.cap_layer)
     {
         const u64 cap = grown(n, S.cap_layer);
-        S.cg.alloc((cap + 2) * 4, s);  // word lanes, goals, overflow
+        S.cg.alloc((cap + 2 + kMaxWorld * kMaxWorld) * 4, s);  // word lanes, goals, overflow, per-owner counts
         S.gbase.alloc((cap + 1) * 8, s);
         S.cap_layer = cap;
     }
     ensure_scan(S, n, s);
 }
 
-void ensure_g(ShardState& S, u64 G, cudaStream_t s)
+/// The layer's candidate bitmaps (G candidates over all ranks) and the per-received-record arrays (recv records).
+void ensure_g(ShardState& S, u64 G, u64 recv, cudaStream_t s)
 {
     if (G > S.cap_g)
     {
@@ -389,14 +417,19 @@ void ensure_g(ShardState& S, u64 G, cudaStream_t s)
         S.fm.alloc(nw * 4, s);
         S.f.alloc(nw * 4, s);
         S.wpre.alloc(nw * 8, s);
+        S.cap_g = cap;
+    }
+    if (recv > S.cap_recv)
+    {
+        const u64 cap = grown(recv, S.cap_recv);
         S.gmin.alloc(cap * 8, s);
         S.cw.alloc(cap * 4, s);
-        S.cap_g = cap;
+        S.cap_recv = cap;
         S.gmin_clean = false;
     }
     if (!S.gmin_clean)
     {
-        B2_CUDA(cudaMemsetAsync(S.gmin.p, 0xFF, S.cap_g * 8, s));
+        B2_CUDA(cudaMemsetAsync(S.gmin.p, 0xFF, S.cap_recv * 8, s));
         S.gmin_clean = true;
     }
     ensure_scan(S, (G + 31) / 32, s);
@@ -439,7 +472,9 @@ void ensure_table(ShardState& S, u64 bound, DistMisc* misc, cudaStream_t s, u64&
 DistMisc read_misc(ShardState& S, b2_comm* comm, cudaStream_t s, DistMisc* other = nullptr)
 {
     B2_CUDA(cudaMemcpyAsync(S.misc_host, S.misc.p, 2 * sizeof(DistMisc), cudaMemcpyDeviceToHost, s));
+    const auto t0 = std::chrono::steady_clock::now();
     comm_sync(comm, s);
+    S.wait_s += std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
     for (int k = 0; k < 2; ++k)
     {
         const u32 st = S.misc_host[k].lm.status;
@@ -498,6 +533,7 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
     S.small.alloc(2 * world * 8, s);
     B2_CUDA(cudaMemsetAsync(S.misc.p, 0, 2 * sizeof(DistMisc), s));
     S.slot = 0;
+    S.wait_s = 0;
     if (comm->cursors.bytes)  // a search that ended early may have left it advanced; no rank pushes before the
         B2_CUDA(cudaMemsetAsync(comm->cursors.local.p, 0, 8, s));  // first layer's collectives
     ensure_table(S, expect, S.misc_at(0), s, B.launches);
@@ -536,6 +572,7 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
         const u32* frontier = S.state_lc.as<u32>() + lb;
         const u32* frontier_id = S.state_id.as<u32>() + lb;
         k_dmisc_init<<<1, 1, 0, s>>>(misc);
+        B2_CUDA(cudaMemsetAsync(S.hist(), 0, world * 8, s));
         if (o.timings)
             B2_CUDA(cudaEventRecord(ev[0], s));
         if (El_max)
@@ -552,26 +589,30 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
                 a.S.rows = S.rows.as<u64>();
                 a.S.W = W;
                 a.pi = pi;
-                jit_launch(B.task->jit->brfs_count[pi], grid, 128, &a, s);
+                a.hist = S.hist();
+                a.world = world;
+                jit_launch(B.task->jit->dbrfs_count[pi], grid, 128, &a, s);
             }
             else
                 dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
-                    k_count<OW, WR><<<grid, 128, 0, s>>>(T, pi, S.rows.as<u64>(), W, frontier, El,
-                                                         S.counts.as<u32>(), &misc->lm, El_dev);
+                    k_dcount<OW, WR><<<grid, 128, 0, s>>>(T, pi, S.rows.as<u64>(), W, frontier, El, El_dev,
+                                                          S.counts.as<u32>(), &misc->lm, S.hist(), world);
                 });
             ++B.launches;
         }
         const u64 lane_words = S.lane == 4 ? E_max : (E_max + 3) / 4;
-        B2_CUDA(cudaMemsetAsync(S.cg.p, 0, (lane_words + 2) * 4, s));
+        const u64 tail_words = 2 + u64{world} * world;
+        B2_CUDA(cudaMemsetAsync(S.cg.p, 0, (lane_words + tail_words) * 4, s));
         k_dscatter<<<grid_for(El_max, 256, sms * 8), 256, 0, s>>>(S.counts.as<u32>(), frontier_id, El, El_dev,
-                                                                  layer_first, S.cg.as<u32>(), lane_words, S.lane, misc);
+                                                                  layer_first, S.cg.as<u32>(), lane_words, S.lane,
+                                                                  S.hist(), me, world, misc);
         B2_CUDA(cudaGetLastError());
         comm_group_begin();
-        comm_allreduce(comm, S.cg.p, S.cg.p, lane_words + 2, CommType::U32, CommOp::Sum, s);
+        comm_allreduce(comm, S.cg.p, S.cg.p, lane_words + tail_words, CommType::U32, CommOp::Sum, s);
         comm_allreduce(comm, &misc->goal_id, &misc->goal_id, 1, CommType::U64, CommOp::Min, s);
         comm_group_end();
-        static_assert(offsetof(DistMisc, overflow_all) == offsetof(DistMisc, goals_all) + 4);
-        B2_CUDA(cudaMemcpyAsync(&misc->goals_all, S.cg.as<u32>() + lane_words, 8, cudaMemcpyDeviceToDevice, s));
+        k_dtail<<<1, 32, 0, s>>>(S.cg.as<u32>() + lane_words, me, world, misc);
+        B2_CUDA(cudaGetLastError());
         if (E_dev)
         {
             device_scan_dev(LaneIn{S.cg.as<u32>(), S.lane}, BaseOut{S.gbase.as<u64>()}, E_dev, E_max,
@@ -586,7 +627,7 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
             device_scan(CountIn{S.counts.as<u32>()}, BaseOut{S.local_base.as<u64>()}, El, &misc->total_local,
                         S.sums.as<u64>(), s, &misc->lm.status);
         }
-        B.launches += 4;
+        B.launches += 5;
         if (o.timings)
             B2_CUDA(cudaEventRecord(ev[1], s));
     };
@@ -660,17 +701,19 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
         u64 N = 0, N_local = 0;
         if (E_exp > 0 && G > 0)
         {
-            ensure_g(S, G, s);
-            ensure_recv(comm, W, G, s);
+            // this rank receives recv_me records (no rank more than recv_max): the per-owner counts of the count pass
+            const u64 recv = m1.recv_me;
+            ensure_g(S, G, recv, s);
+            ensure_recv(comm, W, m1.recv_max, s);
             fill = static_cast<u64*>(comm->cursors.local.p);
             if (!B.task->jit && S.cap_staging < m1.total_local)
             {
                 S.cap_staging = grown(m1.total_local, S.cap_staging);
                 S.staging.alloc(S.cap_staging * RW * 8, s);
             }
-            ensure_cand(S, W, S.cand_next + G, s);
-            ensure_states(S, S.n_local + G, s);
-            ensure_table(S, S.n_local + G, misc, s, B.launches);
+            ensure_cand(S, W, S.cand_next + recv, s);
+            ensure_states(S, S.n_local + recv, s);
+            ensure_table(S, S.n_local + recv, misc, s, B.launches);
             const u64 nw = (G + 31) / 32;
             B2_CUDA(cudaMemsetAsync(S.small.p, 0, world * 8, s));
             B2_CUDA(cudaMemsetAsync(S.fm.p, 0, nw * 4, s));
@@ -751,9 +794,9 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
             // wait returns both; skipped where this layer is the last (a goal stop or the depth bound)
             if (!stop && layers < o.max_depth)
             {
-                ensure_local(S, G, s);
+                ensure_local(S, recv, s);
                 ensure_layer(S, G, s);
-                launch_count(S.misc_at(S.slot ^ 1), S.n_local, layer_end, 0, &misc->next_local, G, 0,
+                launch_count(S.misc_at(S.slot ^ 1), S.n_local, layer_end, 0, &misc->next_local, recv, 0,
                              &misc->next_all, G);
                 counted = true;
             }
@@ -821,6 +864,7 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
     R.gen_ms = gen_ms;
     R.dedup_ms = dedup_ms;
     R.exchange_ms = exchange_ms;
+    R.wait_ms = S.wait_s * 1000;
     R.kernel_launches = B.launches;
     R.status = solved ? B2_SEARCH_SOLVED
                       : (exhausted || layers >= o.max_depth ? B2_SEARCH_EXHAUSTED : B2_SEARCH_OUT_OF_STATES);

@@ -164,6 +164,8 @@ std::shared_ptr<JitModule> jit_module(int device, const Program& prog)
     m->dbrfs_expand[1] = kernel(m->lib, "b2j_dbrfs_expand_nw");
     m->dbrfs_push[0] = kernel(m->lib, "b2j_dbrfs_push_w");
     m->dbrfs_push[1] = kernel(m->lib, "b2j_dbrfs_push_nw");
+    m->dbrfs_count[0] = kernel(m->lib, "b2j_dbrfs_count_w");
+    m->dbrfs_count[1] = kernel(m->lib, "b2j_dbrfs_count_nw");
     m->env_init[0] = kernel(m->lib, "b2j_env_init_w");
     m->env_init[1] = kernel(m->lib, "b2j_env_init_nw");
     m->env_step[0] = kernel(m->lib, "b2j_env_step_w");

@@ -18,7 +18,7 @@ struct JitModule
     u64 digest = 0;
     std::string log;
     // [0]: witness pruning on, [1]: off
-    cudaKernel_t brfs_count[2]{}, brfs_expand[2]{}, dbrfs_expand[2]{}, dbrfs_push[2]{}, env_init[2]{}, env_step[2]{}, expand_count[2]{}, expand_write[2]{};
+    cudaKernel_t brfs_count[2]{}, brfs_expand[2]{}, dbrfs_expand[2]{}, dbrfs_push[2]{}, dbrfs_count[2]{}, env_init[2]{}, env_step[2]{}, expand_count[2]{}, expand_write[2]{};
     JitModule() = default;
     JitModule(const JitModule&) = delete;
     JitModule& operator=(const JitModule&) = delete;

@@ -96,6 +96,47 @@ B2_DI void brfs_count(const BrfsArgs& a)
     }
 }
 
+/// The sharded count pass: brfs_count, plus the successors per owner rank (hashed here, so that every rank learns how
+/// many records it will receive before any is pushed).
+template<int PI>
+B2_DI void dbrfs_count(const BrfsArgs& a)
+{
+    __shared__ u32 hist[kMaxWorld];
+    for (u32 d = threadIdx.x; d < a.world; d += blockDim.x)
+        hist[d] = 0;
+    __syncthreads();
+    const u64 E = a.E_dev ? *a.E_dev : a.E;
+    for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < E; i += static_cast<u64>(gridDim.x) * blockDim.x)
+    {
+        const u64 g = a.frontier[i];
+        const Row st = RowSel<WR>::load(a.S.rows + g * W);
+        if (goal(st))
+        {
+            atomicAdd(&a.misc->goals, 1u);
+            atomicMin(&a.misc->first_goal, static_cast<u32>(i));
+        }
+        u32 k = 0;
+        for_each_schema([&]<int S>() {
+            Run<S, PI>::go(st, [&](const u32* b) {
+                with_successor<S>(st, b, [&](const auto&, u64 h) {
+                    // one shared atomic per owner among the lanes emitting together
+                    const u32 d = owner_of(h, a.world);
+                    const u32 peers = __match_any_sync(__activemask(), d);
+                    if ((threadIdx.x & 31) == static_cast<u32>(__ffs(peers) - 1))
+                        atomicAdd(&hist[d], static_cast<u32>(__popc(peers)));
+                });
+                ++k;
+                return true;
+            });
+        });
+        a.counts[i] = k;
+    }
+    __syncthreads();
+    for (u32 d = threadIdx.x; d < a.world; d += blockDim.x)
+        if (hist[d])
+            atomicAdd(reinterpret_cast<unsigned long long*>(a.hist + d), static_cast<unsigned long long>(hist[d]));
+}
+
 /// A successor waiting in a warp's queue for its insert.
 struct QEntry
 {
@@ -575,6 +616,8 @@ extern "C" __global__ void __launch_bounds__(128, 10) b2j_brfs_expand_w(b2::dev:
 extern "C" __global__ void __launch_bounds__(128, 10) b2j_brfs_expand_nw(b2::dev::BrfsArgs a) { b2::gen::brfs_expand<1>(a); }
 extern "C" __global__ void __launch_bounds__(128) b2j_dbrfs_expand_w(b2::dev::DExpandArgs a) { b2::gen::dbrfs_expand<0>(a); }
 extern "C" __global__ void __launch_bounds__(128) b2j_dbrfs_expand_nw(b2::dev::DExpandArgs a) { b2::gen::dbrfs_expand<1>(a); }
+extern "C" __global__ void __launch_bounds__(128) b2j_dbrfs_count_w(b2::dev::BrfsArgs a) { b2::gen::dbrfs_count<0>(a); }
+extern "C" __global__ void __launch_bounds__(128) b2j_dbrfs_count_nw(b2::dev::BrfsArgs a) { b2::gen::dbrfs_count<1>(a); }
 extern "C" __global__ void __launch_bounds__(128) b2j_dbrfs_push_w(b2::dev::DExpandArgs a) { b2::gen::dbrfs_expand_push<0>(a); }
 extern "C" __global__ void __launch_bounds__(128) b2j_dbrfs_push_nw(b2::dev::DExpandArgs a) { b2::gen::dbrfs_expand_push<1>(a); }
 extern "C" __global__ void b2j_env_init_w(b2::dev::EnvArgs a) { b2::gen::env_init<0>(a); }

@@ -30,6 +30,7 @@ class DeviceBrfsStats:
     local_states: int = 0  # states this rank stores (all of them on one GPU)
     exchanged: int = 0     # successors this rank received from other ranks (sharded search)
     exchange_ms: float = 0.0  # sharded search: device time of the successor exchange (part of gen_ms)
+    wait_ms: float = 0.0      # host time spent waiting for the per-layer results (of search_s)
 
 
 @dataclass
@@ -185,7 +186,8 @@ def brfs(task: Task, ctx: Context | None = None, witness_pruning: bool = True, c
                      solved=bool(r.solved), goal_id=r.goal_id, fingerprint=r.fingerprint, search_s=r.search_s,
                      words=r.words,
                      stats=DeviceBrfsStats(r.count_ms, r.gen_ms, r.dedup_ms, r.rehashes, 1 << r.table_log2,
-                                           r.kernel_launches, r.local_states, r.exchanged, r.exchange_ms),
+                                           r.kernel_launches, r.local_states, r.exchanged, r.exchange_ms,
+                                           r.wait_ms),
                      _search=s)
     return res
 
