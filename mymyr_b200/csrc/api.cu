@@ -3,6 +3,7 @@
 #include "common.cuh"
 #include "jit.hpp"
 
+#include <atomic>
 #include <cstring>
 #include <mutex>
 
@@ -414,3 +415,32 @@ b2_status b2_hash_rows(b2_ctx* ctx, const uint64_t* rows, uint64_t n, uint32_t w
 }
 
 }  // extern "C"
+
+namespace b2
+{
+unsigned scan_blocks(u64 nb)
+{
+    // SM count of the calling thread's current device, read once per device
+    static std::atomic<int> sms[64];
+    int dev = 0;
+    B2_CUDA(cudaGetDevice(&dev));
+    int n = dev < 64 ? sms[dev].load(std::memory_order_relaxed) : 0;
+    if (n == 0)
+    {
+        B2_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+        if (dev < 64)
+            sms[dev].store(n, std::memory_order_relaxed);
+    }
+    const u64 cap = static_cast<u64>(n) * 8;
+    return static_cast<unsigned>(nb < cap ? nb : cap);
+}
+}  // namespace b2
+
+namespace b2
+{
+__global__ void k_scan_clear(u64* __restrict__ scratch, u64 words)
+{
+    for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < words; i += static_cast<u64>(gridDim.x) * blockDim.x)
+        scratch[i] = 0;
+}
+}  // namespace b2

@@ -32,8 +32,10 @@ namespace
 /// Phase B: the deferred inserts, resumed at their slots. Every row they can meet was written by the expansion
 /// kernel (or an earlier one), so the comparisons need no ordering within this kernel. Among equal candidates of the
 /// layer the smallest g takes the slot by atomicMin (the tag sits above g); a displaced one is marked lost.
-__global__ void k_resolve(Store S)
+__global__ void k_resolve(Store S, const DevLayerState* dyn = nullptr)
 {
+    if (dyn)
+        S.layer_cand_begin = dyn->cand_next;
     const u32 n = *S.ndeferred;
     for (u32 q = blockIdx.x * blockDim.x + threadIdx.x; q < n; q += gridDim.x * blockDim.x)
     {
@@ -171,6 +173,119 @@ struct WinOut
             state_g[rank] = static_cast<u32>(cand_begin + c);
     }
 };
+
+/// WinOut of the device-driven loop: the layer's first new state id and first candidate come from the device state.
+struct WinOutDyn
+{
+    u32* state_g;
+    const DevLayerState* d;
+    __device__ __forceinline__ void operator()(u64 c, u64 rank, u32 v) const
+    {
+        if (v)
+            state_g[d->n_states + rank] = static_cast<u32>(d->cand_next + c);
+    }
+};
+
+// ------------------------------------------------------------------------------------------------ device-driven loop
+// One iteration of a CUDA graph's while node per layer: k_g_begin, the count pass and its offsets scan, k_g_mid,
+// k_g_clear, the expansion, the resolve pass, the winners scan, k_g_end (which sets the loop's condition). A layer that
+// does not fit the buffers the graph was built over is left untouched (overflow) for the host loop.
+
+/// Layer start: the end conditions, the layer's parents, its counters.
+__global__ void k_g_begin(DevLayerState* d)
+{
+    d->E = d->E_exp = d->G = 0;
+    if (d->done || d->overflow)
+        return;
+    const u64 E = d->layer_end - d->layer_begin;
+    if (E == 0)
+    {
+        d->exhausted = 1;
+        d->done = 1;
+        return;
+    }
+    if (d->layers == d->max_depth)
+    {
+        d->done = 1;
+        return;
+    }
+    if (E > d->cap_layer || d->layers >= d->log_cap)
+    {
+        d->overflow = 1;
+        return;
+    }
+    d->misc = LayerMisc{0, 0, 0, 0, 0xFFFFFFFFu, d->misc.status, 0};
+    d->E = E;
+}
+
+/// After the count pass: the layer's candidates (up to the first goal parent when stopping at a goal), the check that
+/// the buffers hold them, the goal bookkeeping.
+__global__ void k_g_mid(DevLayerState* d, const u64* __restrict__ cand_base)
+{
+    if (d->E == 0)
+        return;
+    const u64 E = d->E;
+    u64 E_exp = E, G = d->misc.total_cand;
+    const u32 goals = d->misc.goals, first = d->misc.first_goal;
+    const bool stop = goals && d->stop_at_goal;
+    if (stop)
+    {
+        E_exp = first;
+        if (E_exp < E)
+            G = cand_base[E_exp];
+    }
+    const u64 room = (u64{1} << 32) - 1;
+    if (G > d->cap_flags || d->cand_next + G > d->cap_cand || d->n_states + G > d->cap_states ||
+        (d->n_states + G) * 4 > d->table_slots * 3 || G >= room - d->cand_next)
+    {
+        d->overflow = 1;  // nothing of this layer is kept: the host grows the buffers and runs it again
+        d->E = 0;
+        return;
+    }
+    if (goals && !d->solved)
+    {
+        d->solved = 1;
+        d->goal_id = d->layer_begin + first;
+    }
+    d->goals += d->stop_at_goal ? (goals ? 1 : 0) : goals;
+    d->stop = stop ? 1 : 0;
+    d->E_exp = E_exp;
+    d->G = G;
+}
+
+/// The layer's claimed and lost flags.
+__global__ void k_g_clear(const DevLayerState* d, u8* __restrict__ claimed, u8* __restrict__ lost)
+{
+    const u64 G = d->G;
+    for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < G; i += static_cast<u64>(gridDim.x) * blockDim.x)
+    {
+        claimed[i] = 0;
+        lost[i] = 0;
+    }
+}
+
+/// After the winners scan: the layer's counts into the log, the next layer, the loop's condition.
+__global__ void k_g_end(DevLayerState* d, cudaGraphConditionalHandle loop)
+{
+    if (d->E)
+    {
+        const u64 N = d->misc.total_new;
+        u64* l = d->log + 3 * static_cast<u64>(d->layers);
+        l[0] = d->E_exp;
+        l[1] = d->G;
+        l[2] = N;
+        d->expanded += d->E_exp;
+        d->generated += d->G;
+        d->cand_next += d->G;
+        d->n_states += N;
+        d->layer_begin = d->layer_end;
+        d->layer_end = d->n_states;
+        d->layers += 1;
+        if (d->stop || d->misc.status)
+            d->done = 1;
+    }
+    cudaGraphSetConditional(loop, d->done || d->overflow ? 0u : 1u);
+}
 
 __global__ void k_fingerprint(const u32* __restrict__ state_g, u64 first_id, u64 n, const u64* __restrict__ rows,
                               u32 W, u64* acc)
@@ -352,6 +467,120 @@ LayerMisc read_misc(b2_brfs& B, LayerMisc* other = nullptr)
     return B.misc_host[B.slot];
 }
 
+/// Layers the device-driven loop can log.
+constexpr u32 kDeviceLogLayers = 4096;
+
+/// The layer loop as one CUDA graph launch: a while node whose body is one layer (k_g_begin, count, offsets scan,
+/// k_g_mid, k_g_clear, expansion, resolve, winners scan, k_g_end), over the buffers as they are now. Runs until the search
+/// ends or a layer does not fit the buffers (DevLayerState::overflow: that layer is left to the host); returns the
+/// final device state (its log copied into `log`).
+DevLayerState run_device_layers(b2_brfs& B, const DevLayerState& init, std::vector<u64>& log)
+{
+    const Program& P = B.task->prog;
+    const u32 pi = B.opt.witness_pruning ? 0 : 1;
+    const unsigned sms = static_cast<unsigned>(B.task->ctx->sms);
+    cudaStream_t s = B.stream;
+    B.dstate.alloc(sizeof(DevLayerState), s);
+    B.dlog.alloc(kDeviceLogLayers * 3 * sizeof(u64), s);
+    DevLayerState* d = B.dstate.as<DevLayerState>();
+    DevLayerState* host = reinterpret_cast<DevLayerState*>(reinterpret_cast<char*>(B.misc_host) + 128);
+    static_assert(128 + sizeof(DevLayerState) <= PinnedPool::kBlock);
+    *host = init;
+    host->log = B.dlog.as<u64>();
+    host->log_cap = kDeviceLogLayers;
+    host->cap_layer = B.cap_layer;
+    host->cap_flags = B.cap_flags;
+    host->cap_cand = B.cap_cand;
+    host->cap_states = B.cap_states;
+    host->table_slots = B.table_slots;
+    B2_CUDA(cudaMemcpyAsync(d, host, sizeof(DevLayerState), cudaMemcpyHostToDevice, s));
+    stream_wait(s);  // the pinned source is reused for the result below
+
+    if (!B.capture)
+        B2_CUDA(cudaStreamCreateWithFlags(&B.capture, cudaStreamNonBlocking));
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    struct GraphGuard
+    {
+        cudaGraph_t& g;
+        cudaGraphExec_t& e;
+        ~GraphGuard()
+        {
+            if (e)
+                cudaGraphExecDestroy(e);
+            if (g)
+                cudaGraphDestroy(g);
+        }
+    } guard{graph, exec};
+    B2_CUDA(cudaGraphCreate(&graph, 0));
+    cudaGraphConditionalHandle loop;
+    B2_CUDA(cudaGraphConditionalHandleCreate(&loop, graph, 1, cudaGraphCondAssignDefault));
+    cudaGraphNodeParams cp{};
+    cp.type = cudaGraphNodeTypeConditional;
+    cp.conditional.handle = loop;
+    cp.conditional.type = cudaGraphCondTypeWhile;
+    cp.conditional.size = 1;
+    cudaGraphNode_t node;
+    B2_CUDA(cudaGraphAddNode(&node, graph, nullptr, 0, &cp));
+    cudaGraph_t body = cp.conditional.phGraph_out[0];
+
+    cudaStream_t c = B.capture;
+    (void)scan_blocks(1);  // the SM count is read outside the capture
+    B2_CUDA(cudaStreamBeginCaptureToGraph(c, body, nullptr, nullptr, 0, cudaStreamCaptureModeThreadLocal));
+    Store S = make_store(B, 0);
+    S.status = &d->misc.status;
+    S.ndeferred = &d->misc.ndeferred;
+    k_g_begin<<<1, 1, 0, c>>>(d);
+    {
+        dev::BrfsArgs a{};
+        a.frontier = B.state_g.as<u32>();
+        a.counts = B.counts.as<u32>();
+        a.misc = &d->misc;
+        a.S = S;
+        a.pi = pi;
+        a.dyn = d;
+        jit_launch(B.task->jit->brfs_count[pi], sms * 16, 128, &a, c);
+    }
+    device_scan_dev(CountIn{B.counts.as<u32>()}, BaseOut{B.cand_base.as<u64>()}, &d->E, B.cap_layer,
+                    &d->misc.total_cand, B.sums.as<u64>(), c, &d->misc.status);
+    k_g_mid<<<1, 1, 0, c>>>(d, B.cand_base.as<u64>());
+    k_g_clear<<<sms * 4, 256, 0, c>>>(d, S.claimed, S.lost);
+    {
+        dev::BrfsArgs a{};
+        a.frontier = B.state_g.as<u32>();
+        a.cand_base = B.cand_base.as<u64>();
+        a.misc = &d->misc;
+        a.S = S;
+        a.pi = pi;
+        a.dyn = d;
+        jit_launch(B.task->jit->brfs_expand[pi], sms * 10, 128, &a, c);
+    }
+    k_resolve<<<sms * 8, 256, 0, c>>>(S, d);
+    device_scan_dev(WinIn{S.claimed, S.lost}, WinOutDyn{B.state_g.as<u32>(), d}, &d->G, B.cap_flags,
+                    &d->misc.total_new, B.sums.as<u64>(), c, &d->misc.status);
+    k_g_end<<<1, 1, 0, c>>>(d, loop);
+    B2_CUDA(cudaGetLastError());
+    cudaGraph_t captured = nullptr;
+    B2_CUDA(cudaStreamEndCapture(c, &captured));
+    B2_CUDA(cudaGraphInstantiate(&exec, graph, 0));
+    B2_CUDA(cudaGraphLaunch(exec, s));
+    B.launches += 1;
+    B2_CUDA(cudaMemcpyAsync(host, d, sizeof(DevLayerState), cudaMemcpyDeviceToHost, s));
+    const auto t0 = std::chrono::steady_clock::now();
+    stream_wait(s);
+    B.wait_s += std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    const DevLayerState r = *host;
+    B.launches += static_cast<u64>(r.layers + (r.stop ? 0 : 1)) * 11;  // eleven kernels per iteration
+    log.assign(static_cast<size_t>(r.layers) * 3, 0);
+    if (r.layers)
+    {
+        B2_CUDA(cudaMemcpyAsync(log.data(), B.dlog.p, log.size() * sizeof(u64), cudaMemcpyDeviceToHost, s));
+        stream_wait(s);
+    }
+    (void)P;
+    return r;
+}
+
 void run_search(b2_brfs& B, b2_brfs_result& R)
 {
     const auto t0 = std::chrono::steady_clock::now();
@@ -442,13 +671,53 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
             device_scan(CountIn{B.counts.as<u32>()}, BaseOut{B.cand_base.as<u64>()}, E, &misc->total_cand,
                         B.sums.as<u64>(), s, &misc->status);
         B2_CUDA(cudaGetLastError());
-        B.launches += 3;
+        B.launches += 4;
         if (o.timings)
             B2_CUDA(cudaEventRecord(ev[1], s));
     };
     bool counted = false;  // this layer's count already ran (launched with the previous layer), its counters in `next`
     LayerMisc next{};
-    for (;;)
+    bool finished = false;
+    // With the buffers presized (expected_states), no per-layer events and no max_states cut, the layers run as one
+    // graph launch on the device; a layer that outgrows the buffers continues in the host loop below.
+    if (B.task->jit && !o.timings && o.max_states == ~u64{0} && o.expected_states > 0)
+    {
+        DevLayerState init{};
+        init.layer_begin = 0;
+        init.layer_end = 1;
+        init.n_states = 1;
+        init.cand_next = 1;
+        init.max_depth = o.max_depth;
+        init.stop_at_goal = o.stop_at_goal ? 1 : 0;
+        std::vector<u64> log;
+        const DevLayerState r = run_device_layers(B, init, log);
+        if (r.misc.status & kStatusProbeLimit)
+            throw Error(B2_DEVICE_FAULT, "b2_brfs: a hash-set probe ran past its bound");
+        if (r.misc.status & kStatusScanStall)
+            throw Error(B2_DEVICE_FAULT, "b2_brfs: a prefix scan gave up waiting for a tile");
+        if (r.misc.status)
+            throw Error(B2_DEVICE_FAULT, "b2_brfs: device status " + std::to_string(r.misc.status));
+        u64 end = 1;
+        for (u32 k = 0; k < r.layers; ++k)
+        {
+            counts.push_back({log[3 * k], log[3 * k + 1], log[3 * k + 2]});
+            B.layer_begin.push_back(end);
+            end += log[3 * k + 2];
+        }
+        layers = r.layers;
+        expanded = r.expanded;
+        generated = r.generated;
+        goals = r.goals;
+        solved = r.solved != 0;
+        goal_id = r.goal_id;
+        exhausted = r.exhausted != 0;
+        cand_next = r.cand_next;
+        B.n_states = r.n_states;
+        layer_begin = r.layer_begin;
+        layer_end = r.layer_end;
+        finished = r.done != 0;
+    }
+    while (!finished)
     {
         const u64 E = layer_end - layer_begin;
         if (E == 0)
@@ -530,7 +799,7 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
                 B2_CUDA(cudaEventRecord(ev[3], s));
             device_scan(WinIn{S.claimed, S.lost}, WinOut{B.state_g.as<u32>() + B.n_states, cand_next}, G,
                         &misc->total_new, B.sums.as<u64>(), s, &misc->status);
-            B.launches += 2;
+            B.launches += 3;
             if (o.timings)
                 B2_CUDA(cudaEventRecord(ev[4], s));
             // The next layer's count, launched now over this layer's new states (at most G, their number still on
@@ -854,13 +1123,15 @@ void b2_brfs_destroy(b2_brfs* search)
     {
         for (DeviceBuffer* b : {&search->rows, &search->hash, &search->par, &search->kid, &search->state_g,
                                 &search->table, &search->counts, &search->cand_base, &search->flags, &search->deferred,
-                                &search->sums, &search->misc})
+                                &search->sums, &search->misc, &search->dstate, &search->dlog})
             b->reset();
         // the status mirror goes back to the context's pool once no copy into it can be pending
         stream_drain(search->stream);
         if (search->own_stream)
             cudaStreamDestroy(search->stream);
     }
+    if (search->capture)
+        cudaStreamDestroy(search->capture);
     search->task->ctx->pinned.give(search->misc_host);
     delete search;
 }

@@ -14,6 +14,7 @@ namespace
 using dev::insert;
 using dev::kEmpty;
 using dev::LayerMisc;
+using dev::DevLayerState;
 using dev::Store;
 
 template<int OW, int WR>
@@ -357,6 +358,9 @@ struct b2_brfs
     b2::u64 n_states = 0;
     b2::u64 launches = 0;
     double wait_s = 0;  // host time spent waiting for the device's layer results (this search)
+    // the device-driven layer loop: its state, its per-layer log, the stream its body is captured on
+    b2::DeviceBuffer dstate, dlog;
+    cudaStream_t capture = nullptr;
     bool ran = false;
     bool own_stream = false;
     // sharded search (options.comm set)

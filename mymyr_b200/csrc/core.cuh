@@ -321,6 +321,24 @@ struct LayerMisc
     u32 ndeferred;   // inserts left to the resolve pass
 };
 
+/// The state of a BrFS whose layer loop runs on the device (a CUDA graph's while node): the layer's sizes live here,
+/// the kernels of the loop read them, and a few one-thread kernels advance them.
+struct DevLayerState
+{
+    u64 layer_begin, layer_end;  // ids of the current layer's states
+    u64 n_states, cand_next;     // stored states, candidates so far
+    u64 E, E_exp, G;             // the layer's parents, parents expanded, candidates (0 when the layer is skipped)
+    u64 expanded, generated, goals, goal_id;
+    u64 cap_layer, cap_flags, cap_cand, cap_states, table_slots;  // the buffers the loop was built over
+    u64* log;                    // [log_cap, 3] per layer: expanded, generated, new
+    u32 log_cap;
+    u32 layers, max_depth, stop_at_goal;
+    u32 done;                    // the search is over (exhausted, depth bound, goal stop)
+    u32 overflow;                // a buffer is too small for the current layer: left to the host, nothing of it done
+    u32 exhausted, solved, stop, pad;
+    LayerMisc misc;              // the current layer's counters
+};
+
 /// Arguments of the BrFS count / expand kernels.
 struct BrfsArgs
 {
@@ -334,6 +352,8 @@ struct BrfsArgs
     const u64* E_dev;     // count pass: when non-null, the parents are *E_dev (a count still on the device), not E
     u64* hist;            // sharded count pass: successors per owner rank (added to)
     u32 world;            // sharded count pass: ranks
+    const DevLayerState* dyn;  // device-driven loop: frontier = frontier + layer_begin, the parents E (count) or E_exp
+                               // (expand) and the layer's first candidate come from here
 };
 
 // ------------------------------------------------------------------------------------------------ sharded BrFS

@@ -82,10 +82,11 @@ B2_DI u32 count_all(const Row& st)
 template<int PI>
 B2_DI void brfs_count(const BrfsArgs& a)
 {
-    const u64 E = a.E_dev ? *a.E_dev : a.E;
+    const u64 E = a.dyn ? a.dyn->E : a.E_dev ? *a.E_dev : a.E;
+    const u32* frontier = a.dyn ? a.frontier + a.dyn->layer_begin : a.frontier;
     for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < E; i += static_cast<u64>(gridDim.x) * blockDim.x)
     {
-        const u64 g = a.frontier[i];
+        const u64 g = frontier[i];
         const Row st = RowSel<WR>::load(a.S.rows + g * W);
         if (goal(st))
         {
@@ -155,6 +156,16 @@ constexpr u32 kQueue = W <= 4 ? 96u : W <= 6 ? 80u : 64u;
 template<int PI>
 B2_DI void brfs_expand_queued(const BrfsArgs& a)
 {
+    // the layer's parameters: from the arguments, or from the device state of a device-driven loop
+    Store St = a.S;
+    u64 E = a.E;
+    const u32* frontier = a.frontier;
+    if (a.dyn)
+    {
+        St.layer_cand_begin = a.dyn->cand_next;
+        E = a.dyn->E_exp;
+        frontier += a.dyn->layer_begin;
+    }
     __shared__ QEntry q[4][kQueue];  // blockDim.x = 128: four warps
     __shared__ u32 qn[4];
     const u32 wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -162,14 +173,14 @@ B2_DI void brfs_expand_queued(const BrfsArgs& a)
         qn[wid] = 0;
     __syncwarp();
     const u64 stride = static_cast<u64>(gridDim.x) * blockDim.x;
-    for (u64 base = blockIdx.x * static_cast<u64>(blockDim.x) + wid * 32; base < a.E; base += stride)
+    for (u64 base = blockIdx.x * static_cast<u64>(blockDim.x) + wid * 32; base < E; base += stride)
     {
         const u64 i = base + lane;
-        if (i < a.E)
+        if (i < E)
         {
-            const u64 pg = a.frontier[i];
-            const Row st = RowSel<WR>::load(a.S.rows + pg * W);
-            const u64 g0 = a.S.layer_cand_begin + a.cand_base[i];
+            const u64 pg = frontier[i];
+            const Row st = RowSel<WR>::load(St.rows + pg * W);
+            const u64 g0 = St.layer_cand_begin + a.cand_base[i];
             u32 k = 0;
             for_each_schema([&]<int S>() {
                 Run<S, PI>::go(st, [&](const u32* b) {
@@ -187,7 +198,7 @@ B2_DI void brfs_expand_queued(const BrfsArgs& a)
                             e.k = k;
                         }
                         else
-                            insert<static_cast<int>(W)>(a.S, nx, h, g0 + k, static_cast<u32>(i), k);
+                            insert<static_cast<int>(W)>(St, nx, h, g0 + k, static_cast<u32>(i), k);
                     });
                     ++k;
                     return true;
@@ -203,7 +214,7 @@ B2_DI void brfs_expand_queued(const BrfsArgs& a)
 #pragma unroll
             for (int x = 0; x < WR; ++x)
                 r.w[x] = static_cast<u32>(x) < W ? e.w[x < static_cast<int>(W) ? x : 0] : 0;
-            insert<static_cast<int>(W)>(a.S, r, e.h, e.g, e.i, e.k);
+            insert<static_cast<int>(W)>(St, r, e.h, e.g, e.i, e.k);
         }
         __syncwarp();
         if (lane == 0)
@@ -215,21 +226,31 @@ B2_DI void brfs_expand_queued(const BrfsArgs& a)
 template<int PI>
 B2_DI void brfs_expand(const BrfsArgs& a)
 {
+    // the layer's parameters: from the arguments, or from the device state of a device-driven loop
+    Store St = a.S;
+    u64 E = a.E;
+    const u32* frontier = a.frontier;
+    if (a.dyn)
+    {
+        St.layer_cand_begin = a.dyn->cand_next;
+        E = a.dyn->E_exp;
+        frontier += a.dyn->layer_begin;
+    }
     if constexpr (WR > 0)
     {
         brfs_expand_queued<PI>(a);
         return;
     }
-    for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < a.E; i += static_cast<u64>(gridDim.x) * blockDim.x)
+    for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < E; i += static_cast<u64>(gridDim.x) * blockDim.x)
     {
-        const u64 pg = a.frontier[i];
-        const Row st = RowSel<WR>::load(a.S.rows + pg * W);
-        const u64 g0 = a.S.layer_cand_begin + a.cand_base[i];
+        const u64 pg = frontier[i];
+        const Row st = RowSel<WR>::load(St.rows + pg * W);
+        const u64 g0 = St.layer_cand_begin + a.cand_base[i];
         u32 k = 0;
         for_each_schema([&]<int S>() {
             Run<S, PI>::go(st, [&](const u32* b) {
                 with_successor<S>(st, b, [&](const auto& nx, u64 h) {
-                    insert<(WR > 0 ? static_cast<int>(W) : 0)>(a.S, nx, h, g0 + k, static_cast<u32>(i), k);
+                    insert<(WR > 0 ? static_cast<int>(W) : 0)>(St, nx, h, g0 + k, static_cast<u32>(i), k);
                 });
                 ++k;
                 return true;

@@ -113,6 +113,45 @@ def test_brfs_stop_at_goal_matches_reference(ref, make, matcher):
     assert got.layer_counts == want["layer_counts"]
 
 
+@pytest.mark.parametrize("name,make,depth", BRFS_CASES, ids=[c[0] for c in BRFS_CASES])
+@pytest.mark.parametrize("witness", [True, False])
+@pytest.mark.parametrize("presize", ["exact", "small"])
+def test_brfs_device_loop_matches_reference(ref, name, make, depth, witness, presize):
+    """The layer loop as one CUDA graph launch (compiled matcher, buffers presized by expected_states, no per-layer
+    events): the reference's states, ids and node records; with buffers too small for the later layers the search
+    continues in the host loop from the layer that did not fit."""
+    text = make()
+    rt = ref.RefTask(text)
+    t = Task.from_text(text, matcher="compiled")
+    want = rt.brfs(threads=1, max_depth=depth, stop_at_goal=False, witness_pruning=witness, fingerprint=True)
+    expected = want["states"] if presize == "exact" else 64
+    got = b2cuda.brfs(t, max_depth=depth, stop_at_goal=False, witness_pruning=witness, fingerprint=True,
+                      expected_states=expected)
+    for key in ("states", "expanded", "generated", "num_goal_states", "layers", "fingerprint"):
+        assert getattr(got, key) == want[key], key
+    assert got.layer_counts == want["layer_counts"]
+    assert got.exhausted == bool(want["exhausted"]) and got.solved == bool(want["solved"])
+    rows, par, idx = rt.brfs_states(max_depth=depth, witness_pruning=witness)
+    assert np.array_equal(got.state_rows(), rows)
+    p, k = got.nodes()
+    assert np.array_equal(p, par) and np.array_equal(k, idx)
+
+
+@pytest.mark.parametrize("make", [lambda: tasks.tower(7, 0), lambda: tasks.sliding_tile(3, 3, 30, 1),
+                                  lambda: tasks.transport(2, 5, 2, 4)])
+def test_brfs_device_loop_stop_at_goal(ref, make):
+    text = make()
+    rt = ref.RefTask(text)
+    want = rt.brfs(threads=1, stop_at_goal=True, fingerprint=True)
+    t = Task.from_text(text, matcher="compiled")
+    got = b2cuda.brfs(t, stop_at_goal=True, fingerprint=True, expected_states=want["states"] + 1000)
+    for key in ("states", "expanded", "generated", "num_goal_states", "layers", "fingerprint"):
+        assert getattr(got, key) == want[key], key
+    assert got.solved == bool(want["solved"])
+    assert got.layer_counts == want["layer_counts"]
+    assert got.goal_id == b2cuda.brfs(t, stop_at_goal=True).goal_id  # the host loop's first goal state
+
+
 def test_brfs_deterministic_across_runs():
     t = Task.from_text(tasks.sliding_tile(4, 4, 60, 7))
     a = b2cuda.brfs(t, max_depth=13, stop_at_goal=False, fingerprint=True)
@@ -134,6 +173,10 @@ def test_brfs_tile_depth22_full_config(ref):
     assert got.layer_counts == want["layer_counts"]
     assert got.states == want["states"] and got.generated == want["generated"]
     assert got.fingerprint == want["fingerprint"]
+    # the device-driven layer loop (the bench's timed searches run this way)
+    got = b2cuda.brfs(Task.from_text(text), max_depth=22, stop_at_goal=False, fingerprint=True,
+                      expected_states=want["states"])
+    assert got.layer_counts == want["layer_counts"] and got.fingerprint == want["fingerprint"]
 
 
 # ------------------------------------------------------------------------------------------------ expand
