@@ -944,8 +944,6 @@ b2_status b2_brfs_create(b2_task* task, const b2_brfs_options* options, b2_brfs*
             throw std::invalid_argument("b2_brfs_create: null argument");
         if (!task->ctx)
             throw std::invalid_argument("a host-only task (created without a context) cannot run on the device");
-        if (options->max_states != ~uint64_t{0} && options->comm)
-            throw Error(B2_UNSUPPORTED, "b2_brfs: max_states is not supported by the sharded search");
         if (options->comm)
         {
             if (options->comm->device != task->ctx->device)

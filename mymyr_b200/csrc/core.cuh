@@ -374,6 +374,8 @@ struct DistMisc
     u64 sent_self;    // records this rank pushed to itself (the rest of those received came over NVLink)
     u64 recv_me;      // successors of the layer owned by this rank (from the all-reduced per-owner counts)
     u64 recv_max;     // the most successors of the layer any rank owns
+    u64 cut;          // max_states: 1 + the key (parent id << 32 | successor index) of the last state kept (MAX)
+    u64 kept;         // max_states: this rank's new states of the layer with an id below max_states
     u64 next_all;     // new states of the layer over all ranks (the next layer's parents), unpacked on the device
     u64 next_local;   // new states of the layer on this rank (its next local parents)
     u32 goals_all;    // goal parents of the layer over all ranks

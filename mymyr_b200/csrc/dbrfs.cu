@@ -264,6 +264,36 @@ __global__ void k_dassign(DistMisc* misc, u64* __restrict__ gmin, const u32* __r
     }
 }
 
+/// max_states: among this rank's new states of the layer (ids ascending), the ones below max_states (kept), and the key
+/// of state `last` (max_states - 1) if this rank holds it.
+__global__ void k_dcut(const u32* __restrict__ ids, const u32* __restrict__ par, const u32* __restrict__ kid, u64 n,
+                       u64 last, DistMisc* misc)
+{
+    if (threadIdx.x != 0)
+        return;
+    u64 lo = 0, hi = n;  // the first id above last
+    while (lo < hi)
+    {
+        const u64 mid = (lo + hi) / 2;
+        if (ids[mid] <= last)
+            lo = mid + 1;
+        else
+            hi = mid;
+    }
+    misc->kept = lo;
+    misc->cut = lo > 0 && ids[lo - 1] == last ? 1 + ((static_cast<u64>(par[lo - 1]) << 32) | kid[lo - 1]) : 0;
+}
+
+/// max_states: goal states among this rank's parents with an id up to `last_parent` (the parents expanded before the
+/// cut).
+__global__ void k_dcut_goals(DevTask T, const u64* __restrict__ rows, u32 W, const u32* __restrict__ lc,
+                             const u32* __restrict__ ids, u64 n, u64 last_parent, u32* out)
+{
+    for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < n; i += static_cast<u64>(gridDim.x) * blockDim.x)
+        if (ids[i] <= last_parent && goal_holds(T, GlobalRow{rows + static_cast<u64>(lc[i]) * W, W}))
+            atomicAdd(out, 1u);
+}
+
 /// Resets a layer's counter slot.
 __global__ void k_dmisc_init(DistMisc* m)
 {
@@ -557,7 +587,7 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
     u64 layer_begin = 0, layer_end = 1, lb_local = 0, le_local = S.n_local;
     S.layer_begin.assign(1, 0);
     u32 layers = 0;
-    bool exhausted = false, solved = false;
+    bool exhausted = false, solved = false, full = false;
     u64 expanded = 0, generated = 0, goals = 0, goal_id = 0;
     double count_ms = 0, gen_ms = 0, dedup_ms = 0, exchange_ms = 0;
     S.lane = 1;
@@ -643,6 +673,11 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
         }
         if (layers == o.max_depth)
             break;
+        if (S.n_total >= o.max_states)
+        {
+            full = true;  // the store is full before the layer (max_states <= 1)
+            break;
+        }
         ++layers;
         DistMisc* misc = S.misc_at(S.slot);
         DistMisc m1;
@@ -674,28 +709,18 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
         }
         u64 limit = layer_end, G = m1.lm.total_cand;
         bool stop = false;
-        if (m1.goals_all)
+        const u32 layer_goals = m1.goals_all;
+        if (layer_goals && o.stop_at_goal)
         {
-            if (!solved)
+            limit = m1.goal_id;
+            if (limit < layer_end)
             {
-                solved = true;
-                goal_id = m1.goal_id;
+                B2_CUDA(cudaMemcpyAsync(&G, S.gbase.as<u64>() + (limit - layer_begin), 8, cudaMemcpyDeviceToHost, s));
+                comm_sync(comm, s);
             }
-            if (o.stop_at_goal)
-            {
-                limit = m1.goal_id;
-                if (limit < layer_end)
-                {
-                    B2_CUDA(cudaMemcpyAsync(&G, S.gbase.as<u64>() + (limit - layer_begin), 8, cudaMemcpyDeviceToHost, s));
-                    comm_sync(comm, s);
-                }
-                goals += 1;
-                stop = true;
-            }
-            else
-                goals += m1.goals_all;
+            stop = true;
         }
-        const u64 E_exp = limit - layer_begin;
+        u64 E_exp = limit - layer_begin;
         if (S.n_total + G >= (u64{1} << 32) - 1 || S.cand_next + G >= (u64{1} << 32) - 1)
             throw Error(B2_CAPACITY, "b2_brfs: more than 2^32 - 2 states or candidates on a rank");
         u64 N = 0, N_local = 0;
@@ -791,8 +816,9 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
             if (o.timings)
                 B2_CUDA(cudaEventRecord(ev[4], s));
             // the next layer's count, over this layer's new states (at most G on all ranks together), so that one
-            // wait returns both; skipped where this layer is the last (a goal stop or the depth bound)
-            if (!stop && layers < o.max_depth)
+            // wait returns both; skipped where this layer may be the last (a goal stop, the depth bound, or a store
+            // that this layer can fill)
+            if (!stop && layers < o.max_depth && S.n_total + G < o.max_states)
             {
                 ensure_local(S, recv, s);
                 ensure_layer(S, G, s);
@@ -816,6 +842,58 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
                 exchange_ms += x;
             }
         }
+        // the goal parents reached: under stop_at_goal the first one (expansion stops there), else all of them
+        u64 goals_layer = o.stop_at_goal ? (layer_goals ? 1 : 0) : layer_goals;
+        bool goal_reached = layer_goals > 0;
+        if (S.n_total + N >= o.max_states && N > 0)
+        {
+            // max_states: the search stops right after storing state max_states - 1, inside its parent's expansion
+            // (run_flat, src/mymyr/search/brfs.cpp:301-384): the parents up to that parent are expanded, its
+            // successors up to that one generated, the states after it dropped (each rank keeps a prefix of its
+            // id-ordered new states)
+            const u64 last = o.max_states - 1;
+            k_dcut<<<1, 32, 0, s>>>(S.state_id.as<u32>() + S.n_local, S.state_par.as<u32>() + S.n_local,
+                                    S.state_kid.as<u32>() + S.n_local, N_local, last, misc);
+            B2_CUDA(cudaGetLastError());
+            comm_allreduce(comm, &misc->cut, &misc->cut, 1, CommType::U64, CommOp::Max, s);
+            ++B.launches;
+            const DistMisc mc = read_misc(S, comm, s);
+            if (!mc.cut)
+                throw Error(B2_DEVICE_FAULT, "b2_brfs: no rank holds the state at max_states");
+            const u64 pstar = (mc.cut - 1) >> 32, kstar = (mc.cut - 1) & 0xFFFFFFFFull;
+            u64 first = 0;
+            B2_CUDA(cudaMemcpyAsync(&first, S.gbase.as<u64>() + (pstar - layer_begin), 8, cudaMemcpyDeviceToHost, s));
+            comm_sync(comm, s);
+            E_exp = pstar - layer_begin + 1;
+            G = first + kstar + 1;
+            N = o.max_states - S.n_total;
+            N_local = mc.kept;
+            full = stop = true;
+            if (o.stop_at_goal)
+            {
+                goals_layer = 0;  // the layer's first goal parent lies after the cut (the expansion stopped before it)
+                goal_reached = false;
+            }
+            else
+            {
+                B2_CUDA(cudaMemsetAsync(&misc->lm.goals, 0, 4, s));
+                if (El)
+                    k_dcut_goals<<<grid_for(El, 256, sms * 8), 256, 0, s>>>(
+                        T, S.rows.as<u64>(), W, S.state_lc.as<u32>() + lb_local, S.state_id.as<u32>() + lb_local, El,
+                        pstar, &misc->lm.goals);
+                B2_CUDA(cudaGetLastError());
+                comm_allreduce(comm, &misc->lm.goals, &misc->lm.goals, 1, CommType::U32, CommOp::Sum, s);
+                ++B.launches;
+                goals_layer = read_misc(S, comm, s).lm.goals;
+                goal_reached = layer_goals > 0 && m1.goal_id <= pstar;
+            }
+        }
+        if (goal_reached && !solved)
+        {
+            solved = true;
+            goal_id = m1.goal_id;
+        }
+        goals += goals_layer;
         expanded += E_exp;
         generated += G;
         counts.push_back({E_exp, G, N});
@@ -867,7 +945,8 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
     R.wait_ms = S.wait_s * 1000;
     R.kernel_launches = B.launches;
     R.status = solved ? B2_SEARCH_SOLVED
-                      : (exhausted || layers >= o.max_depth ? B2_SEARCH_EXHAUSTED : B2_SEARCH_OUT_OF_STATES);
+                      : full ? B2_SEARCH_OUT_OF_STATES
+                             : (exhausted || layers >= o.max_depth ? B2_SEARCH_EXHAUSTED : B2_SEARCH_OUT_OF_STATES);
     R.rehashes = S.rehashes;
     R.exchanged = S.exchanged;
     R.local_states = S.n_local;

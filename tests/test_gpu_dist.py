@@ -112,6 +112,81 @@ def test_sharded_brfs_matches_reference(ref, world, matcher):
             assert sum(p[1] for p in per_rank) > 0, name  # successors crossed between ranks
 
 
+MAX_STATES_CASES = [
+    ("tower5", tasks.tower(5, 3), None),
+    ("tile3x3_d14", tasks.sliding_tile(3, 3, 30, 0), 14),
+    ("transport_2_4_2", tasks.transport(2, 4, 2, 1), None),
+]
+REF_STATUS = {0: "solved", 1: "exhausted", 2: "out_of_states", 6: "unsolvable"}
+
+
+def _max_states_worker(rank, world, port, limits, out):
+    import torch.distributed as td
+
+    from mymyr_b200 import Context, Task, cuda
+    from mymyr_b200 import dist as bdist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    td.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                          timeout=datetime.timedelta(seconds=120))
+    try:
+        ctx = Context(rank)
+        comm = bdist.Communicator(ctx, timeout_s=60)
+        for name, text, depth in MAX_STATES_CASES:
+            task = Task.from_text(text, ctx)
+            for stop in (False, True):
+                for M in limits[name]:
+                    r = cuda.brfs(task, comm=comm, max_states=M, max_depth=depth, stop_at_goal=stop,
+                                  fingerprint=True)
+                    g = bdist.gather_states(r)
+                    if rank == 0:
+                        out[(name, stop, M)] = {
+                            "got": (r.states, r.expanded, r.generated, r.num_goal_states, r.layers, r.layer_counts,
+                                    r.status, r.fingerprint),
+                            "rows": g["rows"], "parent": g["parent"], "index": g["index"]}
+                    r.close()
+        comm.close()
+        td.barrier()
+    finally:
+        td.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", _worlds())
+def test_sharded_brfs_max_states_matches_reference(ref, world):
+    """max_states on the sharded search: the reference's cut inside the expansion that stores the last state (run_flat)
+    -- counts, per-layer counts, goal count, status, fingerprint, and the kept states, ids and node records."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+
+    from oracle import ref as oref
+
+    limits = {}
+    for name, text, depth in MAX_STATES_CASES:
+        n = oref.RefTask(text).brfs(max_depth=depth, stop_at_goal=False)["states"]
+        limits[name] = sorted({1, 2, 3, 7, n // 3, n // 2 + 1, n - 1, n, n + 3})
+    mgr = mp.get_context("spawn").Manager()
+    out = mgr.dict()
+    mp.start_processes(_max_states_worker, args=(world, _free_port(), limits, out), nprocs=world, join=True,
+                       start_method="spawn")
+    for name, text, depth in MAX_STATES_CASES:
+        rt = oref.RefTask(text)
+        rows, par, idx = rt.brfs_states(max_depth=depth)
+        for stop in (False, True):
+            for M in limits[name]:
+                exp = rt.brfs_limited(M, max_depth=depth, stop_at_goal=stop, fingerprint=True)
+                want = (exp["states"], exp["expanded"], exp["generated"], exp["num_goal_states"], exp["layers"],
+                        exp["layer_counts"], REF_STATUS[exp["status"]], exp["fingerprint"])
+                got = out[(name, stop, M)]
+                assert got["got"] == want, (name, stop, M, got["got"], want)
+                k = exp["states"]
+                np.testing.assert_array_equal(got["rows"], rows[:k], err_msg=f"{name} {M}")
+                np.testing.assert_array_equal(got["parent"], par[:k], err_msg=f"{name} {M}")
+                np.testing.assert_array_equal(got["index"], idx[:k], err_msg=f"{name} {M}")
+
+
 ASTAR_CASES = [
     ("tower5", tasks.tower(5, 3)),
     ("tile3x3", tasks.sliding_tile(3, 3, 30, 0)),
