@@ -282,7 +282,13 @@ b2_status b2_ctx_create(int device, b2_ctx** out)
     });
 }
 
-void b2_ctx_destroy(b2_ctx* ctx) { delete ctx; }
+void b2_ctx_destroy(b2_ctx* ctx)
+{
+    if (!ctx)
+        return;
+    cudaSetDevice(ctx->device);  // the kept buffers are freed on this device
+    delete ctx;
+}
 
 b2_status b2_task_desc_read_text(const char* text, size_t len, b2_task_desc** out)
 {

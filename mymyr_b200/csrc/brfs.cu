@@ -191,6 +191,9 @@ struct WinOutDyn
 // k_g_clear, the expansion, the resolve pass, the winners scan, k_g_end (which sets the loop's condition). A layer that
 // does not fit the buffers the graph was built over is left untouched (overflow) for the host loop.
 
+/// The loop's initial state.
+__global__ void k_g_init(DevLayerState* d, DevLayerState v) { *d = v; }
+
 /// Layer start: the end conditions, the layer's parents, its counters.
 __global__ void k_g_begin(DevLayerState* d)
 {
@@ -467,6 +470,86 @@ LayerMisc read_misc(b2_brfs& B, LayerMisc* other = nullptr)
     return B.misc_host[B.slot];
 }
 
+/// A finished one-GPU search's device buffers and layer-loop graph, kept in its context for the next search there
+/// (b2_ctx::brfs_cache): repeated searches skip the allocations and the graph's capture and instantiation.
+struct BrfsCache
+{
+    DeviceBuffer rows, hash, par, kid, state_g, table, counts, cand_base, flags, deferred, sums, dstate, dlog;
+    u64 cap_cand = 0, cap_states = 0, table_slots = 0, cap_layer = 0, cap_flags = 0;
+    u32 W = 0;
+    cudaGraphExec_t graph_exec = nullptr;
+    std::vector<u64> graph_key;
+    ~BrfsCache()
+    {
+        if (graph_exec)
+            cudaGraphExecDestroy(graph_exec);
+    }
+};
+
+void exchange(b2_brfs& B, BrfsCache& C)
+{
+    DeviceBuffer* mine[] = {&B.rows,   &B.hash,      &B.par,   &B.kid,      &B.state_g, &B.table, &B.counts,
+                            &B.cand_base, &B.flags, &B.deferred, &B.sums, &B.dstate, &B.dlog};
+    DeviceBuffer* kept[] = {&C.rows,   &C.hash,      &C.par,   &C.kid,      &C.state_g, &C.table, &C.counts,
+                            &C.cand_base, &C.flags, &C.deferred, &C.sums, &C.dstate, &C.dlog};
+    for (size_t i = 0; i < std::size(mine); ++i)
+        mine[i]->swap(*kept[i]);
+    std::swap(B.cap_cand, C.cap_cand);
+    std::swap(B.cap_states, C.cap_states);
+    std::swap(B.table_slots, C.table_slots);
+    std::swap(B.cap_layer, C.cap_layer);
+    std::swap(B.cap_flags, C.cap_flags);
+    std::swap(B.graph_exec, C.graph_exec);
+    std::swap(B.graph_key, C.graph_key);
+}
+
+/// At the start of a one-GPU search: the context's kept buffers, if no other search holds them and they were sized for
+/// rows of this width.
+void cache_take(b2_brfs& B)
+{
+    b2_ctx* ctx = B.task->ctx;
+    std::lock_guard lock(ctx->brfs_mu);
+    if (ctx->brfs_cache_busy || !ctx->brfs_cache)
+        return;
+    auto* C = static_cast<BrfsCache*>(ctx->brfs_cache.get());
+    if (C->W != B.W || !C->rows.p)
+        return;
+    exchange(B, *C);
+    ctx->brfs_cache_busy = true;
+    B.from_cache = true;
+    // a buffer regrown during the search is freed in this search's stream order
+    for (DeviceBuffer* b : {&B.rows, &B.hash, &B.par, &B.kid, &B.state_g, &B.table, &B.counts, &B.cand_base, &B.flags,
+                            &B.deferred, &B.sums, &B.dstate, &B.dlog})
+        b->stream = B.stream;
+}
+
+/// When a one-GPU search is released (its stream drained): its buffers and graph go back to the context if they came
+/// from it, or replace the kept ones if no search holds those and they are not larger. What the search ends up holding
+/// is freed by the caller.
+void cache_give(b2_brfs& B)
+{
+    b2_ctx* ctx = B.task->ctx;
+    std::lock_guard lock(ctx->brfs_mu);
+    if (!ctx->brfs_cache)
+        ctx->brfs_cache = std::shared_ptr<void>(new BrfsCache, [](void* p) { delete static_cast<BrfsCache*>(p); });
+    auto* C = static_cast<BrfsCache*>(ctx->brfs_cache.get());
+    if (B.from_cache)
+    {
+        exchange(B, *C);
+        ctx->brfs_cache_busy = false;
+        B.from_cache = false;
+    }
+    else if (!ctx->brfs_cache_busy && B.rows.p && B.cap_cand >= C->cap_cand)
+        exchange(B, *C);
+    else
+        return;
+    C->W = B.W;
+    // kept buffers are freed (if ever) on no particular stream: the search's stream may be gone by then
+    for (DeviceBuffer* b : {&C->rows, &C->hash, &C->par, &C->kid, &C->state_g, &C->table, &C->counts, &C->cand_base,
+                            &C->flags, &C->deferred, &C->sums, &C->dstate, &C->dlog})
+        b->stream = nullptr;
+}
+
 /// Layers the device-driven loop can log.
 constexpr u32 kDeviceLogLayers = 4096;
 
@@ -474,44 +557,85 @@ constexpr u32 kDeviceLogLayers = 4096;
 /// k_g_mid, k_g_clear, expansion, resolve, winners scan, k_g_end), over the buffers as they are now. Runs until the search
 /// ends or a layer does not fit the buffers (DevLayerState::overflow: that layer is left to the host); returns the
 /// final device state (its log copied into `log`).
+void build_device_layers(b2_brfs& B, const std::vector<u64>& key, DevLayerState* d, u32 pi, unsigned sms);
+
 DevLayerState run_device_layers(b2_brfs& B, const DevLayerState& init, std::vector<u64>& log)
 {
     const Program& P = B.task->prog;
     const u32 pi = B.opt.witness_pruning ? 0 : 1;
     const unsigned sms = static_cast<unsigned>(B.task->ctx->sms);
     cudaStream_t s = B.stream;
-    B.dstate.alloc(sizeof(DevLayerState), s);
-    B.dlog.alloc(kDeviceLogLayers * 3 * sizeof(u64), s);
+    if (!B.dstate.p)
+        B.dstate.alloc(sizeof(DevLayerState), s);
+    if (!B.dlog.p)
+        B.dlog.alloc(kDeviceLogLayers * 3 * sizeof(u64), s);
     DevLayerState* d = B.dstate.as<DevLayerState>();
     DevLayerState* host = reinterpret_cast<DevLayerState*>(reinterpret_cast<char*>(B.misc_host) + 128);
     static_assert(128 + sizeof(DevLayerState) <= PinnedPool::kBlock);
-    *host = init;
-    host->log = B.dlog.as<u64>();
-    host->log_cap = kDeviceLogLayers;
-    host->cap_layer = B.cap_layer;
-    host->cap_flags = B.cap_flags;
-    host->cap_cand = B.cap_cand;
-    host->cap_states = B.cap_states;
-    host->table_slots = B.table_slots;
-    B2_CUDA(cudaMemcpyAsync(d, host, sizeof(DevLayerState), cudaMemcpyHostToDevice, s));
-    stream_wait(s);  // the pinned source is reused for the result below
+    DevLayerState v = init;
+    v.log = B.dlog.as<u64>();
+    v.log_cap = kDeviceLogLayers;
+    v.cap_layer = B.cap_layer;
+    v.cap_flags = B.cap_flags;
+    v.cap_cand = B.cap_cand;
+    v.cap_states = B.cap_states;
+    v.table_slots = B.table_slots;
+    k_g_init<<<1, 1, 0, s>>>(d, v);
+    B2_CUDA(cudaGetLastError());
+    ++B.launches;
 
+    // the graph captures the buffers, the capacities the scans are sized for, the hash set's size and the kernels: an
+    // earlier search's graph over the same ones is launched again as it is
+    const std::vector<u64> key = {reinterpret_cast<u64>(B.rows.p),      reinterpret_cast<u64>(B.hash.p),
+                                  reinterpret_cast<u64>(B.par.p),       reinterpret_cast<u64>(B.kid.p),
+                                  reinterpret_cast<u64>(B.state_g.p),   reinterpret_cast<u64>(B.table.p),
+                                  reinterpret_cast<u64>(B.counts.p),    reinterpret_cast<u64>(B.cand_base.p),
+                                  reinterpret_cast<u64>(B.flags.p),     reinterpret_cast<u64>(B.deferred.p),
+                                  reinterpret_cast<u64>(B.sums.p),      reinterpret_cast<u64>(d),
+                                  B.cap_layer,                          B.cap_flags,
+                                  B.table_slots,                        B.W,
+                                  pi,                                   reinterpret_cast<u64>(B.task->jit->brfs_count[pi]),
+                                  reinterpret_cast<u64>(B.task->jit->brfs_expand[pi]), sms};
+    if (!B.graph_exec || B.graph_key != key)
+        build_device_layers(B, key, d, pi, sms);
+    B2_CUDA(cudaGraphLaunch(B.graph_exec, s));
+    B.launches += 1;
+    B2_CUDA(cudaMemcpyAsync(host, d, sizeof(DevLayerState), cudaMemcpyDeviceToHost, s));
+    const auto t0 = std::chrono::steady_clock::now();
+    stream_wait(s);
+    B.wait_s += std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    const DevLayerState r = *host;
+    B.launches += static_cast<u64>(r.layers + (r.stop ? 0 : 1)) * 11;  // eleven kernels per iteration
+    log.assign(static_cast<size_t>(r.layers) * 3, 0);
+    if (r.layers)
+    {
+        B2_CUDA(cudaMemcpyAsync(log.data(), B.dlog.p, log.size() * sizeof(u64), cudaMemcpyDeviceToHost, s));
+        stream_wait(s);
+    }
+    (void)P;
+    return r;
+}
+
+/// Captures and instantiates the device layer loop over the search's current buffers (into B.graph_exec).
+void build_device_layers(b2_brfs& B, const std::vector<u64>& key, DevLayerState* d, u32 pi, unsigned sms)
+{
+    if (B.graph_exec)
+    {
+        cudaGraphExecDestroy(B.graph_exec);
+        B.graph_exec = nullptr;
+    }
     if (!B.capture)
         B2_CUDA(cudaStreamCreateWithFlags(&B.capture, cudaStreamNonBlocking));
     cudaGraph_t graph = nullptr;
-    cudaGraphExec_t exec = nullptr;
     struct GraphGuard
     {
         cudaGraph_t& g;
-        cudaGraphExec_t& e;
         ~GraphGuard()
         {
-            if (e)
-                cudaGraphExecDestroy(e);
             if (g)
                 cudaGraphDestroy(g);
         }
-    } guard{graph, exec};
+    } guard{graph};
     B2_CUDA(cudaGraphCreate(&graph, 0));
     cudaGraphConditionalHandle loop;
     B2_CUDA(cudaGraphConditionalHandleCreate(&loop, graph, 1, cudaGraphCondAssignDefault));
@@ -562,23 +686,8 @@ DevLayerState run_device_layers(b2_brfs& B, const DevLayerState& init, std::vect
     B2_CUDA(cudaGetLastError());
     cudaGraph_t captured = nullptr;
     B2_CUDA(cudaStreamEndCapture(c, &captured));
-    B2_CUDA(cudaGraphInstantiate(&exec, graph, 0));
-    B2_CUDA(cudaGraphLaunch(exec, s));
-    B.launches += 1;
-    B2_CUDA(cudaMemcpyAsync(host, d, sizeof(DevLayerState), cudaMemcpyDeviceToHost, s));
-    const auto t0 = std::chrono::steady_clock::now();
-    stream_wait(s);
-    B.wait_s += std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
-    const DevLayerState r = *host;
-    B.launches += static_cast<u64>(r.layers + (r.stop ? 0 : 1)) * 11;  // eleven kernels per iteration
-    log.assign(static_cast<size_t>(r.layers) * 3, 0);
-    if (r.layers)
-    {
-        B2_CUDA(cudaMemcpyAsync(log.data(), B.dlog.p, log.size() * sizeof(u64), cudaMemcpyDeviceToHost, s));
-        stream_wait(s);
-    }
-    (void)P;
-    return r;
+    B2_CUDA(cudaGraphInstantiate(&B.graph_exec, graph, 0));
+    B.graph_key = key;
 }
 
 void run_search(b2_brfs& B, b2_brfs_result& R)
@@ -612,6 +721,9 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
         return;
     }
     // root
+    cache_take(B);
+    if (B.table_slots)  // kept from an earlier search: emptied (a table grown below is emptied on allocation)
+        B2_CUDA(cudaMemsetAsync(B.table.p, 0xFF, B.table_slots * 8, s));
     const u64 expect = std::max<u64>(o.expected_states, 1024);
     ensure_cand(B, expect * 2, 0);
     ensure_states(B, expect);
@@ -1119,6 +1231,14 @@ void b2_brfs_destroy(b2_brfs* search)
         shard_free(*search);
     if (search->stream)
     {
+        if (!search->shard && search->ran)
+        {
+            // an idle search's buffers (and layer-loop graph) are kept by the context for its next search
+            stream_drain(search->stream);
+            cache_give(*search);
+        }
+        if (search->graph_exec)
+            cudaGraphExecDestroy(search->graph_exec);
         for (DeviceBuffer* b : {&search->rows, &search->hash, &search->par, &search->kid, &search->state_g,
                                 &search->table, &search->counts, &search->cand_base, &search->flags, &search->deferred,
                                 &search->sums, &search->misc, &search->dstate, &search->dlog})

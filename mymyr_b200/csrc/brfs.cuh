@@ -358,9 +358,13 @@ struct b2_brfs
     b2::u64 n_states = 0;
     b2::u64 launches = 0;
     double wait_s = 0;  // host time spent waiting for the device's layer results (this search)
-    // the device-driven layer loop: its state, its per-layer log, the stream its body is captured on
+    // the device-driven layer loop: its state, its per-layer log, the stream its body is captured on, the
+    // instantiated graph and what it was captured over
     b2::DeviceBuffer dstate, dlog;
     cudaStream_t capture = nullptr;
+    cudaGraphExec_t graph_exec = nullptr;
+    std::vector<b2::u64> graph_key;
+    bool from_cache = false;  // the buffers (and graph) came from the context's cache and go back to it
     bool ran = false;
     bool own_stream = false;
     // sharded search (options.comm set)

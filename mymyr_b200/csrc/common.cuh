@@ -205,6 +205,11 @@ struct b2_ctx
     int sms = 0;
     b2::DeviceBuffer scratch;  // per-call scratch of the stream-ordered calls (grown as needed)
     b2::PinnedPool pinned;     // status mirrors of searches on this device
+    // the device buffers and layer-loop graph of a finished one-GPU BrFS, kept for the next search on this context
+    // (brfs.cu: one search holds them at a time)
+    std::mutex brfs_mu;
+    bool brfs_cache_busy = false;
+    std::shared_ptr<void> brfs_cache;
 };
 
 struct b2_task
