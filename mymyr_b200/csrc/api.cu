@@ -1,6 +1,7 @@
 // C ABI: errors, contexts, task descriptions and upload, row hashing.
 
 #include "common.cuh"
+#include "scan.cuh"
 #include "jit.hpp"
 
 #include <atomic>
@@ -444,9 +445,32 @@ unsigned scan_blocks(u64 nb)
 
 namespace b2
 {
-__global__ void k_scan_clear(u64* __restrict__ scratch, u64 words)
+__global__ void __launch_bounds__(1024) k_scan_sums(u64* __restrict__ sums, u64 n_in, const u64* n_dev,
+                                                    u64* __restrict__ total)
 {
-    for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < words; i += static_cast<u64>(gridDim.x) * blockDim.x)
-        scratch[i] = 0;
+    using Scan = cub::BlockScan<u64, 1024>;
+    __shared__ typename Scan::TempStorage tmp;
+    __shared__ u64 carry;
+    const u64 n = scan_count(n_in, n_dev);
+    const u64 nb = (n + kScanTile - 1) / kScanTile;
+    if (threadIdx.x == 0)
+        carry = 0;
+    __syncthreads();
+    for (u64 base = 0; base < nb; base += 1024)
+    {
+        const u64 i = base + threadIdx.x;
+        const u64 v = i < nb ? sums[i] : 0;
+        u64 e, agg;
+        Scan(tmp).ExclusiveSum(v, e, agg);
+        const u64 c = carry;
+        if (i < nb)
+            sums[i] = c + e;
+        __syncthreads();
+        if (threadIdx.x == 0)
+            carry = c + agg;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0)
+        *total = carry;
 }
 }  // namespace b2

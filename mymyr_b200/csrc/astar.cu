@@ -828,7 +828,7 @@ void run_astar(b2_astar& A, b2_astar_result& R)
             A.sums.alloc(scan_scratch_bytes(grow_to(nF, 0)), s);
         device_scan(CountIn{A.counts.as<u32>()}, BaseOut{A.cand_base.as<u64>()}, nF, &misc->lm.total_cand,
                     A.sums.as<u64>(), s, &misc->lm.status);
-        A.launches += 3;
+        A.launches += 4;
         if (A.opt.timings)
             B2_CUDA(cudaEventRecord(ev[1], s));
         k_key_base<<<grid_for(nF, 256, sms * 16), 256, 0, s>>>(A.front.as<u32>(), nF, A.best.as<u64>(),
@@ -938,7 +938,7 @@ void run_astar(b2_astar& A, b2_astar_result& R)
                                                                        static_cast<u32>(fcur), A.next.as<u32>(),
                                                                        A.open.as<u64>());
             B2_CUDA(cudaGetLastError());
-            A.launches += 6;
+            A.launches += 7;
             if (A.opt.timings)
                 B2_CUDA(cudaEventRecord(ev[5], s));
             const AstarMisc mc = read_misc(A);
@@ -1169,7 +1169,7 @@ void run_astar_sharded(b2_astar& A, b2_astar_result& R)
                                                                     A.keyb.as<u64>(), misc);
         B2_CUDA(cudaMemcpyAsync(&misc->gsum, &misc->lm.total_cand, 8, cudaMemcpyDeviceToDevice, s));
         comm_allreduce(comm, &misc->gsum, &misc->gsum, 1, CommType::U64, CommOp::Sum, s);
-        A.launches += 3;
+        A.launches += 4;
         const AstarMisc m1 = read_misc_sync(A);
         const u64 Gl = m1.lm.total_cand, Gt = m1.gsum;
         if (Gt > 0)
@@ -1274,7 +1274,7 @@ void run_astar_sharded(b2_astar& A, b2_astar_result& R)
                                                                             static_cast<u32>(fcur), A.next.as<u32>(),
                                                                             A.open.as<u64>());
                 B2_CUDA(cudaGetLastError());
-                A.launches += 5;
+                A.launches += 6;
             }
         }
         // the ranks' next waves and best goal (global ids: rank << 27 | state)

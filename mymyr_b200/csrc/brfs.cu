@@ -605,7 +605,7 @@ DevLayerState run_device_layers(b2_brfs& B, const DevLayerState& init, std::vect
     stream_wait(s);
     B.wait_s += std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
     const DevLayerState r = *host;
-    B.launches += static_cast<u64>(r.layers + (r.stop ? 0 : 1)) * 11;  // eleven kernels per iteration
+    B.launches += static_cast<u64>(r.layers + (r.stop ? 0 : 1)) * 13;  // thirteen kernels per iteration
     log.assign(static_cast<size_t>(r.layers) * 3, 0);
     if (r.layers)
     {
@@ -783,7 +783,7 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
             device_scan(CountIn{B.counts.as<u32>()}, BaseOut{B.cand_base.as<u64>()}, E, &misc->total_cand,
                         B.sums.as<u64>(), s, &misc->status);
         B2_CUDA(cudaGetLastError());
-        B.launches += 4;
+        B.launches += 5;
         if (o.timings)
             B2_CUDA(cudaEventRecord(ev[1], s));
     };
@@ -911,7 +911,7 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
                 B2_CUDA(cudaEventRecord(ev[3], s));
             device_scan(WinIn{S.claimed, S.lost}, WinOut{B.state_g.as<u32>() + B.n_states, cand_next}, G,
                         &misc->total_new, B.sums.as<u64>(), s, &misc->status);
-            B.launches += 3;
+            B.launches += 4;
             if (o.timings)
                 B2_CUDA(cudaEventRecord(ev[4], s));
             // The next layer's count, launched now over this layer's new states (at most G, their number still on

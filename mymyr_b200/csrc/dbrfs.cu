@@ -657,7 +657,7 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
             device_scan(CountIn{S.counts.as<u32>()}, BaseOut{S.local_base.as<u64>()}, El, &misc->total_local,
                         S.sums.as<u64>(), s, &misc->lm.status);
         }
-        B.launches += 7;
+        B.launches += 9;
         if (o.timings)
             B2_CUDA(cudaEventRecord(ev[1], s));
     };
@@ -812,7 +812,7 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
                                               S.state_kid.as<u32>());
             B2_CUDA(cudaGetLastError());
             S.gmin_clean = true;
-            B.launches += 5;
+            B.launches += 6;
             if (o.timings)
                 B2_CUDA(cudaEventRecord(ev[4], s));
             // the next layer's count, over this layer's new states (at most G on all ranks together), so that one
