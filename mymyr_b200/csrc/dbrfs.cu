@@ -370,6 +370,9 @@ struct ShardState
     u64 cap_g = 0, cap_recv = 0;
     bool gmin_clean = false;  // gmin all ones (false after an interrupted layer)
     u32 lane = 1;             // bytes per count lane (1, or 4 once a parent had more than 255 successors)
+    // per-owner successor counts in the count pass (hashing every successor there), which size each rank's buffers to
+    // its own share; with two ranks the bound by the layer's candidates is at most twice that, and cheaper
+    bool owner_counts = false;
     DeviceBuffer small;  // hist[world] | fingerprints[world]
     DeviceBuffer misc, sums;  // misc: two counter slots, alternating between layers
     DistMisc* misc_host = nullptr;  // pinned mirror of both slots
@@ -591,6 +594,7 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
     u64 expanded = 0, generated = 0, goals = 0, goal_id = 0;
     double count_ms = 0, gen_ms = 0, dedup_ms = 0, exchange_ms = 0;
     S.lane = 1;
+    S.owner_counts = world > 2;
     std::vector<std::array<u64, 3>> counts;
     u64* fill = nullptr;  // this rank's receive-buffer cursor (mapped on the first exchange)
     // The count pass of a layer into counter slot `misc`: the local parents' successor counts and goals, their local
@@ -621,12 +625,18 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
                 a.pi = pi;
                 a.hist = S.hist();
                 a.world = world;
-                jit_launch(B.task->jit->dbrfs_count[pi], grid, 128, &a, s);
+                jit_launch(S.owner_counts ? B.task->jit->dbrfs_count[pi] : B.task->jit->brfs_count[pi], grid, 128,
+                           &a, s);
             }
-            else
+            else if (S.owner_counts)
                 dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
                     k_dcount<OW, WR><<<grid, 128, 0, s>>>(T, pi, S.rows.as<u64>(), W, frontier, El, El_dev,
                                                           S.counts.as<u32>(), &misc->lm, S.hist(), world);
+                });
+            else
+                dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
+                    k_count<OW, WR><<<grid, 128, 0, s>>>(T, pi, S.rows.as<u64>(), W, frontier, El,
+                                                         S.counts.as<u32>(), &misc->lm, El_dev);
                 });
             ++B.launches;
         }
@@ -726,10 +736,11 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
         u64 N = 0, N_local = 0;
         if (E_exp > 0 && G > 0)
         {
-            // this rank receives recv_me records (no rank more than recv_max): the per-owner counts of the count pass
-            const u64 recv = m1.recv_me;
+            // this rank receives recv_me records (no rank more than recv_max): the per-owner counts of the count pass;
+            // without them, at most the layer's G
+            const u64 recv = S.owner_counts ? m1.recv_me : G;
             ensure_g(S, G, recv, s);
-            ensure_recv(comm, W, m1.recv_max, s);
+            ensure_recv(comm, W, S.owner_counts ? m1.recv_max : G, s);
             fill = static_cast<u64*>(comm->cursors.local.p);
             if (!B.task->jit && S.cap_staging < m1.total_local)
             {
