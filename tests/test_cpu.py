@@ -4,6 +4,7 @@ deterministic."""
 
 import hashlib
 import re
+import os
 from pathlib import Path
 
 import numpy as np
@@ -13,7 +14,8 @@ from mymyr_b200 import _lib, tasks
 from mymyr_b200.task import Task
 
 ROOT = Path(__file__).resolve().parent.parent
-REF_TASKS = Path("/root/reference/tests/data/tasks")
+# the reference checkout (read-only; present where the oracle is built, absent on GPU boxes)
+REF_TASKS = Path(os.environ.get("MYMYR_REFERENCE", "/root/reference")) / "tests" / "data" / "tasks"
 
 
 def declared_symbols():

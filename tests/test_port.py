@@ -2,6 +2,7 @@
 (tests/cpp/support/suite.hpp:31-54 of maichmueller/mymyr), its Philox known answers, and the compiled reference
 (oracle/_ref) on the generated benchmark tasks."""
 
+import os
 from pathlib import Path
 
 import numpy as np
@@ -9,7 +10,8 @@ import pytest
 
 from mymyr_b200 import tasks
 
-REF_TASKS = Path("/root/reference/tests/data/tasks")
+# the reference checkout (read-only; present where the oracle is built, absent on GPU boxes)
+REF_TASKS = Path(os.environ.get("MYMYR_REFERENCE", "/root/reference")) / "tests" / "data" / "tasks"
 
 
 @pytest.fixture(scope="module")
