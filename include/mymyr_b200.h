@@ -170,9 +170,12 @@ b2_status b2_expand(b2_task* task, const uint64_t* states, uint64_t rows, uint32
  * has no counterpart in the reference. Same arguments, results and errors as b2_expand; it calls no cudaMalloc,
  * cudaFree or other allocating routine. Its scratch is a fixed array in the library's device memory (about 3 MB, held
  * by every GPU that loads the library until the process exits), so a call takes at most 2^18 (state, schema) segments
- * (rows x schemas) and refuses larger batches with B2_CAPACITY. The first call on a device looks up the array's
- * device address (once per device), so make that first call before any stream capture. All calls share the array:
- * calls that overlap on the GPU (other streams, other threads) race and must be serialized by the caller. */
+ * (rows x schemas) and refuses larger batches with B2_CAPACITY. Whatever it needs is set up before its first call:
+ * b2_ctx_create loads the array and the call's kernels on the device and looks up the array's device address (once
+ * per context), b2_task_create loads the task's compiled kernels. All calls on a device share the one array, which
+ * keeps the last call's contents (each call zeroes what must start at zero); two calls running on the GPU at the same
+ * time would race on it, so the library runs them one at a time: a process-wide lock, and each call returns only
+ * after its stream has finished the work. */
 b2_status b2_expand_noalloc(b2_task* task, const uint64_t* states, uint64_t rows, uint32_t words, int witness_pruning,
                             b2_expansion* out, void* stream);
 
@@ -214,6 +217,9 @@ typedef struct b2_brfs_options {
     int32_t world_size;       /* multi-GPU: ranks sharing the frontier by state-hash owner (1: one GPU) */
     void* stream;             /* the stream the search runs on (NULL: a stream of its own) */
     b2_comm* comm;            /* multi-GPU: the ranks' communicator (NULL: one GPU) */
+    uint64_t max_exchange_records; /* multi-GPU: the most successor records a rank takes in per layer (0: as many
+                                    * as the layer needs; the receive buffers grow to them). A layer that needs more
+                                    * fails on every rank with B2_CAPACITY: records past a buffer are never written */
 } b2_brfs_options;
 
 void b2_brfs_options_default(b2_brfs_options* o);

@@ -279,6 +279,8 @@ b2_status b2_ctx_create(int device, b2_ctx** out)
         B2_CUDA(cudaDeviceGetDefaultMemPool(&pool, device));
         uint64_t keep = ~uint64_t{0};
         B2_CUDA(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep));
+        noalloc_prepare(*c);
+        c->noalloc_host = c->pinned.take();
         *out = c.release();
     });
 }
@@ -288,6 +290,8 @@ void b2_ctx_destroy(b2_ctx* ctx)
     if (!ctx)
         return;
     cudaSetDevice(ctx->device);  // the kept buffers are freed on this device
+    ctx->pinned.give(ctx->noalloc_host);  // freed with the pool
+    ctx->noalloc_host = nullptr;
     delete ctx;
 }
 

@@ -1232,9 +1232,12 @@ void run_astar_sharded(b2_astar& A, b2_astar_result& R)
             const u32 tile = std::min<u32>(kPushThreads, kPushSmemWords / RW);
             u64* cursor = hist;  // the counts were gathered: reuse as this rank's per-owner cursors
             B2_CUDA(cudaMemsetAsync(cursor, 0, world * 8, s));
+            // a record past a receive buffer is dropped and flags the wave (the all-reduce below orders the pushes
+            // before the inserts and sums the flags: every rank then fails the search with B2_CAPACITY)
             k_push<<<grid_for(Gl, tile, sms * 8), kPushThreads, tile * RW * 8, s>>>(
                 A.sstage.as<u64>(), M, reinterpret_cast<u64* const*>(comm->exchange.table.p),
-                reinterpret_cast<unsigned long long*>(cursor), me, world, RW, tile);
+                reinterpret_cast<unsigned long long*>(cursor), me, world, RW, tile, comm->exchange.bytes / (RW * 8),
+                &misc->lm.ndeferred);
             B2_CUDA(cudaGetLastError());
             comm_allreduce(comm, &misc->lm.ndeferred, &misc->lm.ndeferred, 1, CommType::U32, CommOp::Sum, s);
             A.launches += 1;
@@ -1285,6 +1288,8 @@ void run_astar_sharded(b2_astar& A, b2_astar_result& R)
         comm_allreduce(comm, &misc->goal_all, &misc->goal_all, 1, CommType::U64, CommOp::Min, s);
         comm_group_end();
         const AstarMisc m = read_misc_sync(A);
+        if (m.lm.ndeferred)
+            throw Error(B2_CAPACITY, "b2_astar: a wave's successor records did not fit a rank's receive buffer");
         expanded += nF;
         generated += Gl;
         fresh_total += m.nfresh;

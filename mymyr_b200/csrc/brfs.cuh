@@ -159,9 +159,12 @@ constexpr u32 kPushSmemWords = 5120;  // 40 KB of staged records per block (with
 /// owner's run in this rank's region of that owner's receive buffer, and writes the runs with consecutive threads on
 /// consecutive words (coalesced stores over NVLink for the other ranks). This rank's region of owner d starts after
 /// the records of ranks < this one for d (M[s][d]: records of rank s for owner d, all-gathered).
+///
+/// `cap`: records each owner's receive buffer holds. A record that would land past it is dropped and sets *overflow, so
+/// that a sizing error fails the layer instead of writing past another GPU's allocation.
 __global__ void __launch_bounds__(kPushThreads) k_push(const u64* __restrict__ staging, const u64* __restrict__ M,
                                                        u64* const* __restrict__ peers, unsigned long long* cursor,
-                                                       u32 me, u32 world, u32 RW, u32 tile)
+                                                       u32 me, u32 world, u32 RW, u32 tile, u64 cap, u32* overflow)
 {
     extern __shared__ u64 sm[];
     __shared__ u32 cnt[dev::kMaxWorld], start[dev::kMaxWorld];
@@ -217,7 +220,10 @@ __global__ void __launch_bounds__(kPushThreads) k_push(const u64* __restrict__ s
             const u32 sp = q / RW, w = q - sp * RW;
             const u32 rec = order[sp], dd = dst[rec];
             const u64 slot = off[dd] + base[dd] + (sp - start[dd]);
-            peers[dd][slot * RW + w] = sm[rec * RW + w];
+            if (slot < cap)
+                peers[dd][slot * RW + w] = sm[rec * RW + w];
+            else if (w == 0)
+                atomicOr(overflow, 1u);
         }
         __syncthreads();
     }
@@ -229,12 +235,12 @@ __global__ void __launch_bounds__(kPushThreads) k_push(const u64* __restrict__ s
 /// The exchange without a prior all-gather of the per-owner counts: like k_push, but each block reserves each owner's
 /// run by an atomic on that owner's fill cursor (in the owner's memory, over NVLink for the other ranks), so the
 /// records of all senders interleave in the owner's buffer in an order of no meaning (the records carry their keys).
-/// The staged records are the first sum(hist) of the staging area.
+/// The staged records are the first sum(hist) of the staging area. `cap` and `overflow` as for k_push.
 __global__ void __launch_bounds__(kPushThreads) k_push_reserve(const u64* __restrict__ staging,
                                                                const u64* __restrict__ hist, u64* const* __restrict__ peers,
                                                                u64* const* __restrict__ cursors,
                                                                unsigned long long* sent_self, u32 me, u32 world, u32 RW,
-                                                               u32 tile)
+                                                               u32 tile, u64 cap, u32* overflow)
 {
     extern __shared__ u64 sm[];
     __shared__ u32 cnt[dev::kMaxWorld], start[dev::kMaxWorld];
@@ -287,7 +293,10 @@ __global__ void __launch_bounds__(kPushThreads) k_push_reserve(const u64* __rest
             const u32 sp = q / RW, w = q - sp * RW;
             const u32 rec = order[sp], dd = dst[rec];
             const u64 slot = base[dd] + (sp - start[dd]);
-            peers[dd][slot * RW + w] = sm[rec * RW + w];
+            if (slot < cap)
+                peers[dd][slot * RW + w] = sm[rec * RW + w];
+            else if (w == 0)
+                atomicOr(overflow, 1u);
         }
         __syncthreads();
     }

@@ -210,7 +210,18 @@ struct b2_ctx
     std::mutex brfs_mu;
     bool brfs_cache_busy = false;
     std::shared_ptr<void> brfs_cache;
+    // b2_expand_noalloc: the device address of its scratch array on this device, and a pinned word pair for its
+    // results (both set up by b2_ctx_create, so that the call itself allocates nothing)
+    void* noalloc_scratch = nullptr;
+    void* noalloc_host = nullptr;
 };
+
+namespace b2
+{
+/// Sets up b2_expand_noalloc on the context's device (current): loads the module that holds its scratch array and the
+/// kernels it launches, and records the array's device address in ctx.noalloc_scratch (expand.cu).
+void noalloc_prepare(b2_ctx& ctx);
+}  // namespace b2
 
 struct b2_task
 {

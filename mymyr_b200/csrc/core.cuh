@@ -407,6 +407,8 @@ struct DExpandArgs
     u64* const* peers;       // fused push: each rank's receive buffer (peer memory)
     u64* const* cursors;     // fused push: each rank's fill cursor (peer memory)
     unsigned long long* sent_self;  // fused push: records pushed to this rank
+    u64 recv_cap;            // fused push: records each rank's receive buffer holds; a record past it is dropped
+    u32* overflow;           // fused push: set to 1 when a record was dropped (reduced over the ranks by the host)
 };
 
 /// Arguments of the env kernels (b2_env_batch and b2_step_out, flattened).

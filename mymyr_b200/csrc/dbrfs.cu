@@ -141,9 +141,11 @@ struct LaneIn
 /// first *fill of the buffer (its cursor, advanced by all senders).
 __global__ void k_dinsert(const u64* __restrict__ recv, const u64* fill, u64* __restrict__ rows, u64* __restrict__ hash,
                           u64* table, u64 mask, u32 max_probe, u64 cand_begin, u32 W, unsigned long long* gmin,
-                          DistMisc* misc)
+                          DistMisc* misc, u64 cap)
 {
-    const u64 n = *fill;
+    // the fill cursor counts every reservation, also those a sender dropped past the buffer (its overflow flag fails
+    // the layer on every rank): only the records that fit are read
+    const u64 n = min(*fill, cap);
     if (blockIdx.x == 0 && threadIdx.x == 0)
     {
         misc->recv = n;
@@ -742,6 +744,11 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
             ensure_g(S, G, recv, s);
             ensure_recv(comm, W, S.owner_counts ? m1.recv_max : G, s);
             fill = static_cast<u64*>(comm->cursors.local.p);
+            // records a receive buffer holds (the same on every rank), at most options.max_exchange_records: the push
+            // kernels drop a record past it and flag the layer, which then fails on every rank with B2_CAPACITY
+            u64 recv_cap = comm->exchange.bytes / (RW * 8);
+            if (o.max_exchange_records)
+                recv_cap = std::min<u64>(recv_cap, o.max_exchange_records);
             if (!B.task->jit && S.cap_staging < m1.total_local)
             {
                 S.cap_staging = grown(m1.total_local, S.cap_staging);
@@ -779,6 +786,8 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
                 a.peers = reinterpret_cast<u64* const*>(comm->exchange.table.p);
                 a.cursors = reinterpret_cast<u64* const*>(comm->cursors.table.p);
                 a.sent_self = reinterpret_cast<unsigned long long*>(&misc->sent_self);
+                a.recv_cap = recv_cap;
+                a.overflow = &misc->barrier;
                 const unsigned grid = grid_for(El, 128, sms * 64);
                 if (fused)
                     jit_launch(B.task->jit->dbrfs_push[pi], grid, 128, &a, s);
@@ -796,10 +805,12 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
                 k_push_reserve<<<grid_for(m1.total_local, tile, sms * 8), kPushThreads, tile * RW * 8, s>>>(
                     S.staging.as<u64>(), S.hist(), reinterpret_cast<u64* const*>(comm->exchange.table.p),
                     reinterpret_cast<u64* const*>(comm->cursors.table.p),
-                    reinterpret_cast<unsigned long long*>(&misc->sent_self), me, world, RW, tile);
+                    reinterpret_cast<unsigned long long*>(&misc->sent_self), me, world, RW, tile, recv_cap,
+                    &misc->barrier);
                 B2_CUDA(cudaGetLastError());
                 ++B.launches;
             }
+            // orders the pushes before the inserts; its sum is the number of ranks that dropped a record
             comm_allreduce(comm, &misc->barrier, &misc->barrier, 1, CommType::U32, CommOp::Sum, s);
             if (o.timings)
                 B2_CUDA(cudaEventRecord(ev[6], s));
@@ -807,7 +818,7 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
             k_dinsert<<<sms * 8, 256, 0, s>>>(static_cast<const u64*>(comm->exchange.local.p), fill, S.rows.as<u64>(),
                                               S.hash.as<u64>(), S.table.as<u64>(), S.table_slots - 1,
                                               max_probe(S.table_slots), S.cand_next, W,
-                                              S.gmin.as<unsigned long long>(), misc);
+                                              S.gmin.as<unsigned long long>(), misc, std::min(recv_cap, S.cap_recv));
             B2_CUDA(cudaGetLastError());
             if (o.timings)
                 B2_CUDA(cudaEventRecord(ev[3], s));
@@ -838,6 +849,10 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
                 counted = true;
             }
             const DistMisc m3 = read_misc(S, comm, s, &next);
+            if (m3.barrier)  // the same sum on every rank: all of them fail here
+                throw Error(B2_CAPACITY, "b2_brfs: a layer's successor records did not fit a rank's receive buffer (" +
+                                             std::to_string(recv_cap) + " records); " + std::to_string(m3.barrier) +
+                                             " rank(s) dropped records");
             N = m3.new_packed & 0xFFFFFFFFull;
             N_local = m3.new_packed >> 32;
             S.cand_next += m3.recv;

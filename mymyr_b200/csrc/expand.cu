@@ -88,7 +88,7 @@ __global__ void k_offsets(const u64* __restrict__ seg_off, u64 rows, u32 nschema
                           i32* __restrict__ offsets)
 {
     for (u64 r = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; r <= rows; r += static_cast<u64>(gridDim.x) * blockDim.x)
-        offsets[r] = static_cast<i32>(r < rows ? seg_off[r * nschemas] : *total);
+        offsets[r] = nschemas == 0 ? 0 : static_cast<i32>(r < rows ? seg_off[r * nschemas] : *total);
 }
 }  // namespace
 }  // namespace b2
@@ -188,6 +188,12 @@ extern "C" b2_status b2_expand(b2_task* task, const uint64_t* states, uint64_t r
 // device-wide synchronization of cudaMalloc/cudaFree is unacceptable. Its scratch (per-segment counts and offsets, the
 // scan's block sums, the total and a status word) lives in a file-scope __device__ array of kNoAllocScratchBytes
 // that every GPU loading this library holds until the process exits.
+//
+// Everything that needs memory is set up before the first call: b2_ctx_create (noalloc_prepare) loads this file's
+// module on the device, which places the array in device memory, loads the kernels the call launches and records the
+// array's device address (cudaGetSymbolAddress, with the device current: the array's host-side name is not a device
+// address); it also takes the pinned word pair the call reads its results into. The task's compiled kernels are loaded
+// by b2_task_create.
 
 namespace b2
 {
@@ -202,27 +208,38 @@ constexpr size_t kNoAllocScratchBytes = kNoAllocCounts + kNoAllocOffsets + 256 +
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
+/// One b2_expand_noalloc call at a time in this process: the calls share the scratch array (and each context's pinned
+/// result words), and each returns only after its stream has finished, so taking turns keeps them from overlapping.
 std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[256] = {};  // per device: the device address of g_noalloc_scratch
 
-/// The device address of the scratch array on `device` (which must be current). The host-side name of the array is
-/// not a device address; its address on each device comes from cudaGetSymbolAddress, once per device.
-void* noalloc_scratch(int device)
+template<class K>
+void load_kernel(K* k)
 {
-    if (device < 0 || device >= 256)
-        throw std::invalid_argument("b2_expand_noalloc: device index out of range");
-    std::lock_guard lock(g_noalloc_mu);
-    if (!g_noalloc_ptr[device])
-    {
-        void* p = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (e != cudaSuccess || !p)
-            throw Error(B2_CUDA_ERROR, std::string("b2_expand_noalloc: cudaGetSymbolAddress: ") + cudaGetErrorString(e));
-        g_noalloc_ptr[device] = p;
-    }
-    return g_noalloc_ptr[device];
+    cudaFuncAttributes attr{};
+    B2_CUDA(cudaFuncGetAttributes(&attr, reinterpret_cast<const void*>(k)));
 }
 }  // namespace
+
+void noalloc_prepare(b2_ctx& ctx)
+{
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+        throw Error(B2_CUDA_ERROR, std::string("b2_expand_noalloc set-up: cudaGetSymbolAddress: ") +
+                                       cudaGetErrorString(e));
+    ctx.noalloc_scratch = p;
+    // the kernels of the call, loaded now (lazy module loading would otherwise load them at its first launch)
+    load_kernel(k_offsets);
+    load_kernel(k_tile_reduce<SegCountIn>);
+    load_kernel(k_scan_sums);
+    load_kernel(k_tile_apply<SegCountIn, SegCountOut>);
+    for (u32 ow = 1; ow <= 4; ++ow)
+        for (u32 words : {1u, 2u, 4u, 8u, 9u})
+            dispatch_shapes(ow, words, [&]<int OW, int WR>() {
+                load_kernel(k_expand_count<OW, WR>);
+                load_kernel(k_expand_write<OW, WR>);
+            });
+}
 }  // namespace b2
 
 extern "C" b2_status b2_expand_noalloc(b2_task* task, const uint64_t* states, uint64_t rows, uint32_t words,
@@ -241,6 +258,8 @@ extern "C" b2_status b2_expand_noalloc(b2_task* task, const uint64_t* states, ui
             throw std::invalid_argument("b2_expand_noalloc: label width below the largest schema arity");
         if (out->succ && out->words < P.words)
             throw std::invalid_argument("b2_expand_noalloc: successor rows narrower than the task's words");
+        if (rows > (u64{1} << 31) - 1)
+            throw std::invalid_argument("b2_expand_noalloc: more than 2^31 - 1 states");
         if (witness_pruning && task->witness_refused)
             throw Error(B2_UNSUPPORTED, "witness pruning with a witness parameter before an effect parameter");
         const u64 nseg = rows * P.nschemas;
@@ -249,17 +268,22 @@ extern "C" b2_status b2_expand_noalloc(b2_task* task, const uint64_t* states, ui
                                          std::to_string(P.nschemas) + " schemas exceed its fixed scratch of " +
                                          std::to_string(kNoAllocMaxSegments) +
                                          " (state, schema) segments; use b2_expand or smaller batches");
+        b2_ctx* ctx = task->ctx;
+        if (!ctx->noalloc_scratch || !ctx->noalloc_host)
+            throw Error(B2_CUDA_ERROR, "b2_expand_noalloc: the context was not set up for it");
+        std::lock_guard lock(g_noalloc_mu);
         cudaStream_t s = static_cast<cudaStream_t>(stream);
-        B2_CUDA(cudaSetDevice(task->ctx->device));
-        char* base = static_cast<char*>(noalloc_scratch(task->ctx->device));
+        B2_CUDA(cudaSetDevice(ctx->device));
+        char* base = static_cast<char*>(ctx->noalloc_scratch);
         u32* counts = reinterpret_cast<u32*>(base);
         u64* seg_off = reinterpret_cast<u64*>(base + kNoAllocCounts);
         u64* total = reinterpret_cast<u64*>(base + kNoAllocCounts + kNoAllocOffsets);
         u32* status = reinterpret_cast<u32*>(base + kNoAllocCounts + kNoAllocOffsets + 8);
         u64* sums = reinterpret_cast<u64*>(base + kNoAllocCounts + kNoAllocOffsets + 256);
-        B2_CUDA(cudaMemsetAsync(status, 0, 4, s));  // the array keeps the last call's contents
+        // the array keeps the last call's contents: the status word and the total start at zero
+        B2_CUDA(cudaMemsetAsync(total, 0, 16, s));
         const u32 pi = witness_pruning ? 0 : 1;
-        const unsigned grid = grid_for(nseg, 128, static_cast<unsigned>(task->ctx->sms) * 64);
+        const unsigned grid = grid_for(nseg, 128, static_cast<unsigned>(ctx->sms) * 64);
         dev::ExpandArgs a{};
         a.states = states;
         a.rows = rows;
@@ -282,7 +306,8 @@ extern "C" b2_status b2_expand_noalloc(b2_task* task, const uint64_t* states, ui
             dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
                 k_expand_count<OW, WR><<<grid, 128, 0, s>>>(task->dev, states, rows, words, pi, counts);
             });
-        device_scan(SegCountIn{counts}, SegCountOut{seg_off}, nseg, total, sums, s, status);
+        if (nseg)
+            device_scan(SegCountIn{counts}, SegCountOut{seg_off}, nseg, total, sums, s, status);
         if (nseg && task->jit)
             jit_launch(task->jit->expand_write[pi], grid, 128, &a, s);
         else if (nseg)
@@ -292,11 +317,12 @@ extern "C" b2_status b2_expand_noalloc(b2_task* task, const uint64_t* states, ui
         if (out->offsets)
             k_offsets<<<grid_for(rows + 1, 256), 256, 0, s>>>(seg_off, rows, P.nschemas, total, out->offsets);
         B2_CUDA(cudaGetLastError());
-        u64 gen = 0;
-        u32 st = 0;
-        B2_CUDA(cudaMemcpyAsync(&gen, total, 8, cudaMemcpyDeviceToHost, s));
-        B2_CUDA(cudaMemcpyAsync(&st, status, 4, cudaMemcpyDeviceToHost, s));
+        // total (u64) and status (u32) sit next to each other: one copy into the context's pinned words
+        u64* host = static_cast<u64*>(ctx->noalloc_host);
+        B2_CUDA(cudaMemcpyAsync(host, total, 16, cudaMemcpyDeviceToHost, s));
         B2_CUDA(cudaStreamSynchronize(s));
+        const u64 gen = host[0];
+        const u32 st = static_cast<u32>(host[1]);
         out->generated = gen;
         if (st)
             throw Error(B2_DEVICE_FAULT, "b2_expand_noalloc: device status " + std::to_string(st));

@@ -174,6 +174,13 @@ std::shared_ptr<JitModule> jit_module(int device, const Program& prog)
     m->expand_count[1] = kernel(m->lib, "b2j_expand_count_nw");
     m->expand_write[0] = kernel(m->lib, "b2j_expand_write_w");
     m->expand_write[1] = kernel(m->lib, "b2j_expand_write_nw");
+    // the batched expand's kernels are loaded on the device now, not at their first launch, so that
+    // b2_expand_noalloc's calls load nothing
+    for (cudaKernel_t k : {m->expand_count[0], m->expand_count[1], m->expand_write[0], m->expand_write[1]})
+    {
+        cudaFuncAttributes attr{};
+        B2_CUDA(cudaFuncGetAttributes(&attr, reinterpret_cast<const void*>(k)));
+    }
     std::lock_guard lock(g_mu);
     return g_modules.emplace(std::make_pair(device, key), m).first->second;
 }

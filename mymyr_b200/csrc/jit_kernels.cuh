@@ -338,7 +338,7 @@ B2_DI void dbrfs_expand_push(const DExpandArgs& a)
                 Run<S, PI>::go(st, [&](const u32* b) {
                     with_successor<S>(st, b, [&](const auto& nx, u64 h) {
                         const u32 s = atomicAdd(&qn[wid], 1u);
-                        u64* r;
+                        u64* r = nullptr;
                         if (s < kPushQ)
                             r = Q + s * kRW;
                         else
@@ -347,13 +347,19 @@ B2_DI void dbrfs_expand_push(const DExpandArgs& a)
                             const u64 slot = atomicAdd_system(reinterpret_cast<unsigned long long*>(a.cursors[d]), 1ull);
                             if (d == a.me)
                                 atomicAdd(a.sent_self, 1ull);
-                            r = a.peers[d] + slot * kRW;
+                            if (slot < a.recv_cap)
+                                r = a.peers[d] + slot * kRW;
+                            else
+                                atomicOr(a.overflow, 1u);  // past the owner's buffer: dropped, the layer fails
                         }
+                        if (r)
+                        {
 #pragma unroll
-                        for (u32 x = 0; x < W; ++x)
-                            r[x] = nx.word(x);
-                        r[W] = h;
-                        r[W + 1] = key0 + k;
+                            for (u32 x = 0; x < W; ++x)
+                                r[x] = nx.word(x);
+                            r[W] = h;
+                            r[W + 1] = key0 + k;
+                        }
                     });
                     ++k;
                     return true;
@@ -397,7 +403,11 @@ B2_DI void dbrfs_expand_push(const DExpandArgs& a)
             {
                 const u32 sp = x / kRW, w = x - sp * kRW;
                 const u32 s = order[wid][sp], d = dst[wid][s];
-                a.peers[d][(base[wid][d] + (sp - start[wid][d])) * kRW + w] = Q[s * kRW + w];
+                const u64 slot = base[wid][d] + (sp - start[wid][d]);
+                if (slot < a.recv_cap)
+                    a.peers[d][slot * kRW + w] = Q[s * kRW + w];
+                else if (w == 0)
+                    atomicOr(a.overflow, 1u);  // past the owner's buffer: dropped, the layer fails
             }
             __syncwarp();
             if (lane == 0)

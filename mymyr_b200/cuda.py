@@ -151,12 +151,13 @@ class _Search:
 def brfs(task: Task, ctx: Context | None = None, witness_pruning: bool = True, canonical_order: bool = True,
          max_states: int | None = None, stop_at_goal: bool = True, fingerprint: bool = False,
          chunk_states: int | None = None, expected_states: int | None = None, max_depth: int | None = None,
-         timings: bool = False, stream=None, comm=None) -> BrfsResult:
+         timings: bool = False, stream=None, comm=None, max_exchange_records: int | None = None) -> BrfsResult:
     """The device BrFS (cuda::brfs). Ids, per-layer counts and the fingerprint equal the reference CPU BrFS with
     deterministic ids. ``chunk_states`` is accepted for signature compatibility: layers are never chunked here, and
     ids do not depend on it. ``comm`` (a ``mymyr_b200.dist.Communicator``) shards the search over its ranks by state
     hash: every rank calls brfs together and gets the same result; each rank reads its own states with
-    ``BrfsResult.local``."""
+    ``BrfsResult.local``. ``max_exchange_records`` bounds the successor records a rank takes in per layer (a layer
+    that needs more raises ValueError on every rank, B2_CAPACITY)."""
     if not canonical_order:
         raise ValueError("mymyr_b200 brfs: canonical_order=False is not supported (ids are defined in canonical order)")
     if ctx is not None and task.ctx is not None and ctx.device != task.ctx.device:
@@ -178,6 +179,8 @@ def brfs(task: Task, ctx: Context | None = None, witness_pruning: bool = True, c
     if comm is not None:
         o.comm = comm.handle
         o.world_rank, o.world_size = comm.rank, comm.world
+    if max_exchange_records is not None:
+        o.max_exchange_records = int(max_exchange_records)
     s = _Search(task, o)
     r = s.run()
     res = BrfsResult(status=STATUS.get(r.status, str(r.status)), states=r.states, expanded=r.expanded,

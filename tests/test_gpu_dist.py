@@ -1,6 +1,7 @@
-"""The sharded BrFS on 2+ GPUs (one process per GPU, NCCL) against the reference: the same states, ids, node records,
-hashes, layer counts and fingerprint as the reference's CPU BrFS with deterministic ids, on both matcher backends.
-Skipped on a box with fewer than two GPUs."""
+"""The sharded BrFS (one process per GPU, NCCL) against the reference: the same states, ids, node records, hashes,
+layer counts and fingerprint as the reference's CPU BrFS with deterministic ids, on both matcher backends. World 1 (a
+communicator of one rank, every record pushed to itself through the same kernels) runs on any box; larger worlds are
+skipped on a box with fewer GPUs."""
 
 from __future__ import annotations
 
@@ -80,7 +81,7 @@ def _run(world, matcher):
 
 def _worlds():
     n = torch.cuda.device_count() if torch.cuda.is_available() else 0
-    return sorted({2, n}) if n >= 2 else [2]
+    return sorted({1, 2, n}) if n >= 2 else [1, 2]
 
 
 @pytest.mark.parametrize("matcher", ["compiled", "interpreted"])
@@ -109,7 +110,8 @@ def test_sharded_brfs_matches_reference(ref, world, matcher):
             np.testing.assert_array_equal(got["parent"], par, err_msg=name)
             np.testing.assert_array_equal(got["index"], idx, err_msg=name)
             assert [int(h) for h in got["hashes"]] == [oref.hash_state(r) for r in rows], name
-            assert sum(p[1] for p in per_rank) > 0, name  # successors crossed between ranks
+            if world > 1:
+                assert sum(p[1] for p in per_rank) > 0, name  # successors crossed between ranks
 
 
 MAX_STATES_CASES = [
@@ -244,3 +246,56 @@ def test_sharded_astar_optimal_cost(ref, world, matcher):
         one = cuda.astar(Task.from_text(text, matcher=matcher))
         assert (expanded, generated, states) == (one.expanded, one.generated, one.states), name
         one.close()
+
+
+def _overflow_worker(rank, world, port, matcher, out):
+    import torch.distributed as td
+
+    from mymyr_b200 import Context, Task, cuda
+    from mymyr_b200 import _lib
+    from mymyr_b200 import dist as bdist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    td.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                          timeout=datetime.timedelta(seconds=120))
+    try:
+        ctx = Context(rank)
+        comm = bdist.Communicator(ctx, timeout_s=60)
+        task = Task.from_text(tasks.sliding_tile(3, 3, 30, 0), ctx, matcher=matcher)
+        try:
+            cuda.brfs(task, comm=comm, stop_at_goal=False, max_exchange_records=40)
+            out[("small", rank)] = "ran"
+        except _lib.CapacityError as e:
+            out[("small", rank)] = "capacity: " + str(e)
+        # the context and the communicator stay usable: the same search with room for its records
+        r = cuda.brfs(task, comm=comm, stop_at_goal=False, fingerprint=True)
+        out[("full", rank)] = (r.states, r.fingerprint, r.layer_counts)
+        r.close()
+        comm.close()
+        td.barrier()
+    finally:
+        td.destroy_process_group()
+
+
+@pytest.mark.parametrize("matcher", ["compiled", "interpreted"])
+@pytest.mark.parametrize("world", _worlds())
+def test_sharded_brfs_receive_buffer_overflow_fails_every_rank(ref, world, matcher):
+    """A layer whose records do not fit a rank's receive buffer (bounded here by max_exchange_records) fails with
+    B2_CAPACITY on every rank: the push kernels drop the records past the buffer instead of writing into another GPU's
+    memory, and the next search on the same communicator runs normally."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+
+    mgr = mp.get_context("spawn").Manager()
+    out = mgr.dict()
+    mp.start_processes(_overflow_worker, args=(world, _free_port(), matcher, out), nprocs=world, join=True,
+                       start_method="spawn")
+    exp = ref.RefTask(tasks.sliding_tile(3, 3, 30, 0)).brfs(stop_at_goal=False, fingerprint=True)
+    for r in range(world):
+        assert out[("small", r)].startswith("capacity:"), out[("small", r)]
+        assert "receive buffer" in out[("small", r)]
+        states, fp, lc = out[("full", r)]
+        assert (states, fp, lc) == (exp["states"], exp["fingerprint"], exp["layer_counts"])
