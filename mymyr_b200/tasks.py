@@ -3,11 +3,12 @@
 predicates, as the reference's normalization compiles them. The random source is a self-contained splitmix64, so a
 (generator, seed) pair always yields the same text; parity depends only on the emitted text.
 
-    tower(7, seed=0)                 BASELINE config [1]: 7-block tower stacking, full-space BrFS
-    transport(2, 40, 2, seed=0)      config [2]: two-room gripper transport for the env step
-    sliding_tile(4, 4, 60, seed=0)   config [3]: 4x4 sliding tile, BrFS to depth 22
-    random_domain(seed=0)            config [4]: 24 predicates, 16 schemas of 3-5 parameters, 200 typed objects
-    logistics(8, 4, 6, 2, 30, seed=0)  config [5]: logistics for A* with h^max
+    tower(7, seed=0)                   7-block tower stacking, full-space BrFS
+    transport(2, 40, 2, seed=0)        two-room gripper transport for the batched env step (65,536 envs)
+    sliding_tile(4, 4, 60, seed=0)     4x4 sliding tile, BrFS to depth 22 (the headline workload)
+    random_domain(seed=0)              24 predicates, 16 schemas of 3-5 parameters, 200 typed objects (the lifted
+                                       successor-generation stress test over bernoulli_rows batches)
+    logistics(8, 4, 6, 2, 30, seed=0)  logistics for A* with h^max
 """
 
 from __future__ import annotations
@@ -337,3 +338,49 @@ CONFIGS = {
     "tile4x4": lambda: sliding_tile(4, 4, 60, 0),
     "random": lambda: random_domain(0),
 }
+
+
+# ------------------------------------------------------------------------------------------------ random state batches
+_K_GOLDEN = -7046029254386353131   # 0x9E3779B97F4A7C15 as int64
+_K_MIX1 = -4658895280553007687     # 0xBF58476D1CE4E5B9
+_K_MIX2 = -7723592293110705685     # 0x94D049BB133111EB
+
+
+def _srl(x, k: int):
+    """Logical right shift of int64 tensor bits."""
+    return (x >> k) & ((1 << (64 - k)) - 1)
+
+
+def _mix64(x):
+    """splitmix64's finalizer on int64 tensors (wrapping multiplies, logical shifts)."""
+    x = x ^ _srl(x, 30)
+    x = x * _K_MIX1
+    x = x ^ _srl(x, 27)
+    x = x * _K_MIX2
+    return x ^ _srl(x, 31)
+
+
+def bernoulli_rows(n: int, words: int, slots: int, density: float = 0.05, seed: int = 0, device="cpu",
+                   first: int = 0, chunk: int = 1 << 14):
+    """A batch of n state rows [n, words] (int64 tensor holding the uint64 words) in which each of the first `slots`
+    slots is set independently with probability `density`; slot j of state i is decided by a counter-based draw keyed
+    (seed, first + i, j): splitmix64 of seed * golden + (first + i) * 2^20 + j, set iff its top 24 bits are below
+    round(density * 2^24). The same (seed, state, slot) always gives the same bit, on any device and in any chunking
+    (the successor-generation stress workload draws its 1,048,576 states at 5 % density over every fluent slot)."""
+    import torch
+
+    if slots > (1 << 20) or words * 64 < slots:
+        raise ValueError("bernoulli_rows: slots must fit the words and be below 2^20")
+    thr = int(round(density * (1 << 24)))
+    out = torch.zeros((n, words), dtype=torch.int64, device=device)
+    j = torch.arange(words * 64, dtype=torch.int64, device=device)
+    live = j < slots
+    shifts = torch.arange(64, dtype=torch.int64, device=device)
+    base_seed = (seed * _K_GOLDEN) & ((1 << 63) - 1)
+    for c0 in range(0, n, chunk):
+        c1 = min(n, c0 + chunk)
+        i = torch.arange(first + c0, first + c1, dtype=torch.int64, device=device)
+        key = base_seed + (i[:, None] << 20) + j[None, :]
+        bits = (_srl(_mix64(key), 40) < thr) & live[None, :]
+        out[c0:c1] = (bits.view(c1 - c0, words, 64).to(torch.int64) << shifts).sum(-1)
+    return out

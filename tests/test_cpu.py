@@ -15,7 +15,7 @@ from mymyr_b200.task import Task
 
 ROOT = Path(__file__).resolve().parent.parent
 # the reference checkout (read-only; present where the oracle is built, absent on GPU boxes)
-REF_TASKS = Path(os.environ.get("MYMYR_REFERENCE", "/root/reference")) / "tests" / "data" / "tasks"
+REF_TASKS = Path(os.environ.get("MYMYR_REFERENCE", Path(__file__).resolve().parents[2] / "reference")) / "tests" / "data" / "tasks"
 
 
 def declared_symbols():
@@ -141,3 +141,19 @@ def test_oracle_philox_known_answers(ref):
     for ctr, key, want in kats:
         ref.lib().ref_philox_block(*ctr, *key, out.ctypes.data)
         assert tuple(int(x) for x in out) == want
+
+
+def test_tile_brfs_golden_file_matches_reference(ref):
+    """The golden BrFS results the bench checks its searches against equal the reference's own BrFS (shallow depths;
+    the generating script, tests/golden/make_brfs_golden.py, writes every depth the same way)."""
+    import json
+
+    from mymyr_b200 import tasks
+
+    g = json.loads((ROOT / "tests" / "golden" / "tile4x4_brfs.json").read_text())["depths"]
+    assert all(str(d) in g for d in range(12, 26))
+    rt = ref.RefTask(tasks.sliding_tile(4, 4, 60, 0))
+    for d in (12, 15, 18):
+        r = rt.brfs(threads=4, max_depth=d, stop_at_goal=False, fingerprint=True, store="concurrent")
+        assert g[str(d)]["states"] == r["states"] and g[str(d)]["fingerprint"] == f"{r['fingerprint']:#018x}"
+        assert g[str(d)]["layer_counts"] == [list(x) for x in r["layer_counts"]]

@@ -162,7 +162,7 @@ def test_brfs_deterministic_across_runs():
 
 @pytest.mark.slow
 def test_brfs_tile_depth22_full_config(ref):
-    """BASELINE config [3] at full size: per-layer counts and fingerprint against the reference's multi-threaded BrFS
+    """The 4x4 sliding-tile BrFS to depth 22 at full size: per-layer counts and fingerprint against the reference's multi-threaded BrFS
     (deterministic ids)."""
     import os
 
@@ -215,6 +215,37 @@ def test_expand_matches_reference(ref, name, make, n, density, witness, matcher)
     assert np.array_equal(got.binding.cpu().numpy()[:, :lw], want["binding"])
     assert np.array_equal(as_u64(got.succ_hash), want["succ_hash"])
     assert np.array_equal(as_u64(got.succ), want["succ"])
+
+
+@pytest.mark.parametrize("matcher", MATCHERS)
+def test_expand_full_stress_batch_matches_reference(ref, matcher):
+    """The lifted successor-generation stress workload at its full size: 1,048,576 states of the seeded random domain
+    (24 predicates, 16 schemas of 3-5 parameters, 200 typed objects) with every slot set at 5 % density, witness
+    pruning off, canonical order. Offsets, parents, schemas, bindings and successor hashes equal the reference's
+    rl::expand (its thread-pool overload) element for element; successor rows are compared on the first 8,192
+    states."""
+    import os
+
+    text = tasks.random_domain(0)
+    t = Task.from_text(text, matcher=matcher)
+    n = 1 << 20
+    states = tasks.bernoulli_rows(n, t.words, t.fluent_slots, 0.05, seed=0, device="cuda")
+    host = states.cpu().numpy().view(np.uint64)
+    rt = ref.RefTask(text)
+    got = b2rl.expand(t, states, witness_pruning=False)
+    want = rt.expand(host, witness_pruning=False, threads=max(1, min(32, os.cpu_count() or 1)))
+    assert got.generated == want["generated"] > 5 * n
+    assert np.array_equal(got.offsets.cpu().numpy(), want["offsets"])
+    assert np.array_equal(got.parent.cpu().numpy(), want["parent"])
+    assert np.array_equal(got.schema.cpu().numpy(), want["schema"])
+    lw = want["binding"].shape[1]
+    assert np.array_equal(got.binding.cpu().numpy()[:, :lw], want["binding"])
+    assert np.array_equal(as_u64(got.succ_hash), want["succ_hash"])
+    k = 8192
+    part = b2rl.expand(t, states[:k].contiguous(), witness_pruning=False, succ=True)
+    want_k = rt.expand(host[:k], witness_pruning=False, succ=True)
+    assert np.array_equal(as_u64(part.succ), want_k["succ"])
+    assert np.array_equal(as_u64(part.succ_hash), want_k["succ_hash"])
 
 
 def test_expand_empty_batch():
@@ -289,23 +320,46 @@ def test_env_given_actions_match_reference(ref, matcher):
         assert np.array_equal(env.reward.cpu().numpy(), renv.reward)
 
 
+def _step_digest(reward, terminated, truncated, goal, schema, count, binding):
+    """One step's outputs of every env folded into a few integers (row-weighted sums, exact in int64)."""
+    w = np.arange(1, len(count) + 1, dtype=np.int64)
+    return (int((reward.view(np.int32).astype(np.int64) * w).sum()), int((terminated.astype(np.int64) * w).sum()),
+            int((truncated.astype(np.int64) * w).sum()), int((goal.astype(np.int64) * w).sum()),
+            int((schema.astype(np.int64) * w).sum()), int((count.astype(np.int64) * w).sum()),
+            int((binding.astype(np.int64) * w[:, None]).sum()))
+
+
 @pytest.mark.slow
 def test_env_full_config_digest(ref):
-    """BASELINE config [2] at its batch size (65,536 envs): states and counters after 50 steps, compared in full."""
+    """The batched env step at its full size: 65,536 envs of the two-room transport task (40 balls, 2 grippers), random
+    policy, seed 0, autoreset, for all 1,000 steps. Every step's outputs (rewards, terminated, truncated, goal, chosen
+    schema and binding, successor counts) agree with the reference's HostEnv through a row-weighted digest, and the
+    full state rows and counters are compared every 100 steps and after the last."""
     import os
 
     text = tasks.transport(2, 40, 2, 0)
     rt = ref.RefTask(text)
     t = Task.from_text(text)
-    n = 65536
+    n, steps = 65536, 1000
     env = b2rl.BatchedEnv(t, n, seed=0)
-    renv = ref.RefEnv(rt, n, seed=0, threads=os.cpu_count() or 8)
+    renv = ref.RefEnv(rt, n, seed=0, threads=max(1, min(64, os.cpu_count() or 8)))
     env.reset()
     renv.reset()
-    for _ in range(50):
+    lw = renv.lw
+    resets = 0
+    for s in range(steps):
         env.step()
         renv.step()
-    _compare_env(env, renv)
+        got = _step_digest(env.reward.cpu().numpy(), env.terminated.cpu().numpy(), env.truncated.cpu().numpy(),
+                           env.goal.cpu().numpy(), env.schema.cpu().numpy(), env.count.cpu().numpy(),
+                           env.binding.cpu().numpy()[:, :lw])
+        want = _step_digest(renv.reward, renv.terminated, renv.truncated, renv.goal, renv.schema, renv.count,
+                            renv.binding)
+        assert got == want, s
+        resets += int(renv.terminated.sum())
+        if (s + 1) % 100 == 0:
+            _compare_env(env, renv)
+    assert resets > 0  # some envs reached the goal and were reset within the 1,000 steps
 
 
 MAX_STATES_CASES = [

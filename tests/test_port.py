@@ -11,7 +11,7 @@ import pytest
 from mymyr_b200 import tasks
 
 # the reference checkout (read-only; present where the oracle is built, absent on GPU boxes)
-REF_TASKS = Path(os.environ.get("MYMYR_REFERENCE", "/root/reference")) / "tests" / "data" / "tasks"
+REF_TASKS = Path(os.environ.get("MYMYR_REFERENCE", Path(__file__).resolve().parents[2] / "reference")) / "tests" / "data" / "tasks"
 
 
 @pytest.fixture(scope="module")
