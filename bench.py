@@ -358,6 +358,7 @@ def expand_secondary(args, device, world=1, rank=0, pg=None, with_cpu=False):
                                   chunk=1 << 13)
     L = _lib.lib()
     stream = torch.cuda.Stream(device)
+    stream.wait_stream(torch.cuda.current_stream(device))  # the rows were drawn on the current stream
     sp = stream.cuda_stream
     W, lw = t.words, max(1, t.label_width)
     probe = _lib.Expansion()

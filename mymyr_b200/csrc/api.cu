@@ -183,8 +183,9 @@ void upload(b2_task& t)
     const size_t o_sch = put(P.schemas.data(), P.schemas.size() * sizeof(DSchema));
     const size_t o_dom = put(P.domain.data(), P.domain.size() * 4);
     const size_t o_pdb = put(P.pos_dom_begin.data(), P.pos_dom_begin.size() * 4);
-    const size_t o_srb = put(P.srel_bits.data(), P.srel_bits.size() * 8);
-    const size_t o_srs = put(P.srel_size.data(), P.srel_size.size() * 8);
+    const size_t o_srt = put(P.srel_table.data(), P.srel_table.size() * 8);
+    const size_t o_srm = put(P.srel_mask.data(), P.srel_mask.size() * 8);
+    const size_t o_srp = put(P.srel_probes.data(), P.srel_probes.size() * 8);
     const size_t o_gp = put(P.goal_pos.data(), P.goal_pos.size() * 8);
     const size_t o_gn = put(P.goal_neg.data(), P.goal_neg.size() * 8);
     t.blob.alloc(host.size());
@@ -207,8 +208,9 @@ void upload(b2_task& t)
     D.schemas = reinterpret_cast<const DSchema*>(b + o_sch);
     D.domain = reinterpret_cast<const u32*>(b + o_dom);
     D.pos_dom_begin = reinterpret_cast<const u32*>(b + o_pdb);
-    D.srel_bits = reinterpret_cast<const u64*>(b + o_srb);
-    D.srel_size = reinterpret_cast<const u64*>(b + o_srs);
+    D.srel_table = reinterpret_cast<const u64*>(b + o_srt);
+    D.srel_mask = reinterpret_cast<const u64*>(b + o_srm);
+    D.srel_probes = reinterpret_cast<const u64*>(b + o_srp);
     D.goal_pos = reinterpret_cast<const u64*>(b + o_gp);
     D.goal_neg = reinterpret_cast<const u64*>(b + o_gn);
 }

@@ -85,8 +85,8 @@ struct Gen
         if (l.fluent)
             e << "([&] { const u64 k_ = " << k << "; return k_ < F && bit_of(st, k_); }())";
         else
-            e << "([&] { const u64 k_ = " << k << "; return k_ < " << P.srel_size[l.pred] << "ull && ((POOL["
-              << P.srel_bits[l.pred] << "ull + (k_ >> 6)] >> (k_ & 63)) & 1); }())";
+            e << "static_member(POOL + " << P.srel_table[l.pred] << "ull, " << P.srel_mask[l.pred] << "ull, "
+              << P.srel_probes[l.pred] << "u, " << k << ")";
         return l.neg ? "(!" + e.str() + ")" : e.str();
     }
 

@@ -19,6 +19,7 @@
 #include "task.hpp"
 
 #include <algorithm>
+#include <array>
 #include <bit>
 #include <map>
 #include <set>
@@ -255,23 +256,26 @@ private:
 
 inline u32 obj_of(i32 term) { return static_cast<u32>(-(static_cast<long long>(term) + 1)); }
 
-u64 sat_mul(u64 a, u64 b)
+/// a * b, or kSizeCap once the product passes it (key spaces that large are refused where they arise).
+constexpr u64 kSizeCap = u64{1} << 62;
+u64 capped_product(u64 a, u64 b)
 {
-    constexpr u64 cap = u64{1} << 62;
-    if (a == 0 || b == 0)
-        return 0;
-    if (a > cap / b)
-        return cap;
-    return std::min(cap, a * b);
+    u64 r = 0;
+    return __builtin_mul_overflow(a, b, &r) || r > kSizeCap ? kSizeCap : r;
 }
 
-std::vector<u32> distinct_params(const std::vector<i32>& terms)
+/// The parameters a literal mentions, in the order of their first occurrence (schemas have at most 8).
+std::vector<u32> params_of(const std::vector<i32>& terms)
 {
-    std::vector<u32> v;
+    std::vector<u32> out;
+    u32 seen = 0;
     for (i32 x : terms)
-        if (x >= 0 && std::find(v.begin(), v.end(), static_cast<u32>(x)) == v.end())
-            v.push_back(static_cast<u32>(x));
-    return v;
+        if (x >= 0 && !((seen >> x) & 1u))
+        {
+            seen |= 1u << x;
+            out.push_back(static_cast<u32>(x));
+        }
+    return out;
 }
 
 struct Compiler
@@ -281,12 +285,13 @@ struct Compiler
     std::vector<StaticRel>& S;
     Program& P;
     u32 n = 0, OW = 1;
-    std::vector<std::vector<u64>> s_unary;                    // per static unary predicate
-    std::vector<std::vector<const std::vector<u32>*>> satoms;  // static atoms per predicate
-    std::map<std::tuple<u32, u32, u32>, u64> row_tables;      // (pred, from, to) -> pool offset
+    std::vector<std::vector<const std::vector<u32>*>> sfacts;  // per static predicate: its atoms (task order)
+    std::vector<std::vector<u64>> sunary;                      // per static unary predicate: its object set
+    std::vector<std::array<u64, 2>> sadj;                      // per static binary predicate: adjacency tables
     std::vector<std::vector<std::vector<u64>>> dom0;           // per schema, per parameter: OW words
     std::vector<u64> layout_rs_off;                            // per position: pool offset of rs
-    std::vector<u64> static_rs_off;                            // per static predicate: pool offset of its rs
+    std::vector<u64> static_rs_off;                            // per static predicate: pool offset of its
+                                                               // per-argument key contributions (arity x n)
 
     Compiler(const TaskSpec& t, Layout& l, std::vector<StaticRel>& s, Program& p) : T(t), L(l), S(s), P(p) {}
 
@@ -306,94 +311,99 @@ struct Compiler
         for (const Schema& s : T.schemas)
             if (s.arity > 8)
                 throw std::invalid_argument("mymyr_b200: schema " + s.name + " has more than 8 parameters");
-        statics();
+        index_statics();
         domains();
         layout();
         program();
     }
 
     // ---------------------------------------------------------------------------------------------- statics
-    void statics()
+    /// Indexes every static predicate's atoms (StaticRel): packed keys, sorted, and the open-addressed key set the
+    /// kernels probe (at most half full); unary predicates also as object sets.
+    void index_statics()
     {
         const u32 m = static_cast<u32>(T.kind.size());
-        s_unary.assign(m, {});
-        satoms.assign(m, {});
+        sfacts.assign(m, {});
+        sunary.assign(m, {});
+        sadj.assign(m, {kNoTable, kNoTable});
         S.assign(m, {});
         for (const auto& a : T.static_init)
         {
             if (T.kind[a[0]] != kStatic)
                 throw std::invalid_argument("mymyr_b200: a static initial atom over a non-static predicate");
-            satoms[a[0]].push_back(&a);
+            sfacts[a[0]].push_back(&a);
         }
         for (u32 p = 0; p < m; ++p)
         {
             if (T.kind[p] != kStatic)
                 continue;
-            const u32 ar = T.arity[p];
-            if (ar == 1)
-            {
-                s_unary[p].assign(OW, 0);
-                for (auto* a : satoms[p])
-                    set_bit(s_unary[p].data(), (*a)[1]);
-            }
             StaticRel& R = S[p];
-            R.arity = ar;
-            std::vector<std::vector<u32>> rank(ar, std::vector<u32>(n, ~0u));
-            std::vector<u32> dsize(ar, 0);
-            for (auto* a : satoms[p])
-                for (u32 i = 0; i < ar; ++i)
-                    rank[i][(*a)[1 + i]] = 0;
-            for (u32 i = 0; i < ar; ++i)
-                for (u32 o = 0; o < n; ++o)
-                    if (rank[i][o] == 0)
-                        rank[i][o] = dsize[i]++;
-            u64 size = 1;
-            for (u32 i = 0; i < ar; ++i)
-                size = sat_mul(size, dsize[i]);
-            if (size > (u64{1} << 28))
+            R.arity = T.arity[p];
+            if (R.arity >= 8)
                 throw std::invalid_argument("mymyr_b200: static predicate " + T.pred_names[p] +
-                                            " has a key space above 2^28");
-            R.size = size;
-            R.rs.assign(static_cast<std::size_t>(ar) * n, kStaticOutside);
-            u64 stride = 1;
-            for (u32 i = ar; i-- > 0;)
+                                            " has 8 or more arguments");
+            R.keys.reserve(sfacts[p].size());
+            for (const auto* a : sfacts[p])
+                R.keys.push_back(fact_key(*a));
+            std::sort(R.keys.begin(), R.keys.end());
+            R.keys.erase(std::unique(R.keys.begin(), R.keys.end()), R.keys.end());
+            u64 slots = 8;
+            while (slots < 2 * R.keys.size())
+                slots <<= 1;
+            R.table.assign(slots, kEmptyStaticSlot);
+            R.probes = 1;
+            for (const u64 k : R.keys)
             {
-                for (u32 o = 0; o < n; ++o)
-                    if (rank[i][o] != ~0u)
-                        R.rs[static_cast<std::size_t>(i) * n + o] = rank[i][o] * stride;
-                stride *= std::max<u32>(1, dsize[i]);
+                u64 j = static_key_home(k, slots - 1);
+                u32 run = 1;
+                for (; R.table[j] != kEmptyStaticSlot; j = (j + 1) & (slots - 1))
+                    ++run;
+                R.table[j] = k;
+                R.probes = std::max(R.probes, run);
             }
-            R.bits.assign(std::max<u32>(1, words_for(size)), 0);
-            for (auto* a : satoms[p])
+            if (R.arity == 1)
             {
-                u64 k = 0;
-                for (u32 i = 0; i < ar; ++i)
-                    k += R.rs[static_cast<std::size_t>(i) * n + (*a)[1 + i]];
-                set_bit(R.bits.data(), k);
+                sunary[p].assign(OW, 0);
+                for (const auto* a : sfacts[p])
+                    set_bit(sunary[p].data(), (*a)[1]);
             }
         }
     }
 
-    bool static_ground_holds(const Lit& l) const
+    static constexpr u64 kNoTable = ~u64{0};
+
+    /// The packed key of a static atom record [pred, args...].
+    static u64 fact_key(const std::vector<u32>& a)
     {
-        const StaticRel& R = S[l.pred];
         u64 k = 0;
-        for (u32 i = 0; i < R.arity; ++i)
-            k += R.rs[static_cast<std::size_t>(i) * n + obj_of(l.terms[i])];
-        return k < R.size && test_bit(R.bits.data(), k);
+        for (u32 i = 1; i < a.size(); ++i)
+            k += static_arg_key(i - 1, a[i]);
+        return k;
     }
 
-    /// Pool offset of the n * OW row table of static `pred`: row(a[from]) has bit a[to].
-    u64 static_rows(u32 pred, u32 from, u32 to)
+    /// Whether a ground static literal's atom is a static fact.
+    bool static_fact(const Lit& l) const
     {
-        const auto key = std::make_tuple(pred, from, to);
-        if (auto it = row_tables.find(key); it != row_tables.end())
-            return it->second;
-        const u64 off = P.pool.size();
+        u64 k = 0;
+        for (u32 i = 0; i < l.terms.size(); ++i)
+            k += static_arg_key(i, obj_of(l.terms[i]));
+        return S[l.pred].holds(k);
+    }
+
+    /// The adjacency table of static binary predicate `pred` selected by argument `by` (0 or 1): n object sets of OW
+    /// words in the pool, set o holding the objects o is related to at the other argument. Built on first use.
+    u64 adjacency(u32 pred, u32 by)
+    {
+        u64& off = sadj[pred][by];
+        if (off != kNoTable)
+            return off;
+        off = P.pool.size();
         P.pool.resize(off + static_cast<std::size_t>(n) * OW, 0);
-        for (auto* a : satoms[pred])
-            set_bit(P.pool.data() + off + static_cast<std::size_t>((*a)[1 + from]) * OW, (*a)[1 + to]);
-        row_tables.emplace(key, off);
+        for (const auto* a : sfacts[pred])
+        {
+            const u32 sel = (*a)[1 + by], other = (*a)[2 - by];
+            set_bit(P.pool.data() + off + static_cast<std::size_t>(sel) * OW, other);
+        }
         return off;
     }
 
@@ -416,13 +426,13 @@ struct Compiler
             for (const Lit& l : sc.pre)
             {
                 const bool fluent = T.kind[l.pred] != kStatic;
-                const auto vars = distinct_params(l.terms);
+                const auto vars = params_of(l.terms);
                 if (vars.empty() || fluent)
                     continue;
                 const u32 ar = T.arity[l.pred];
                 if (ar == 1)
                 {
-                    and_words(vars[0], s_unary[l.pred].data(), !l.pos);
+                    and_words(vars[0], sunary[l.pred].data(), !l.pos);
                     continue;
                 }
                 if (ar == 2 && l.terms[0] != l.terms[1])
@@ -432,7 +442,7 @@ struct Compiler
                         continue;
                     const u32 fpos = f0 ? 0 : 1, opos = 1 - fpos;
                     const u32 v = static_cast<u32>(l.terms[fpos]);
-                    const u64 off = static_rows(l.pred, opos, fpos);
+                    const u64 off = adjacency(l.pred, opos);
                     and_words(v, P.pool.data() + off + static_cast<std::size_t>(obj_of(l.terms[opos])) * OW, !l.pos);
                     continue;
                 }
@@ -441,7 +451,7 @@ struct Compiler
                         if (l.terms[i] >= 0)
                         {
                             std::vector<u64> proj(OW, 0);
-                            for (auto* a : satoms[l.pred])
+                            for (const auto* a : sfacts[l.pred])
                             {
                                 bool ok = true;
                                 for (u32 j = 0; j < ar && ok; ++j)
@@ -517,7 +527,7 @@ struct Compiler
                     if (test_bit(bits[p][i].data(), o))
                         L.domain.push_back(o);
                 L.dsize[pos] = static_cast<u32>(L.domain.size() - L.dom_begin[pos]);
-                size = sat_mul(size, L.dsize[pos]);
+                size = capped_product(size, L.dsize[pos]);
             }
             u64 st = 1;
             for (u32 i = ar; i-- > 0;)
@@ -526,7 +536,7 @@ struct Compiler
                 L.stride[pos] = st;
                 for (u32 r = 0; r < L.dsize[pos]; ++r)
                     L.rs[static_cast<std::size_t>(pos) * n + L.domain[L.dom_begin[pos] + r]] = r * st;
-                st = sat_mul(st, std::max<u32>(1, L.dsize[pos]));
+                st = capped_product(st, std::max<u32>(1, L.dsize[pos]));
             }
             L.size[p] = size;
             L.offset[p] = running;
@@ -571,7 +581,7 @@ struct Compiler
             for (u32 i = 0; i < l.terms.size(); ++i)
             {
                 if (l.terms[i] < 0)
-                    d.base += S[l.pred].rs[static_cast<std::size_t>(i) * n + obj_of(l.terms[i])];
+                    d.base += static_arg_key(i, obj_of(l.terms[i]));
                 else
                     P.vars.push_back({static_cast<u32>(l.terms[i]), 0, static_rs_off[l.pred] + static_cast<u64>(i) * n});
             }
@@ -596,7 +606,7 @@ struct Compiler
         for (const Lit& l : sc.pre)
         {
             const bool fluent = T.kind[l.pred] != kStatic;
-            const auto vars = distinct_params(l.terms);
+            const auto vars = params_of(l.terms);
             if (vars.empty())
                 continue;
             const u32 ar = T.arity[l.pred];
@@ -678,7 +688,7 @@ struct Compiler
             if (!has_v || !others_placed)
                 continue;
             const bool fluent = T.kind[l.pred] == kFluent;
-            double atoms = fluent ? static_cast<double>(init_count[l.pred]) : static_cast<double>(satoms[l.pred].size());
+            double atoms = fluent ? static_cast<double>(init_count[l.pred]) : static_cast<double>(sfacts[l.pred].size());
             double values = 1;
             for (u32 i = 0; i < ar; ++i)
                 if (l.terms[i] < 0 || static_cast<u32>(l.terms[i]) != v)
@@ -706,7 +716,7 @@ struct Compiler
             for (u32 i = 0; i < T.arity[p]; ++i)
             {
                 std::vector<u8> seen(n, 0);
-                for (auto* a : satoms[p])
+                for (const auto* a : sfacts[p])
                     if (!seen[(*a)[1 + i]]++)
                         ++spv[p][i];
             }
@@ -770,12 +780,12 @@ struct Compiler
         {
             const bool fluent = T.kind[l.pred] == kFluent;
             const u32 ar = T.arity[l.pred];
-            const auto vars = distinct_params(l.terms);
+            const auto vars = params_of(l.terms);
             if (vars.empty())
             {
                 if (!fluent)
                 {
-                    if (static_ground_holds(l) != l.pos)
+                    if (static_fact(l) != l.pos)
                         pg.never = 1;
                 }
                 else
@@ -822,7 +832,7 @@ struct Compiler
                     else
                     {
                         f.kind = kFiltSRow;
-                        f.base = static_rows(l.pred, epos, lpos);
+                        f.base = adjacency(l.pred, epos);
                     }
                     filt[level_of[later]].push_back(f);
                     continue;
@@ -895,16 +905,22 @@ struct Compiler
             P.pool.insert(P.pool.end(), L.rs.begin() + pos * n, L.rs.begin() + (pos + 1) * n);
         }
         static_rs_off.assign(m, 0);
-        P.srel_bits.assign(m, 0);
-        P.srel_size.assign(m, 0);
+        P.srel_table.assign(m, 0);
+        P.srel_mask.assign(m, 0);
+        P.srel_probes.assign(m, 0);
         for (u32 p = 0; p < m; ++p)
             if (T.kind[p] == kStatic)
             {
+                // per argument position: the key contribution of each object (the kernels add one per bound
+                // parameter), then the key set
                 static_rs_off[p] = P.pool.size();
-                P.pool.insert(P.pool.end(), S[p].rs.begin(), S[p].rs.end());
-                P.srel_bits[p] = P.pool.size();
-                P.pool.insert(P.pool.end(), S[p].bits.begin(), S[p].bits.end());
-                P.srel_size[p] = S[p].size;
+                for (u32 i = 0; i < T.arity[p]; ++i)
+                    for (u32 o = 0; o < n; ++o)
+                        P.pool.push_back(static_arg_key(i, o));
+                P.srel_table[p] = P.pool.size();
+                P.pool.insert(P.pool.end(), S[p].table.begin(), S[p].table.end());
+                P.srel_mask[p] = S[p].table.size() - 1;
+                P.srel_probes[p] = S[p].probes;
             }
         P.domain = L.domain;
         P.pos_dom_begin = L.dom_begin;
@@ -976,7 +992,7 @@ struct Compiler
         {
             if (T.kind[l.pred] == kStatic)
             {
-                if (static_ground_holds(l) != l.pos)
+                if (static_fact(l) != l.pos)
                     P.goal_unsat = 1;
                 continue;
             }

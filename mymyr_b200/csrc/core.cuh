@@ -91,6 +91,29 @@ B2_DI u64 hash_words_fixed(Get&& w)
 /// brfs_fingerprint_term (src/mymyr/search/brfs.cpp:34-37).
 B2_DI u64 fingerprint_term(u64 id, u64 canonical) { return mix64(id * 0x9E3779B97F4A7C15ULL ^ canonical); }
 
+// ------------------------------------------------------------------------------------------------ static key sets
+/// The empty slot of a static predicate's key set (no packed key of an arity below 8 has its top byte set).
+constexpr u64 kNoStaticKey = ~u64{0};
+
+/// Home slot of a packed static key in a key set of mask + 1 slots.
+B2_DI u64 static_key_slot(u64 key, u64 mask) { return mix64(key ^ 0x6a09e667f3bcc909ULL) & mask; }
+
+/// Membership of a packed key in a static key set: linear probing from its home slot, at most `probes` slots (the
+/// longest run any stored key needed when the set was built).
+B2_DI bool static_member(const u64* table, u64 mask, u32 probes, u64 key)
+{
+    u64 j = static_key_slot(key, mask);
+    for (u32 i = 0; i < probes; ++i, j = (j + 1) & mask)
+    {
+        const u64 x = table[j];
+        if (x == key)
+            return true;
+        if (x == kNoStaticKey)
+            return false;
+    }
+    return false;
+}
+
 // ------------------------------------------------------------------------------------------------ Philox
 // rl::rng (include/mymyr/rl/rng.hpp:45-84): Philox-4x32-10 of (seed; draw lo, draw hi, env, purpose).
 B2_DI u64 philox_bits64(u64 seed, u64 env, u64 draw, u32 purpose)

@@ -31,6 +31,7 @@ using dev::hash_words;
 using dev::mix64;
 using dev::philox_bits64;
 using dev::RegRow;
+using dev::static_member;
 
 template<class St>
 __device__ __forceinline__ bool test_bit(const St& st, u64 bit)
@@ -53,8 +54,9 @@ struct DevTask
     const DSchema* schemas;
     const u32* domain;
     const u32* pos_dom_begin;
-    const u64* srel_bits;
-    const u64* srel_size;
+    const u64* srel_table;   // per predicate: pool offset of its static key set
+    const u64* srel_mask;
+    const u64* srel_probes;
     const u64* goal_pos;
     const u64* goal_neg;
 };
@@ -148,7 +150,8 @@ __device__ __forceinline__ bool literal_holds(const DevTask& T, const St& st, co
     if (l.fluent)
         t = k < T.fluent_count && test_bit(st, k);
     else
-        t = k < T.srel_size[l.pred] && ((T.pool[T.srel_bits[l.pred] + (k >> 6)] >> (k & 63)) & 1);
+        t = static_member(T.pool + T.srel_table[l.pred], T.srel_mask[l.pred],
+                          static_cast<u32>(T.srel_probes[l.pred]), k);
     return t != (l.neg != 0);
 }
 

@@ -61,11 +61,10 @@ struct Grounder
 
     bool static_holds(const CLit& l, const u32* bind) const
     {
-        const StaticRel& R = S[l.pred];
         u64 k = 0;
-        for (u32 i = 0; i < R.arity; ++i)
-            k += R.rs[static_cast<std::size_t>(i) * n + object(l.terms[i], bind)];
-        return k < R.size && test(R.bits, k);
+        for (u32 i = 0; i < l.terms.size(); ++i)
+            k += static_arg_key(i, object(l.terms[i], bind));
+        return S[l.pred].holds(k);
     }
 
     bool holds(const CLit& l, const u32* bind, const std::vector<u64>& reached) const

@@ -12,6 +12,7 @@
 
 #include <cstdint>
 #include <string>
+#include <algorithm>
 #include <vector>
 
 namespace b2
@@ -76,13 +77,38 @@ struct Layout
     std::vector<u64> rs;          // per position: n entries, rank * stride or kOutside
 };
 
+/// A static predicate's ground atoms as packed keys: argument i of an atom is its object in bits 8i..8i+7 (objects
+/// are below 256, arities below 8), so a literal's key is its constants' part plus one shifted object per bound
+/// parameter, the same additive form as a fluent literal's slot. `keys` holds them sorted (host lookups);
+/// `table` is the open-addressed set the kernels probe (2^k slots, kEmptyStaticSlot empty, linear probing from
+/// static_key_home), and no stored key sits more than `probes` - 1 slots past its home.
 struct StaticRel
 {
     u32 arity = 0;
-    u64 size = 0;              // key space
-    std::vector<u64> rs;       // arity * n: rank * stride or kStaticOutside
-    std::vector<u64> bits;     // dense membership
+    std::vector<u64> keys;
+    std::vector<u64> table;
+    u32 probes = 0;
+    bool holds(u64 key) const { return std::binary_search(keys.begin(), keys.end(), key); }
 };
+
+/// The contribution of object o at argument position i to a static atom's packed key.
+inline u64 static_arg_key(u32 i, u32 o) { return static_cast<u64>(o) << (8 * i); }
+
+/// The empty slot of a static key set (a packed key of an arity below 8 never has its top byte set).
+constexpr u64 kEmptyStaticSlot = ~u64{0};
+
+/// Home slot of a packed static key in a key set of mask + 1 slots: the splitmix64 finalizer of the key xor a fixed
+/// constant. The kernels' static_key_slot (core.cuh) computes the same.
+inline u64 static_key_home(u64 key, u64 mask)
+{
+    u64 x = key ^ 0x6a09e667f3bcc909ULL;
+    x ^= x >> 30;
+    x *= 0xbf58476d1ce4e5b9ULL;
+    x ^= x >> 27;
+    x *= 0x94d049bb133111ebULL;
+    x ^= x >> 31;
+    return x & mask;
+}
 
 // ------------------------------------------------------------------------------------------------ device program
 
@@ -170,8 +196,9 @@ struct Program
     std::vector<DSchema> schemas;
     std::vector<u32> domain;      // the layout's domains (rank -> object)
     std::vector<u32> pos_dom_begin;
-    std::vector<u64> srel_bits;   // per predicate: u64 pool offset of its static relation bits
-    std::vector<u64> srel_size;   // per predicate: key space
+    std::vector<u64> srel_table;  // per predicate: u64 pool offset of its static key set (StaticRel::table)
+    std::vector<u64> srel_mask;   // per predicate: slots of the key set - 1
+    std::vector<u64> srel_probes; // per predicate: probes that find any stored key (StaticRel::probes)
     std::vector<u64> goal_pos, goal_neg;  // [words] goal masks
     std::vector<u64> initial;     // [words]
     std::vector<std::vector<u32>> slot_atoms;  // per slot: [pred, args...]

@@ -332,6 +332,38 @@ def logistics(n_cities: int = 8, locs_per_city: int = 4, n_trucks: int = 6, n_ai
     return t.text()
 
 
+def counters(n_counters: int = 3, modulus: int = 5, seed: int = 0) -> str:
+    """Modular counters: each counter holds a value mod `modulus` (fluent val(counter, value)); static facts
+    plus(a, b, c) for a + b = c (mod modulus) and le(a, b) for a <= b. Schemas: add(c1, c2, x, y, z) sets c1 to
+    x + y through the ternary plus(x, y, z); double(c, x, z) through plus(x, x, z), a static literal with a repeated
+    parameter; reset(c, x) back to value 0 under le(x, x). Initial values are drawn from the seed. Exercises the
+    matchers' checks of static literals by key (arity 3 and repeated parameters), which the other workloads lack."""
+    rng = SplitMix(seed)
+    k, m = n_counters, modulus
+    cs = list(range(k))
+    vs = list(range(k, k + m))
+    t = TaskText(n=k + m)
+    counter = t.pred("S", 1, "counter")
+    value = t.pred("S", 1, "value")
+    plus = t.pred("S", 3, "plus")
+    le = t.pred("S", 2, "le")
+    val = t.pred("F", 2, "val")
+    t.static_init += [(counter, (c,)) for c in cs] + [(value, (v,)) for v in vs]
+    t.static_init += [(plus, (vs[a], vs[b], vs[(a + b) % m])) for a in range(m) for b in range(m)]
+    t.static_init += [(le, (vs[a], vs[b])) for a in range(m) for b in range(a, m)]
+    for c in cs:
+        t.fluent_init.append((val, (c, vs[rng.below(m)])))
+    t.goal.append((val, True, (cs[0], vs[m - 1])))
+    t.schemas.append(("add", 5, [(counter, 1, (0,)), (counter, 1, (1,)), (val, 1, (0, 2)), (val, 1, (1, 3)),
+                                 (plus, 1, (2, 3, 4))],
+                      [(val, 0, (0, 2)), (val, 1, (0, 4))]))
+    t.schemas.append(("double", 3, [(counter, 1, (0,)), (val, 1, (0, 1)), (plus, 1, (1, 1, 2))],
+                      [(val, 0, (0, 1)), (val, 1, (0, 2))]))
+    t.schemas.append(("reset", 2, [(counter, 1, (0,)), (val, 1, (0, 1)), (le, 1, (1, 1))],
+                      [(val, 0, (0, 1)), (val, 1, (0, obj(vs[0])))]))
+    return t.text()
+
+
 CONFIGS = {
     "tower7": lambda: tower(7, 0),
     "transport": lambda: transport(2, 40, 2, 0),

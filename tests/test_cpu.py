@@ -50,6 +50,7 @@ GENERATED = {
     "tile3x3": lambda: tasks.sliding_tile(3, 3, 40, 5),
     "random0": lambda: tasks.random_domain(0),
     "random1": lambda: tasks.random_domain(1),
+    "counters": lambda: tasks.counters(3, 5, 0),
 }
 
 
@@ -62,11 +63,12 @@ def test_generators_are_deterministic_and_pinned():
     assert digests == want
 
 
-@pytest.mark.parametrize("name", ["tile4x4", "transport_2_200_3"])
+@pytest.mark.parametrize("name", ["tile4x4", "transport_2_200_3", "counters"])
 def test_compiled_matcher_kernels_build_on_the_host(name):
     """The task's generated matcher and the kernels over it (count, expand, fused expand + push, env, batched expand)
     compile for sm_100a with NVRTC without a device."""
-    text = {"tile4x4": tasks.sliding_tile(4, 4, 60, 0), "transport_2_200_3": tasks.transport(2, 200, 3, 0)}[name]
+    text = {"tile4x4": tasks.sliding_tile(4, 4, 60, 0), "transport_2_200_3": tasks.transport(2, 200, 3, 0),
+            "counters": tasks.counters(3, 5, 0)}[name]
     src = Task.from_text(text, host_only=True).compile()
     assert "b2::gen" in src or "namespace" in src
 
