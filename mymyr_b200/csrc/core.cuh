@@ -332,6 +332,117 @@ B2_DI void insert(const Store& S, const Row& s, u64 h, u64 g, u32 i, u32 k)
     atomicOr(S.status, kStatusProbeLimit);
 }
 
+/// insert() for up to NB candidates of one lane at once (n valid), with their probes interleaved so that their memory
+/// accesses overlap: candidate e has hash h[e], candidate index g[e], parent index i[e], successor index k[e] and row
+/// words rw(e, q). Same protocol and outcomes as insert(), step by step: read the slot; claim an empty one by CAS;
+/// compare a state of an earlier layer in place; defer a tag match with a candidate of this layer.
+template<int NB, int NW, class RowWord>
+B2_DI void insert_batch(const Store& S, u32 n, const u64* h, const u64* g, const u32* i, const u32* k, RowWord&& rw)
+{
+    u64 j[NB], mine[NB], og[NB];
+    u32 ph[NB], probes[NB];  // ph: 0 done, 1 read the slot at j, 2 claim it by CAS, 3 compare the row of og
+#pragma unroll
+    for (int e = 0; e < NB; ++e)
+    {
+        ph[e] = static_cast<u32>(e) < n ? 1u : 0u;
+        mine[e] = (h[e] & 0xFFFFFFFF00000000ull) | g[e];
+        j[e] = h[e] & S.mask;
+        og[e] = 0;
+        probes[e] = 0;
+    }
+    for (;;)
+    {
+        u32 any = 0;
+#pragma unroll
+        for (int e = 0; e < NB; ++e)
+            any |= ph[e];
+        if (!any)
+            break;
+        u64 cur[NB];
+        bool eq[NB];
+#pragma unroll
+        for (int e = 0; e < NB; ++e)
+        {
+            cur[e] = 0;
+            eq[e] = false;
+            if (ph[e] == 1)
+                cur[e] = __ldcg(S.table + j[e]);
+            else if (ph[e] == 2)
+                cur[e] = atomicCAS(reinterpret_cast<unsigned long long*>(S.table + j[e]), kEmpty, mine[e]);
+            else if (ph[e] == 3)
+            {
+                const u64* r = S.rows + og[e] * S.W;
+                bool same = true;
+                for_words<NW>(S.W, [&](u32 q) { same = same && __ldcg(r + q) == rw(e, q); });
+                eq[e] = same;
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < NB; ++e)
+        {
+            if (ph[e] == 3)
+            {
+                if (eq[e])
+                    ph[e] = 0;  // a state of an earlier layer
+                else
+                {
+                    j[e] = (j[e] + 1) & S.mask;
+                    ph[e] = ++probes[e] < S.max_probe ? 1u : 4u;
+                }
+                continue;
+            }
+            if (ph[e] != 1 && ph[e] != 2)
+                continue;
+            if (cur[e] == kEmpty)
+            {
+                if (ph[e] == 2)
+                {
+                    const u64 ge = g[e];
+                    u64* r = S.rows + ge * S.W;
+                    for_words<NW>(S.W, [&](u32 q) { r[q] = rw(e, q); });
+                    S.hash[ge] = h[e];
+                    S.par[ge] = i[e];
+                    S.kid[ge] = k[e];
+                    S.claimed[ge - S.layer_cand_begin] = 1;
+                    ph[e] = 0;
+                }
+                else
+                    ph[e] = 2;
+                continue;
+            }
+            if ((cur[e] >> 32) != (mine[e] >> 32))
+            {
+                j[e] = (j[e] + 1) & S.mask;
+                ph[e] = ++probes[e] < S.max_probe ? 1u : 4u;
+                continue;
+            }
+            og[e] = cur[e] & 0xFFFFFFFFull;
+            if (og[e] >= S.layer_cand_begin)
+            {
+                // a candidate of this layer with the same tag: this one's record, then the resolve pass
+                const u64 ge = g[e];
+                u64* r = S.rows + ge * S.W;
+                for_words<NW>(S.W, [&](u32 q) { r[q] = rw(e, q); });
+                S.hash[ge] = h[e];
+                S.par[ge] = i[e];
+                S.kid[ge] = k[e];
+                const u32 qd = atomicAdd(S.ndeferred, 1u);
+                S.deferred[qd] = (j[e] << 32) | ge;
+                ph[e] = 0;
+            }
+            else
+                ph[e] = 3;
+        }
+#pragma unroll
+        for (int e = 0; e < NB; ++e)
+            if (ph[e] == 4)
+            {
+                atomicOr(S.status, kStatusProbeLimit);
+                ph[e] = 0;
+            }
+    }
+}
+
 // ------------------------------------------------------------------------------------------------ kernel arguments
 struct LayerMisc
 {

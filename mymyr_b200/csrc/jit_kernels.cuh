@@ -148,6 +148,8 @@ struct QEntry
 };
 /// Queue entries per warp: about 21 KB per 128-thread block (ten blocks per SM).
 constexpr u32 kQueue = W <= 4 ? 96u : W <= 6 ? 80u : 64u;
+/// Queued successors a lane inserts at once (their probes interleaved).
+constexpr int kInsertBatch = 2;
 
 /// The expansion with warp-cooperative inserts (rows in registers): each lane runs its parent's matcher and queues
 /// every successor (row, hash, candidate index) in shared memory; after the round all 32 lanes insert the queued
@@ -207,14 +209,27 @@ B2_DI void brfs_expand_queued(const BrfsArgs& a)
         }
         __syncwarp();
         const u32 n = min(qn[wid], kQueue);
-        for (u32 s = lane; s < n; s += 32)
+        // the queued successors, kInsertBatch per lane at a time with their probes interleaved
+        for (u32 s0 = lane; s0 < n; s0 += 32 * kInsertBatch)
         {
-            const QEntry& e = q[wid][s];
-            Row r;
+            u64 h[kInsertBatch], g[kInsertBatch];
+            u32 ii[kInsertBatch], kk[kInsertBatch], idx[kInsertBatch];
+            u32 m = 0;
 #pragma unroll
-            for (int x = 0; x < WR; ++x)
-                r.w[x] = static_cast<u32>(x) < W ? e.w[x < static_cast<int>(W) ? x : 0] : 0;
-            insert<static_cast<int>(W)>(St, r, e.h, e.g, e.i, e.k);
+            for (int e = 0; e < kInsertBatch; ++e)
+            {
+                const u32 sx = s0 + 32 * static_cast<u32>(e);
+                idx[e] = sx < n ? sx : s0;
+                const QEntry& x = q[wid][idx[e]];
+                h[e] = x.h;
+                g[e] = x.g;
+                ii[e] = x.i;
+                kk[e] = x.k;
+                if (sx < n)
+                    m = static_cast<u32>(e) + 1;
+            }
+            insert_batch<kInsertBatch, static_cast<int>(W)>(St, m, h, g, ii, kk,
+                                                              [&](int e, u32 w) { return q[wid][idx[e]].w[w]; });
         }
         __syncwarp();
         if (lane == 0)
