@@ -292,6 +292,17 @@ struct Gen
         const DSchema& S = P.schemas[s];
         const DProgram& pg = S.prog[pi];
         const std::string name = "Run<" + std::to_string(s) + ", " + std::to_string(pi) + ">";
+        if (pg.sorted && !pg.never)
+        {
+            // bindings that do not come out in canonical order: the matcher as it binds (RunRaw), emitted sorted
+            const std::string raw = "RunRaw<" + std::to_string(s) + ", " + std::to_string(pi) + ">";
+            run_struct(raw, S, pg);
+            o << "template<> struct " << name << " {\n"
+              << "template<class St, class E> B2_DI static bool go(const St& st, E&& emit) {\n"
+              << "  return emit_sorted(" << S.arity << "u, [&](auto&& f_) { return " << raw
+              << "::go(st, f_); }, emit);\n}\n};\n";
+            return;
+        }
         // the selectivity order applies when the program binds every parameter (witness pruning without
         // witness-only parameters binds them all too)
         const bool fast = S.fast_on && !pg.never && pg.first_exist == pg.nlevels && pg.nlevels == S.arity;
@@ -345,6 +356,7 @@ struct Gen
         }
         o << "}\n";
         o << "template<int S, int PI> struct Run;\ntemplate<int S, int PI> struct RunCanon;\n"
+          << "template<int S, int PI> struct RunRaw;\n"
           << "template<int S> struct Eff;\n";
         for (u32 s = 0; s < P.nschemas; ++s)
         {

@@ -761,6 +761,7 @@ struct Compiler
         DProgram pg;
         pg.nlevels = static_cast<u32>(order.size());
         pg.first_exist = first_exist;
+        pg.nparams = static_cast<u32>(T.schemas[s].arity);
         pg.level_begin = static_cast<u32>(P.levels.size());
         std::vector<i32> level_of(sc.arity, -1);
         for (u32 d = 0; d < order.size(); ++d)
@@ -940,14 +941,17 @@ struct Compiler
             for (u32 v = 0; v < sc.arity; ++v)
                 all[v] = v;
             ds.prog[1] = matcher(s, all, sc.arity);
-            // witness pruning on: relevant parameters in index order, then the witness-only ones
+            // witness pruning on: relevant parameters in index order, then the witness-only ones in the reference's
+            // order for them; every assignment of the relevant parameters keeps the first witness found
             std::vector<u32> order;
             for (u32 v = 0; v < sc.arity; ++v)
                 if (relevant[v])
                     order.push_back(v);
             const u32 first_exist = static_cast<u32>(order.size());
-            // canonical order needs every witness parameter after every relevant one (the emitted bindings then
-            // differ in their relevant parameters, which decide the order alone)
+            // the bindings come out in canonical order when every witness parameter follows every relevant one (they
+            // then differ in their relevant parameters, which decide the order alone); otherwise the matchers buffer
+            // and sort them, as the reference does for a matcher that does not bind in index order
+            // (successor/successors.hpp:147-248)
             const u32 last_relevant = order.empty() ? 0 : order.back();
             bool in_order = true;
             for (u32 v : witness_order(s, relevant))
@@ -956,14 +960,8 @@ struct Compiler
                     in_order = false;
                 order.push_back(v);
             }
-            if (!in_order)
-            {
-                // the device would have to sort such a schema's bindings; refuse witness pruning on it
-                ds.prog[0] = ds.prog[1];
-                ds.prog[0].never = 0xFFFFFFFFu;
-            }
-            else
-                ds.prog[0] = matcher(s, order, first_exist);
+            ds.prog[0] = matcher(s, order, first_exist);
+            ds.prog[0].sorted = in_order ? 0 : 1;
             // the compiled matcher's selectivity order: keys of 8 bits per parameter (at most 256 objects, 8
             // parameters) sort into canonical order
             double cost_sel = 0, cost_idx = 0;

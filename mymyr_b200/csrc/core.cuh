@@ -143,6 +143,85 @@ B2_DI u32 below(u64 x, u32 n)
     return static_cast<u32>((hi + (lo >> 32)) >> 32);
 }
 
+// ------------------------------------------------------------------------------------------------ sorted bindings
+/// Emits the bindings that raw(f) enumerates (f(const u32* b) for each, `arity` parameters, objects below 256) in
+/// canonical order, the order the reference emits a matcher's bindings in when the matcher does not bind in index
+/// order (it buffers them, packs them into keys and sorts them): the keys (8 bits per parameter, the first highest) of
+/// up to 16 bindings are buffered and sorted; more are emitted by selection passes, each of which enumerates again and
+/// emits the smallest key above the last one. emit returning false stops (and returns false).
+template<class Raw, class Emit>
+B2_DI bool emit_sorted(u32 arity, Raw&& raw, Emit&& emit)
+{
+    constexpr u32 kBuf = 16;
+    u64 buf[kBuf];
+    u32 n = 0;
+    bool over = false;
+    raw([&](const u32* b) {
+        u64 k = 0;
+        for (u32 v = 0; v < arity; ++v)
+            k = (k << 8) | b[v];
+        if (n < kBuf)
+            buf[n++] = k;
+        else
+            over = true;
+        return true;
+    });
+    u32 b[8];
+    const auto unpack = [&](u64 k) {
+        for (u32 v = arity; v-- > 0;)
+        {
+            b[v] = static_cast<u32>(k & 0xFFu);
+            k >>= 8;
+        }
+    };
+    if (!over)
+    {
+        for (u32 i = 1; i < n; ++i)
+        {
+            const u64 x = buf[i];
+            u32 j = i;
+            while (j > 0 && buf[j - 1] > x)
+            {
+                buf[j] = buf[j - 1];
+                --j;
+            }
+            buf[j] = x;
+        }
+        for (u32 i = 0; i < n; ++i)
+        {
+            unpack(buf[i]);
+            if (!emit(static_cast<const u32*>(b)))
+                return false;
+        }
+        return true;
+    }
+    u64 last = 0;
+    bool first = true;
+    for (;;)
+    {
+        u64 best = ~u64{0};
+        bool any = false;
+        raw([&](const u32* x) {
+            u64 k = 0;
+            for (u32 v = 0; v < arity; ++v)
+                k = (k << 8) | x[v];
+            if ((first || k > last) && k <= best)
+            {
+                best = k;
+                any = true;
+            }
+            return true;
+        });
+        if (!any)
+            return true;
+        unpack(best);
+        if (!emit(static_cast<const u32*>(b)))
+            return false;
+        last = best;
+        first = false;
+    }
+}
+
 // ------------------------------------------------------------------------------------------------ rows
 /// A state row of up to WR words in registers; word(i) for i >= WR reads zero.
 template<int WR>

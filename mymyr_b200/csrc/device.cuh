@@ -205,10 +205,10 @@ __device__ __forceinline__ bool level_candidates(const DevTask& T, const St& st,
 
 constexpr int kMaxLevels = 8;
 
-/// Calls emit(bind) for every applicable binding of program `pg` in state `st`, in canonical order. emit returns
-/// false to stop; the function then returns false.
+/// Calls emit(bind) for every applicable binding of program `pg` in state `st`, in the program's binding order. emit
+/// returns false to stop; the function then returns false.
 template<int OW, class St, class Emit>
-__device__ bool enumerate(const DevTask& T, const DProgram& pg, const St& st, u32* bind, Emit&& emit)
+__device__ bool enumerate_raw(const DevTask& T, const DProgram& pg, const St& st, u32* bind, Emit&& emit)
 {
     if (pg.never)
         return true;
@@ -263,6 +263,22 @@ __device__ bool enumerate(const DevTask& T, const DProgram& pg, const St& st, u3
             ++d;
     }
     return true;
+}
+
+/// enumerate_raw() in canonical order: a program whose bindings do not come out in it (pg.sorted) has them buffered
+/// and sorted (emit_sorted).
+template<int OW, class St, class Emit>
+__device__ bool enumerate(const DevTask& T, const DProgram& pg, const St& st, u32* bind, Emit&& emit)
+{
+    if (!pg.sorted)
+        return enumerate_raw<OW>(T, pg, st, bind, emit);
+    return dev::emit_sorted(
+        pg.nparams, [&](auto&& f) { return enumerate_raw<OW>(T, pg, st, bind, f); },
+        [&](const u32* b) {
+            for (u32 v = 0; v < pg.nparams; ++v)
+                bind[v] = b[v];
+            return emit(static_cast<const u32*>(bind));
+        });
 }
 
 /// The slots an action deletes and adds (dense: slot = canonical id). Deletes outside the layout are dropped.

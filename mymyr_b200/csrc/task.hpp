@@ -165,6 +165,9 @@ struct DProgram
     u32 level_begin = 0;      // into levels
     u32 pre_begin = 0, pre_end = 0;  // ground fluent checks (into checks)
     u32 never = 0;            // statically inapplicable
+    u32 sorted = 0;           // the bindings do not come out in canonical order (witness pruning with a witness-only
+                              // parameter before an effect parameter): they are buffered and emitted sorted
+    u32 nparams = 0;          // the schema's parameters (the sorted bindings' keys)
 };
 
 struct DSchema

@@ -203,12 +203,13 @@ def sliding_tile(rows: int = 4, cols: int = 4, scramble: int = 60, seed: int = 0
 
 
 def random_domain(seed: int = 0, n_types: int = 10, per_type: int = 20, n_unary: int = 6, n_binary: int = 14,
-                  n_ternary: int = 4, n_schemas: int = 16) -> str:
+                  n_ternary: int = 4, n_schemas: int = 16, n_init: int = 4) -> str:
     """A synthetic typed STRIPS domain: n_types types of per_type objects (200 objects by default), 24 fluent
     predicates of arity 1-3 with random type signatures, and n_schemas schemas with 3-5 typed parameters, as many
     positive fluent preconditions as parameters plus 0-1 (3-6 in all, every parameter mentioned), and 2-4 add/delete
     effects. The precondition count scales with the parameters so that a state at 5% atom density keeps a bounded
-    number of applicable actions."""
+    number of applicable actions. The initial state holds n_init atoms (4 by default: the stress test expands random
+    states, not the initial one; a larger one gives a searchable space)."""
     rng = SplitMix(seed)
     n = n_types * per_type
     t = TaskText(n=n)
@@ -259,6 +260,13 @@ def random_domain(seed: int = 0, n_types: int = 10, per_type: int = 20, n_unary:
     for p, sig in sigs[:4]:
         args = tuple(ty * per_type + rng.below(per_type) for ty in sig)
         t.fluent_init.append((p, args))
+    seen = set(t.fluent_init)
+    while len(t.fluent_init) < n_init:
+        p, sig = sigs[rng.below(len(sigs))]
+        atom = (p, tuple(ty * per_type + rng.below(per_type) for ty in sig))
+        if atom not in seen:
+            seen.add(atom)
+            t.fluent_init.append(atom)
     p, sig = sigs[-1]
     t.goal.append((p, True, tuple(ty * per_type for ty in sig)))
     return t.text()

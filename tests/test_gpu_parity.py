@@ -68,6 +68,8 @@ BRFS_CASES = [
     ("tile3x3", lambda: tasks.sliding_tile(3, 3, 40, 5), None),
     ("tile4x4_d12", lambda: tasks.sliding_tile(4, 4, 60, 0), 12),
     ("counters", lambda: tasks.counters(4, 6, 1), None),
+    # witness-only parameters before effect parameters: under witness pruning the bindings are emitted sorted
+    ("random600_d2", lambda: tasks.random_domain(0, n_init=600), 2),
 ]
 
 
@@ -202,12 +204,8 @@ def test_expand_matches_reference(ref, name, make, n, density, witness, matcher)
     states = random_states(t.words, t.fluent_slots, n, density, seed=hash(name) & 0xFFFF)
     states[0] = t.initial_state()
     want = rt.expand(states, witness_pruning=witness, succ=True)
-    if witness and name.startswith("random"):
-        # these schemas bind witness-only parameters before effect parameters; the device path refuses them under
-        # witness pruning rather than emit them out of canonical order
-        with pytest.raises(UnsupportedTask):
-            b2rl.expand(t, to_dev(states), witness_pruning=witness, succ=True)
-        return
+    # the random domains' schemas bind witness-only parameters before effect parameters: under witness pruning their
+    # bindings come out of the matcher out of canonical order and are emitted sorted
     got = b2rl.expand(t, to_dev(states), witness_pruning=witness, succ=True)
     assert got.generated == want["generated"]
     assert np.array_equal(got.offsets.cpu().numpy(), want["offsets"])
