@@ -261,3 +261,50 @@ def hash_state(row: np.ndarray) -> int:
 
 def philox_bits64(seed, env, draw, purpose=0) -> int:
     return int(lib().ref_philox_bits64(seed, env, draw, purpose))
+
+
+# ------------------------------------------------------------------------------------------------ reference-side shim
+_shim = None
+
+
+def shim_available() -> bool:
+    return (HERE / "_ref" / "libshim_check.so").exists()
+
+
+def _shim_lib():
+    """oracle/_ref/libshim_check.so: include/mymyr_b200_shim.hpp compiled against the reference (oracle/shim_check.cpp)."""
+    global _shim
+    if _shim is None:
+        import mymyr_b200  # the device library first: the shim links it
+
+        mymyr_b200.lib()
+        L = C.CDLL(str(HERE / "_ref" / "libshim_check.so"))
+        L.shim_check_layout.argtypes = [C.c_char_p, C.c_int, C.c_char_p, C.c_size_t]
+        L.shim_check_layout.restype = C.c_int
+        L.shim_check_brfs.argtypes = [C.c_char_p, C.c_int, C.c_uint32, C.c_int, C.c_int, C.c_void_p, C.c_char_p,
+                                      C.c_size_t]
+        L.shim_check_brfs.restype = C.c_int
+        _shim = L
+    return _shim
+
+
+ATOMS = {"auto": 0, "reachable": 1, "dense": 2}
+
+
+def shim_layout(text: str, atoms: str = "auto") -> tuple[int, str]:
+    """The shim's describe() + b2_task_create (host only) against the reference Task's dense twin: (0, "") when
+    words, slots and the initial row agree."""
+    msg = C.create_string_buffer(1024)
+    rc = _shim_lib().shim_check_layout(text.encode(), ATOMS[atoms], msg, 1024)
+    return rc, msg.value.decode(errors="replace")
+
+
+def shim_brfs(text: str, atoms: str = "auto", max_depth=None, witness_pruning=True, stop_at_goal=False):
+    """b2shim::brfs (the device) and mymyr::brfs on the same reference Task: (rc, device fields, reference fields,
+    message); rc 0 when every field and the per-layer counts agree."""
+    out = np.zeros(16, np.uint64)
+    msg = C.create_string_buffer(1024)
+    rc = _shim_lib().shim_check_brfs(text.encode(), ATOMS[atoms], 0xFFFFFFFF if max_depth is None else max_depth,
+                                     int(witness_pruning), int(stop_at_goal), out.ctypes.data, msg, 1024)
+    keys = ["states", "expanded", "generated", "num_goal_states", "layers", "fingerprint", "solved", "status"]
+    return rc, dict(zip(keys, map(int, out[:8]))), dict(zip(keys, map(int, out[8:]))), msg.value.decode(errors="replace")

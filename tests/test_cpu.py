@@ -159,3 +159,25 @@ def test_tile_brfs_golden_file_matches_reference(ref):
         r = rt.brfs(threads=4, max_depth=d, stop_at_goal=False, fingerprint=True, store="concurrent")
         assert g[str(d)]["states"] == r["states"] and g[str(d)]["fingerprint"] == f"{r['fingerprint']:#018x}"
         assert g[str(d)]["layer_counts"] == [list(x) for x in r["layer_counts"]]
+
+
+@pytest.mark.parametrize("atoms", ["auto", "reachable", "dense"])
+@pytest.mark.parametrize("name", ["tower7", "transport", "tile4x4", "counters", "random0"])
+def test_reference_side_shim_describes_the_task(ref, name, atoms):
+    """The reference-side shim (include/mymyr_b200_shim.hpp, compiled against the reference's headers by
+    oracle/Makefile): describe() of a reference Task's TaskData gives a device task whose words, fluent slots and
+    initial row equal the reference's dense twin of the task (Task::translate for Auto and Reachable slots)."""
+    if not ref.shim_available():
+        pytest.skip("oracle/_ref/libshim_check.so not built")
+    rc, msg = ref.shim_layout(GENERATED[name](), atoms)
+    assert rc == 0, msg
+
+
+@pytest.mark.parametrize("path", _suite_texts()[:8], ids=lambda p: p.stem)
+def test_reference_side_shim_on_suite_tasks(ref, path):
+    """The shim on the reference's own task fixtures (read in place): a task the device path accepts is described
+    with the reference's dense layout; one it does not is refused with std::invalid_argument."""
+    if not ref.shim_available():
+        pytest.skip("oracle/_ref/libshim_check.so not built")
+    rc, msg = ref.shim_layout(path.read_text(), "auto")
+    assert rc == 0 or (rc == -1 and ("support" in msg or "does not run" in msg)), msg

@@ -395,3 +395,24 @@ def test_brfs_max_states_matches_reference(ref, name, make, depth, matcher, stop
         np.testing.assert_array_equal(p, par[:k])
         np.testing.assert_array_equal(i, idx[:k])
         r.close()
+
+
+SHIM_CASES = [
+    ("tower7", lambda: tasks.tower(7, 0), None, False),
+    ("tile3x3_goal", lambda: tasks.sliding_tile(3, 3, 30, 1), None, True),
+    ("tile4x4_d14", lambda: tasks.sliding_tile(4, 4, 60, 0), 14, False),
+    ("transport_2_6_2", lambda: tasks.transport(2, 6, 2, 1), None, False),
+]
+
+
+@pytest.mark.parametrize("atoms", ["auto", "dense"])
+@pytest.mark.parametrize("name,make,depth,stop", SHIM_CASES, ids=[c[0] for c in SHIM_CASES])
+def test_reference_side_shim_brfs_matches_reference(ref, name, make, depth, stop, atoms):
+    """mymyr::brfs and the shim's device brfs (include/mymyr_b200_shim.hpp: the same signature, options and result
+    struct) on the same reference Task, default Auto atom slots included: states, expanded, generated, goal states,
+    layers, per-layer counts, fingerprint and status agree."""
+    if not ref.shim_available():
+        pytest.skip("oracle/_ref/libshim_check.so not built")
+    rc, dev, want, msg = ref.shim_brfs(make(), atoms, max_depth=depth, stop_at_goal=stop)
+    assert rc == 0, (msg, dev, want)
+    assert dev == want
