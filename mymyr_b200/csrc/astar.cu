@@ -52,6 +52,12 @@ struct HmaxArgs
     const u64* goal_pos;
     const u64* goal_neg;
     u8* flags;
+    // the triggered evaluation: the operators that need each proposition (CSR over the props), the goal propositions
+    // as a bitset
+    const u32* need_begin;
+    const u32* need;
+    const u32* goal_bits;
+    u32 props;
 };
 
 __device__ __forceinline__ bool sbit(const u64* b, u32 s) { return (b[s >> 6] >> (s & 63)) & 1; }
@@ -132,6 +138,123 @@ __global__ void k_hmax(HmaxArgs H, const u64* __restrict__ rows, u64 stride, con
                     h = layer;
                     break;
                 }
+            }
+        }
+        if (lane == 0)
+            out[out_by_node ? node : i] = h;
+        __syncwarp();
+    }
+}
+
+/// h^max by operator triggering (unit costs): the same layers as k_hmax, without sweeping every operator per layer.
+/// Warp per state; per warp in shared memory: the reached propositions (W words), each operator's count of
+/// preconditions not reached yet (ops words), and the propositions in the order they are reached (props words, a
+/// queue whose layers follow one another). Layer 0 is the state; an operator whose count is 0 adds its propositions to
+/// the next layer; every proposition first reached in layer L lowers the counts of the operators that need it, and an
+/// operator that reaches 0 then adds its propositions to layer L + 1. h is the layer in which the last goal proposition
+/// is reached, a dead end (kDeadEnd) when a layer adds nothing before.
+__global__ void k_hmax_trig(HmaxArgs H, const u64* __restrict__ rows, u64 stride, const u32* __restrict__ nodes,
+                            const u64* n_dev, u64 n_host, u32* __restrict__ out, u32 out_by_node)
+{
+    extern __shared__ u64 sm[];
+    const u32 lane = threadIdx.x & 31, wib = threadIdx.x >> 5, wpb = blockDim.x >> 5;
+    const u64 per_warp = H.W + (static_cast<u64>(H.ops) + H.props + 4 + 1) / 2;  // u64 words
+    u64* reached = sm + wib * per_warp;
+    u32* unsat = reinterpret_cast<u32*>(reached + H.W);
+    u32* queue = unsat + H.ops;
+    u32* ctl = queue + H.props;  // [0] queue tail, [1] goal propositions left
+    const u64 n = n_dev ? *n_dev : n_host;
+    for (u64 i = static_cast<u64>(blockIdx.x) * wpb + wib; i < n; i += static_cast<u64>(gridDim.x) * wpb)
+    {
+        const u64 node = nodes ? nodes[i] : i;
+        const u64* row = rows + node * stride;
+        bool gpos = true, gneg = true;
+        for (u32 w = lane; w < H.W; w += 32)
+        {
+            const u64 x = row[w];
+            reached[w] = x;
+            if (H.flags)
+            {
+                gpos = gpos && (x & H.goal_pos[w]) == H.goal_pos[w];
+                gneg = gneg && (x & H.goal_neg[w]) == 0;
+            }
+        }
+        if (lane == 0)
+            ctl[0] = 0;
+        __syncwarp();
+        if (H.flags && __all_sync(0xFFFFFFFFu, gpos && gneg) && lane == 0)
+            H.flags[node] |= kGoal;
+        // goal propositions not true in the state
+        u32 left = 0;
+        for (u32 q = lane; q < H.ngoal; q += 32)
+            left += sbit(reached, H.goal[q]) ? 0u : 1u;
+        for (int o = 16; o > 0; o >>= 1)
+            left += __shfl_xor_sync(0xFFFFFFFFu, left, o);
+        u32 h = 0;
+        if (H.unreachable)
+            h = kDeadEnd;
+        else if (left)
+        {
+            if (lane == 0)
+                ctl[1] = left;
+            // layer 0: every operator's unreached preconditions; those with none add layer 1
+            for (u32 o = lane; o < H.ops; o += 32)
+            {
+                u32 c = 0;
+                for (u32 q = H.pre_begin[o], e = H.pre_begin[o + 1]; q < e; ++q)
+                    c += sbit(reached, H.pre[q]) ? 0u : 1u;
+                unsat[o] = c;
+            }
+            __syncwarp();
+            // an operator that fires adds its propositions not reached yet to the queue (the next layer)
+            const auto fire = [&](u32 o) {
+                for (u32 q = H.add_begin[o], e = H.add_begin[o + 1]; q < e; ++q)
+                {
+                    const u32 p = H.add[q];
+                    const unsigned long long bit = 1ull << (p & 63);
+                    if (reached[p >> 6] & bit)
+                        continue;
+                    const unsigned long long was = atomicOr(reinterpret_cast<unsigned long long*>(reached + (p >> 6)), bit);
+                    if (was & bit)
+                        continue;
+                    queue[atomicAdd(&ctl[0], 1u)] = p;
+                    if ((H.goal_bits[p >> 5] >> (p & 31)) & 1u)
+                        atomicSub(&ctl[1], 1u);
+                }
+            };
+            for (u32 o = lane; o < H.ops; o += 32)
+                if (unsat[o] == 0)
+                    fire(o);
+            __syncwarp();
+            u32 head = 0;
+            for (u32 layer = 1;; ++layer)
+            {
+                const u32 tail = ctl[0];
+                if (ctl[1] == 0)
+                {
+                    h = layer;  // the last goal proposition was reached in this layer
+                    break;
+                }
+                if (tail == head)
+                {
+                    h = kDeadEnd;  // the layer added nothing
+                    break;
+                }
+                __syncwarp();
+                // the layer's propositions lower the counts of the operators that need them; those reaching 0 add
+                // the next layer
+                for (u32 k = head + lane; k < tail; k += 32)
+                {
+                    const u32 p = queue[k];
+                    for (u32 q = H.need_begin[p], e = H.need_begin[p + 1]; q < e; ++q)
+                    {
+                        const u32 o = H.need[q];
+                        if (atomicSub(&unsat[o], 1u) == 1u)
+                            fire(o);
+                    }
+                }
+                head = tail;
+                __syncwarp();
             }
         }
         if (lane == 0)
@@ -509,7 +632,25 @@ b2_heuristic* make_heuristic(b2_task* task)
             blob.push_back(0);  // no empty array
             return at;
         };
+        // the operators that need each proposition (the precondition CSR inverted), and the goal propositions as
+        // a bitset, for the triggered evaluation
+        std::vector<u32> need_begin(R.props + 1, 0), need;
+        for (u32 q = 0; q < R.pre.size(); ++q)
+            ++need_begin[R.pre[q] + 1];
+        for (u32 p = 0; p < R.props; ++p)
+            need_begin[p + 1] += need_begin[p];
+        need.assign(R.pre.size(), 0);
+        {
+            std::vector<u32> fill(need_begin.begin(), need_begin.end() - 1);
+            for (u32 o = 0; o < R.ops(); ++o)
+                for (u32 q = R.pre_begin[o]; q < R.pre_begin[o + 1]; ++q)
+                    need[fill[R.pre[q]]++] = o;
+        }
+        std::vector<u32> goal_bits((R.props + 31) / 32 + 1, 0);
+        for (u32 g : R.goal)
+            goal_bits[g >> 5] |= 1u << (g & 31);
         const u64 o0 = put(R.pre_begin), o1 = put(R.pre), o2 = put(R.add_begin), o3 = put(R.add), o4 = put(R.goal);
+        const u64 o5 = put(need_begin), o6 = put(need), o7 = put(goal_bits);
         H->blob.alloc(blob.size() * 4);
         B2_CUDA(cudaMemcpy(H->blob.p, blob.data(), blob.size() * 4, cudaMemcpyHostToDevice));
         const u32* b = H->blob.as<u32>();
@@ -520,7 +661,7 @@ b2_heuristic* make_heuristic(b2_task* task)
         B2_CUDA(cudaMemcpy(H->goal_masks.p, masks.data(), masks.size() * 8, cudaMemcpyHostToDevice));
         H->args = HmaxArgs{b + o0, b + o1, b + o2, b + o3, b + o4, R.ops(), static_cast<u32>(R.goal.size()), W,
                            R.goal_unreachable || task->prog.goal_unsat ? 1u : 0u, H->goal_masks.as<u64>(),
-                           H->goal_masks.as<u64>() + W, nullptr};
+                           H->goal_masks.as<u64>() + W, nullptr, b + o5, b + o6, b + o7, R.props};
     }
     return H.release();
 }
@@ -532,6 +673,19 @@ void launch_hmax(const b2_heuristic& H, const u64* rows, u64 stride, const u32* 
 {
     HmaxArgs a = H.args;
     a.flags = flags;
+    // the triggered evaluation where its per-warp tables (reached props, operator counts, queue) fit shared memory
+    const size_t trig_warp = (a.W + (static_cast<size_t>(a.ops) + a.props + 4 + 1) / 2) * 8;
+    if (a.props >= a.W * 64 - 63 && trig_warp * (kHmaxThreads / 32) <= 160 * 1024)
+    {
+        const size_t smem = trig_warp * (kHmaxThreads / 32);
+        if (smem > 48 * 1024)
+            B2_CUDA(cudaFuncSetAttribute(k_hmax_trig, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem)));
+        const unsigned grid = grid_for(n_bound, kHmaxThreads / 32, static_cast<unsigned>(sms) * 32);
+        k_hmax_trig<<<grid, kHmaxThreads, smem, s>>>(a, rows, stride, nodes, n_dev, n_bound, out, by_node ? 1 : 0);
+        B2_CUDA(cudaGetLastError());
+        return;
+    }
     const unsigned warps = kHmaxThreads / 32;
     const size_t smem = static_cast<size_t>(warps) * 2 * a.W * 8;
     if (smem > 200 * 1024)
@@ -817,7 +971,7 @@ void run_astar(b2_astar& A, b2_astar_result& R)
             a.S.rows = A.rows.as<u64>();
             a.S.W = W;
             a.pi = pi;
-            jit_launch(task->jit->brfs_count[pi], grid, 128, &a, s);
+            jit_launch(task->jit->get(kJitBrfsCount, pi), grid, 128, &a, s);
         }
         else
             dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
@@ -901,7 +1055,7 @@ void run_astar(b2_astar& A, b2_astar_result& R)
             a.W = W;
             a.pi = pi;
             if (task->jit)
-                jit_launch(task->jit->dbrfs_expand[pi], gridc, 128, &a, s);
+                jit_launch(task->jit->get(kJitDbrfsExpand, pi), gridc, 128, &a, s);
             else
                 dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() { k_dexpand<OW, WR><<<gridc, 128, 0, s>>>(T, a); });
             InsertArgs in{};
@@ -1150,7 +1304,7 @@ void run_astar_sharded(b2_astar& A, b2_astar_result& R)
                 a.S.rows = A.rows.as<u64>();
                 a.S.W = W;
                 a.pi = pi;
-                jit_launch(task->jit->brfs_count[pi], grid, 128, &a, s);
+                jit_launch(task->jit->get(kJitBrfsCount, pi), grid, 128, &a, s);
             }
             else
                 dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
@@ -1197,7 +1351,7 @@ void run_astar_sharded(b2_astar& A, b2_astar_result& R)
                 a.pi = pi;
                 const unsigned grid = grid_for(nF, 128, sms * 64);
                 if (task->jit)
-                    jit_launch(task->jit->dbrfs_expand[pi], grid, 128, &a, s);
+                    jit_launch(task->jit->get(kJitDbrfsExpand, pi), grid, 128, &a, s);
                 else
                     dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() { k_dexpand<OW, WR><<<grid, 128, 0, s>>>(T, a); });
                 ++A.launches;

@@ -594,8 +594,8 @@ DevLayerState run_device_layers(b2_brfs& B, const DevLayerState& init, std::vect
                                   reinterpret_cast<u64>(B.sums.p),      reinterpret_cast<u64>(d),
                                   B.cap_layer,                          B.cap_flags,
                                   B.table_slots,                        B.W,
-                                  pi,                                   reinterpret_cast<u64>(B.task->jit->brfs_count[pi]),
-                                  reinterpret_cast<u64>(B.task->jit->brfs_expand[pi]), sms};
+                                  pi,                                   reinterpret_cast<u64>(B.task->jit->get(kJitBrfsCount, pi)),
+                                  reinterpret_cast<u64>(B.task->jit->get(kJitBrfsExpand, pi)), sms};
     if (!B.graph_exec || B.graph_key != key)
         build_device_layers(B, key, d, pi, sms);
     B2_CUDA(cudaGraphLaunch(B.graph_exec, s));
@@ -663,7 +663,7 @@ void build_device_layers(b2_brfs& B, const std::vector<u64>& key, DevLayerState*
         a.S = S;
         a.pi = pi;
         a.dyn = d;
-        jit_launch(B.task->jit->brfs_count[pi], sms * 16, 128, &a, c);
+        jit_launch(B.task->jit->get(kJitBrfsCount, pi), sms * 16, 128, &a, c);
     }
     device_scan_dev(CountIn{B.counts.as<u32>()}, BaseOut{B.cand_base.as<u64>()}, &d->E, B.cap_layer,
                     &d->misc.total_cand, B.sums.as<u64>(), c, &d->misc.status);
@@ -677,7 +677,7 @@ void build_device_layers(b2_brfs& B, const std::vector<u64>& key, DevLayerState*
         a.S = S;
         a.pi = pi;
         a.dyn = d;
-        jit_launch(B.task->jit->brfs_expand[pi], sms * 10, 128, &a, c);
+        jit_launch(B.task->jit->get(kJitBrfsExpand, pi), sms * 10, 128, &a, c);
     }
     k_resolve<<<sms * 8, 256, 0, c>>>(S, d);
     device_scan_dev(WinIn{S.claimed, S.lost}, WinOutDyn{B.state_g.as<u32>(), d}, &d->G, B.cap_flags,
@@ -769,7 +769,7 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
             a.misc = misc;
             a.S = make_store(B, cand_begin);
             a.pi = pi;
-            jit_launch(B.task->jit->brfs_count[pi], grid, 128, &a, s);
+            jit_launch(B.task->jit->get(kJitBrfsCount, pi), grid, 128, &a, s);
         }
         else
             dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
@@ -898,7 +898,7 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
                 a.misc = misc;
                 a.S = S;
                 a.pi = pi;
-                jit_launch(B.task->jit->brfs_expand[pi], grid_e, 128, &a, s);
+                jit_launch(B.task->jit->get(kJitBrfsExpand, pi), grid_e, 128, &a, s);
             }
             else
                 dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {

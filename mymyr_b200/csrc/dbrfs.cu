@@ -627,7 +627,7 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
                 a.pi = pi;
                 a.hist = S.hist();
                 a.world = world;
-                jit_launch(S.owner_counts ? B.task->jit->dbrfs_count[pi] : B.task->jit->brfs_count[pi], grid, 128,
+                jit_launch(S.owner_counts ? B.task->jit->get(kJitDbrfsCount, pi) : B.task->jit->get(kJitBrfsCount, pi), grid, 128,
                            &a, s);
             }
             else if (S.owner_counts)
@@ -790,7 +790,7 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
                 a.overflow = &misc->barrier;
                 const unsigned grid = grid_for(El, 128, sms * 64);
                 if (fused)
-                    jit_launch(B.task->jit->dbrfs_push[pi], grid, 128, &a, s);
+                    jit_launch(B.task->jit->get(kJitDbrfsPush, pi), grid, 128, &a, s);
                 else
                     dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
                         k_dexpand<OW, WR><<<grid, 128, 0, s>>>(T, a);

@@ -287,7 +287,7 @@ b2_status b2_env_create(b2_task* task, const b2_env_config* config, b2_env** out
             dev::EnvArgs a{};
             a.init = e->init.as<u64>();
             a.status = e->init_info.as<u32>();  // the init kernel writes goal, total and per-schema counts here
-            jit_launch(task->jit->env_init[pi], 1, 1, &a, nullptr);
+            jit_launch(task->jit->get(kJitEnvInit, pi), 1, 1, &a, nullptr);
         }
         else
             dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
@@ -391,7 +391,7 @@ b2_status b2_env_step(b2_env* env, const b2_env_batch* batch, const b2_step_out*
             a.dead_end_terminal = p.dead_end_terminal;
             a.autoreset = p.autoreset;
             a.pi = p.pi;
-            jit_launch(env->task->jit->env_step[p.pi], grid, 128, &a, s);
+            jit_launch(env->task->jit->get(kJitEnvStep, p.pi), grid, 128, &a, s);
         }
         else
             dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {

@@ -153,14 +153,14 @@ extern "C" b2_status b2_expand(b2_task* task, const uint64_t* states, uint64_t r
         a.succ_hash = out->succ_hash;
         a.status = status;
         if (nseg && task->jit)
-            jit_launch(task->jit->expand_count[pi], grid, 128, &a, s);
+            jit_launch(task->jit->get(kJitExpandCount, pi), grid, 128, &a, s);
         else if (nseg)
             dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
                 k_expand_count<OW, WR><<<grid, 128, 0, s>>>(task->dev, states, rows, words, pi, counts);
             });
         device_scan(SegCountIn{counts}, SegCountOut{seg_off}, nseg, total, sums, s, status);
         if (nseg && task->jit)
-            jit_launch(task->jit->expand_write[pi], grid, 128, &a, s);
+            jit_launch(task->jit->get(kJitExpandWrite, pi), grid, 128, &a, s);
         else if (nseg)
             dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
                 k_expand_write<OW, WR><<<grid, 128, 0, s>>>(task->dev, states, rows, words, pi, seg_off, *out, status);
@@ -301,7 +301,7 @@ extern "C" b2_status b2_expand_noalloc(b2_task* task, const uint64_t* states, ui
         a.succ_hash = out->succ_hash;
         a.status = status;
         if (nseg && task->jit)
-            jit_launch(task->jit->expand_count[pi], grid, 128, &a, s);
+            jit_launch(task->jit->get(kJitExpandCount, pi), grid, 128, &a, s);
         else if (nseg)
             dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
                 k_expand_count<OW, WR><<<grid, 128, 0, s>>>(task->dev, states, rows, words, pi, counts);
@@ -309,7 +309,7 @@ extern "C" b2_status b2_expand_noalloc(b2_task* task, const uint64_t* states, ui
         if (nseg)
             device_scan(SegCountIn{counts}, SegCountOut{seg_off}, nseg, total, sums, s, status);
         if (nseg && task->jit)
-            jit_launch(task->jit->expand_write[pi], grid, 128, &a, s);
+            jit_launch(task->jit->get(kJitExpandWrite, pi), grid, 128, &a, s);
         else if (nseg)
             dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
                 k_expand_write<OW, WR><<<grid, 128, 0, s>>>(task->dev, states, rows, words, pi, seg_off, *out, status);

@@ -1,7 +1,9 @@
 // Run-time compilation of a task's kernels: the generated matcher (codegen.cpp) plus jit_kernels.cuh, compiled by
-// NVRTC (loaded with dlopen on first use) to an sm_100a cubin, loaded with the runtime's library API
-// (cudaLibraryLoadData) and launched with cudaLaunchKernel. Cubins are cached per process by source digest, loaded
-// libraries per (device, digest): tasks with the same compiled program share them. Compiling needs no GPU.
+// NVRTC (loaded with dlopen on first use) to sm_100a cubins, loaded with the runtime's library API
+// (cudaLibraryLoadData) and launched with cudaLaunchKernel. Every kernel pair (witness pruning on, off) is its own
+// compile unit, compiled when first used: a task with a large matcher pays only for the kernels its calls launch.
+// Cubins are cached per process by (source digest, kernel), modules per (device, digest): tasks with the same
+// compiled program share them. Compiling needs no GPU.
 
 #include "common.cuh"
 #include "jit.hpp"
@@ -21,7 +23,7 @@ namespace b2
 namespace
 {
 std::mutex g_mu;
-std::map<u64, std::shared_ptr<std::vector<char>>> g_cubins;          // digest -> cubin
+std::map<std::pair<u64, u32>, std::shared_ptr<std::vector<char>>> g_cubins;  // (digest, kernel) -> cubin
 std::map<std::pair<int, u64>, std::shared_ptr<JitModule>> g_modules;  // (device, digest) -> module
 
 u64 digest(const std::string& s)
@@ -81,15 +83,17 @@ const Nvrtc& nvrtc()
             throw Error(B2_CUDA_ERROR, std::string(#call) + ": " + N.error(r_));                                  \
     } while (0)
 
-std::shared_ptr<std::vector<char>> compile(const std::string& src, std::string& log)
+/// Compiles the kernel pair `which` of the source (kJitKernels: all of them).
+std::shared_ptr<std::vector<char>> compile(const std::string& src, u32 which, std::string& log)
 {
     const Nvrtc& N = nvrtc();
     nvrtcProgram prog;
     const char* headers[] = {b2_jit_core_source, b2_jit_kernels_source};
     const char* names[] = {"b2_core.cuh", "b2_jit_kernels.cuh"};
     B2_NVRTC(N.create(&prog, src.c_str(), "b2_task.cu", 2, headers, names));
-    const char* opts[] = {"-arch=sm_100a", "-std=c++20", "-lineinfo", "-DNDEBUG", "-default-device"};
-    const nvrtcResult rc = N.compile(prog, 5, opts);
+    const std::string select = which == kJitKernels ? "-DB2J_ALL" : "-DB2J_K" + std::to_string(which);
+    const char* opts[] = {"-arch=sm_100a", "-std=c++20", "-lineinfo", "-DNDEBUG", "-default-device", select.c_str()};
+    const nvrtcResult rc = N.compile(prog, 6, opts);
     size_t n = 0;
     N.log_size(prog, &n);
     log.assign(n, '\0');
@@ -115,12 +119,47 @@ cudaKernel_t kernel(cudaLibrary_t lib, const char* name)
     B2_CUDA(cudaLibraryGetKernel(&k, lib, name));
     return k;
 }
+
+constexpr const char* kKernelNames[kJitKernels] = {"brfs_count", "brfs_expand", "dbrfs_expand", "dbrfs_count",
+                                                   "dbrfs_push", "env_init",    "env_step",     "expand_count",
+                                                   "expand_write"};
+
+/// The cubin of kernel pair `which` (kJitKernels: all) of a source, compiled once per process.
+std::shared_ptr<std::vector<char>> cubin_of(const std::string& src, u64 key, u32 which, std::string* log_out)
+{
+    {
+        std::lock_guard lock(g_mu);
+        if (auto it = g_cubins.find({key, which}); it != g_cubins.end())
+            return it->second;
+    }
+    std::string log;
+    auto cubin = compile(src, which, log);
+    if (log_out)
+        *log_out = log;
+    std::lock_guard lock(g_mu);
+    return g_cubins.emplace(std::make_pair(key, which), cubin).first->second;
+}
 }  // namespace
 
 JitModule::~JitModule()
 {
-    if (lib)
-        cudaLibraryUnload(lib);
+    for (cudaLibrary_t l : lib)
+        if (l)
+            cudaLibraryUnload(l);
+}
+
+cudaKernel_t JitModule::get(JitKernel which, u32 pi)
+{
+    std::lock_guard lock(mu);
+    if (!lib[which])
+    {
+        const auto cubin = cubin_of(source, digest, which, &log);
+        B2_CUDA(cudaLibraryLoadData(&lib[which], cubin->data(), nullptr, nullptr, 0, nullptr, nullptr, 0));
+        const std::string name = std::string("b2j_") + kKernelNames[which];
+        k[which][0] = kernel(lib[which], (name + "_w").c_str());
+        k[which][1] = kernel(lib[which], (name + "_nw").c_str());
+    }
+    return k[which][pi];
 }
 
 std::shared_ptr<std::vector<char>> jit_cubin(const Program& prog, u64* key_out, std::string* log_out)
@@ -129,58 +168,30 @@ std::shared_ptr<std::vector<char>> jit_cubin(const Program& prog, u64* key_out, 
     const u64 key = digest(src);
     if (key_out)
         *key_out = key;
-    {
-        std::lock_guard lock(g_mu);
-        if (auto it = g_cubins.find(key); it != g_cubins.end())
-            return it->second;
-    }
-    std::string log;
-    auto cubin = compile(src, log);
-    if (log_out)
-        *log_out = log;
-    std::lock_guard lock(g_mu);
-    return g_cubins.emplace(key, cubin).first->second;
+    return cubin_of(src, key, kJitKernels, log_out);
 }
 
 std::shared_ptr<JitModule> jit_module(int device, const Program& prog)
 {
-    u64 key = 0;
-    std::string log;
-    const std::shared_ptr<std::vector<char>> cubin = jit_cubin(prog, &key, &log);
+    std::string src = generate_matcher_source(prog);
+    const u64 key = digest(src);
     {
         std::lock_guard lock(g_mu);
         if (auto it = g_modules.find({device, key}); it != g_modules.end())
             return it->second;
     }
     auto m = std::make_shared<JitModule>();
+    m->device = device;
     m->digest = key;
-    m->log = log;
-    B2_CUDA(cudaLibraryLoadData(&m->lib, cubin->data(), nullptr, nullptr, 0, nullptr, nullptr, 0));
-    m->brfs_count[0] = kernel(m->lib, "b2j_brfs_count_w");
-    m->brfs_count[1] = kernel(m->lib, "b2j_brfs_count_nw");
-    m->brfs_expand[0] = kernel(m->lib, "b2j_brfs_expand_w");
-    m->brfs_expand[1] = kernel(m->lib, "b2j_brfs_expand_nw");
-    m->dbrfs_expand[0] = kernel(m->lib, "b2j_dbrfs_expand_w");
-    m->dbrfs_expand[1] = kernel(m->lib, "b2j_dbrfs_expand_nw");
-    m->dbrfs_push[0] = kernel(m->lib, "b2j_dbrfs_push_w");
-    m->dbrfs_push[1] = kernel(m->lib, "b2j_dbrfs_push_nw");
-    m->dbrfs_count[0] = kernel(m->lib, "b2j_dbrfs_count_w");
-    m->dbrfs_count[1] = kernel(m->lib, "b2j_dbrfs_count_nw");
-    m->env_init[0] = kernel(m->lib, "b2j_env_init_w");
-    m->env_init[1] = kernel(m->lib, "b2j_env_init_nw");
-    m->env_step[0] = kernel(m->lib, "b2j_env_step_w");
-    m->env_step[1] = kernel(m->lib, "b2j_env_step_nw");
-    m->expand_count[0] = kernel(m->lib, "b2j_expand_count_w");
-    m->expand_count[1] = kernel(m->lib, "b2j_expand_count_nw");
-    m->expand_write[0] = kernel(m->lib, "b2j_expand_write_w");
-    m->expand_write[1] = kernel(m->lib, "b2j_expand_write_nw");
-    // the batched expand's kernels are loaded on the device now, not at their first launch, so that
+    m->source = std::move(src);
+    // the batched expand's kernels are compiled and loaded on the device now, not at their first launch, so that
     // b2_expand_noalloc's calls load nothing
-    for (cudaKernel_t k : {m->expand_count[0], m->expand_count[1], m->expand_write[0], m->expand_write[1]})
-    {
-        cudaFuncAttributes attr{};
-        B2_CUDA(cudaFuncGetAttributes(&attr, reinterpret_cast<const void*>(k)));
-    }
+    for (JitKernel which : {kJitExpandCount, kJitExpandWrite})
+        for (u32 pi = 0; pi < 2; ++pi)
+        {
+            cudaFuncAttributes attr{};
+            B2_CUDA(cudaFuncGetAttributes(&attr, reinterpret_cast<const void*>(m->get(which, pi))));
+        }
     std::lock_guard lock(g_mu);
     return g_modules.emplace(std::make_pair(device, key), m).first->second;
 }

@@ -656,21 +656,40 @@ B2_DI void expand_write(const ExpandArgs& a)
 }  // namespace gen
 }  // namespace b2
 
+#if defined(B2J_ALL) || defined(B2J_K0)
+// Each pair is compiled alone (-DB2J_K<index of the pair in JitKernel>, jit.cu) or all together (-DB2J_ALL).
 extern "C" __global__ void __launch_bounds__(128) b2j_brfs_count_w(b2::dev::BrfsArgs a) { b2::gen::brfs_count<0>(a); }
 extern "C" __global__ void __launch_bounds__(128) b2j_brfs_count_nw(b2::dev::BrfsArgs a) { b2::gen::brfs_count<1>(a); }
+#endif
+#if defined(B2J_ALL) || defined(B2J_K1)
 extern "C" __global__ void __launch_bounds__(128, 10) b2j_brfs_expand_w(b2::dev::BrfsArgs a) { b2::gen::brfs_expand<0>(a); }
 extern "C" __global__ void __launch_bounds__(128, 10) b2j_brfs_expand_nw(b2::dev::BrfsArgs a) { b2::gen::brfs_expand<1>(a); }
+#endif
+#if defined(B2J_ALL) || defined(B2J_K2)
 extern "C" __global__ void __launch_bounds__(128) b2j_dbrfs_expand_w(b2::dev::DExpandArgs a) { b2::gen::dbrfs_expand<0>(a); }
 extern "C" __global__ void __launch_bounds__(128) b2j_dbrfs_expand_nw(b2::dev::DExpandArgs a) { b2::gen::dbrfs_expand<1>(a); }
+#endif
+#if defined(B2J_ALL) || defined(B2J_K3)
 extern "C" __global__ void __launch_bounds__(128) b2j_dbrfs_count_w(b2::dev::BrfsArgs a) { b2::gen::dbrfs_count<0>(a); }
 extern "C" __global__ void __launch_bounds__(128) b2j_dbrfs_count_nw(b2::dev::BrfsArgs a) { b2::gen::dbrfs_count<1>(a); }
+#endif
+#if defined(B2J_ALL) || defined(B2J_K4)
 extern "C" __global__ void __launch_bounds__(128) b2j_dbrfs_push_w(b2::dev::DExpandArgs a) { b2::gen::dbrfs_expand_push<0>(a); }
 extern "C" __global__ void __launch_bounds__(128) b2j_dbrfs_push_nw(b2::dev::DExpandArgs a) { b2::gen::dbrfs_expand_push<1>(a); }
+#endif
+#if defined(B2J_ALL) || defined(B2J_K5)
 extern "C" __global__ void b2j_env_init_w(b2::dev::EnvArgs a) { b2::gen::env_init<0>(a); }
 extern "C" __global__ void b2j_env_init_nw(b2::dev::EnvArgs a) { b2::gen::env_init<1>(a); }
+#endif
+#if defined(B2J_ALL) || defined(B2J_K6)
 extern "C" __global__ void __launch_bounds__(128) b2j_env_step_w(b2::dev::EnvArgs a) { b2::gen::env_step<0>(a); }
 extern "C" __global__ void __launch_bounds__(128) b2j_env_step_nw(b2::dev::EnvArgs a) { b2::gen::env_step<1>(a); }
+#endif
+#if defined(B2J_ALL) || defined(B2J_K7)
 extern "C" __global__ void __launch_bounds__(128) b2j_expand_count_w(b2::dev::ExpandArgs a) { b2::gen::expand_count<0>(a); }
 extern "C" __global__ void __launch_bounds__(128) b2j_expand_count_nw(b2::dev::ExpandArgs a) { b2::gen::expand_count<1>(a); }
+#endif
+#if defined(B2J_ALL) || defined(B2J_K8)
 extern "C" __global__ void __launch_bounds__(128) b2j_expand_write_w(b2::dev::ExpandArgs a) { b2::gen::expand_write<0>(a); }
 extern "C" __global__ void __launch_bounds__(128) b2j_expand_write_nw(b2::dev::ExpandArgs a) { b2::gen::expand_write<1>(a); }
+#endif
