@@ -296,12 +296,13 @@ def env_secondary(args, device, world=1, rank=0, pg=None, with_cpu=False):
         for _ in range(per_graph):
             env.step(stream=stream.cuda_stream)
     replays = max(1, args.env_steps // per_graph)
-    graph.replay()
-    stream.synchronize()
-    a.record(stream)
-    for _ in range(replays):
+    with torch.cuda.stream(stream):  # replay() launches on the current stream
         graph.replay()
-    b.record(stream)
+        stream.synchronize()
+        a.record(stream)
+        for _ in range(replays):
+            graph.replay()
+        b.record(stream)
     stream.synchronize()
     ms_graph = a.elapsed_time(b) * args.env_steps / (replays * per_graph)
     launches += replays * per_graph

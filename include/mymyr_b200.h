@@ -144,6 +144,11 @@ b2_status b2_task_slot_atom(const b2_task* task, uint32_t slot, uint32_t* pred_a
  * hash::state of n device rows of `words` words into out[n] (device). Replaces hash_rows
  * (python/src/module.cpp:187) for classical rows (numeric_words = 0). */
 b2_status b2_hash_rows(b2_ctx* ctx, const uint64_t* rows, uint64_t n, uint32_t words, uint64_t* out, void* stream);
+/* hash_rows with numeric words: each row is [words - numeric_words atom words | numeric_words numeric words], hashed
+ * as hash::state (include/mymyr/core/hash.hpp:55-60): the trimmed atom words seeded by hash::words of the numeric
+ * words. numeric_words = 0 is b2_hash_rows. */
+b2_status b2_hash_rows_numeric(b2_ctx* ctx, const uint64_t* rows, uint64_t n, uint32_t words, uint32_t numeric_words,
+                               uint64_t* out, void* stream);
 
 /* ------------------------------------------------------------------------------------------------ batched expand
  * rl::expand (include/mymyr/rl/expand.hpp:137-147) on the device: the successors of n states in canonical order
@@ -392,7 +397,14 @@ b2_status b2_env_reset(b2_env* env, const b2_env_batch* batch, const uint8_t* ma
 /* One step of every row: actions[rows] (int64, device; NULL: the random policy). */
 b2_status b2_env_step(b2_env* env, const b2_env_batch* batch, const b2_step_out* out, const int64_t* actions,
                       void* stream);
-/* Sticky device status of the env (0: none). */
+/* b2_env_step with next_task_ids[rows] (int32, device; NULL: none), the task an autoresetting row restarts in
+ * (cuda::DeviceEnv::step, include/mymyr/cuda/env.hpp:180-184). The env has one task, id 0: another id, in any row, is
+ * reported by b2_env_check_errors (B2_INVALID_ARGUMENT) and the rows keep their task. */
+b2_status b2_env_step_ex(b2_env* env, const b2_env_batch* batch, const b2_step_out* out, const int64_t* actions,
+                         const int32_t* next_task_ids, void* stream);
+/* The env's device status since the last check (synchronizes the device; the status is cleared once reported):
+ * B2_DEVICE_FAULT when a step found a state whose count cache did not match it (states written without a reset),
+ * B2_INVALID_ARGUMENT for next_task_ids outside the env's tasks. */
 b2_status b2_env_check_errors(b2_env* env);
 void b2_env_destroy(b2_env* env);
 

@@ -155,6 +155,7 @@ SIGNATURES = {
     "b2_task_initial_state": (C.c_int, [P, P, U32]),
     "b2_task_slot_atom": (C.c_int, [P, U32, P, U32]),
     "b2_hash_rows": (C.c_int, [P, P, U64, U32, P, P]),
+    "b2_hash_rows_numeric": (C.c_int, [P, P, U64, U32, U32, P, P]),
     "b2_expand": (C.c_int, [P, P, U64, U32, C.c_int, C.POINTER(Expansion), P]),
     "b2_expand_noalloc": (C.c_int, [P, P, U64, U32, C.c_int, C.POINTER(Expansion), P]),
     "b2_comm_id_new": (C.c_int, [C.POINTER(CommId)]),
@@ -183,6 +184,7 @@ SIGNATURES = {
     "b2_env_create": (C.c_int, [P, C.POINTER(EnvConfig), PP]),
     "b2_env_reset": (C.c_int, [P, C.POINTER(EnvBatch), P, P, P]),
     "b2_env_step": (C.c_int, [P, C.POINTER(EnvBatch), C.POINTER(StepOut), P, P]),
+    "b2_env_step_ex": (C.c_int, [P, C.POINTER(EnvBatch), C.POINTER(StepOut), P, P, P]),
     "b2_env_check_errors": (C.c_int, [P]),
     "b2_env_destroy": (None, [P]),
 }

@@ -215,12 +215,16 @@ void upload(b2_task& t)
     D.goal_neg = reinterpret_cast<const u64*>(b + o_gn);
 }
 
-__global__ void k_hash_rows(const u64* __restrict__ rows, u64 n, u32 W, u64* __restrict__ out)
+/// hash::state of rows [atom words | nnum numeric words] (W words in all): the trimmed atom words, seeded by the
+/// numeric words' hash when there are any.
+__global__ void k_hash_rows(const u64* __restrict__ rows, u64 n, u32 W, u32 nnum, u64* __restrict__ out)
 {
     for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < n; i += static_cast<u64>(gridDim.x) * blockDim.x)
     {
         const u64* r = rows + i * W;
-        out[i] = hash_words([&](u32 k) { return __ldg(r + k); }, W);
+        const u32 na = W - nnum;
+        const u64 seed = nnum ? dev::hash_span([&](u32 k) { return __ldg(r + na + k); }, nnum) : dev::kHashSeed;
+        out[i] = hash_words([&](u32 k) { return __ldg(r + k); }, na, seed);
     }
 }
 }  // namespace
@@ -413,18 +417,26 @@ b2_status b2_task_slot_atom(const b2_task* task, uint32_t slot, uint32_t* pred_a
     });
 }
 
-b2_status b2_hash_rows(b2_ctx* ctx, const uint64_t* rows, uint64_t n, uint32_t words, uint64_t* out, void* stream)
+b2_status b2_hash_rows_numeric(b2_ctx* ctx, const uint64_t* rows, uint64_t n, uint32_t words, uint32_t numeric_words,
+                               uint64_t* out, void* stream)
 {
     return guarded([&] {
         if (!ctx || (n && (!rows || !out)) || words == 0)
             throw std::invalid_argument("b2_hash_rows: bad argument");
+        if (numeric_words > words)
+            throw std::invalid_argument("b2_hash_rows: numeric_words exceeds the row width");
         if (!n)
             return;
         B2_CUDA(cudaSetDevice(ctx->device));
         const unsigned grid = grid_for(n, 256, static_cast<unsigned>(ctx->sms) * 16);
-        k_hash_rows<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(rows, n, words, out);
+        k_hash_rows<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(rows, n, words, numeric_words, out);
         B2_CUDA(cudaGetLastError());
     });
+}
+
+b2_status b2_hash_rows(b2_ctx* ctx, const uint64_t* rows, uint64_t n, uint32_t words, uint64_t* out, void* stream)
+{
+    return b2_hash_rows_numeric(ctx, rows, n, words, 0, out, stream);
 }
 
 }  // extern "C"

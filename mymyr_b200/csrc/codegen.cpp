@@ -203,6 +203,11 @@ struct Gen
     std::string canon;  // the index-order matcher of the schema being generated, for the fallback
     u32 buffer_arity = 0;
 
+    /// Counting matchers (Count<S, PI>): the leaf adds its candidates instead of emitting them. Selecting matchers
+    /// (Select<S, PI>): the leaf skips r_ bindings, by popcount where it can, and emits the next one.
+    bool counting = false;
+    bool selecting = false;
+
     void level(const DProgram& pg, u32 d, u32 arity)
     {
         const DLevel& L = P.levels[pg.level_begin + d];
@@ -212,6 +217,51 @@ struct Gen
             o << "    u64 c" << D << "_" << k << " = " << hex(P.pool[L.dom0 + k]) << ";\n";
         for (u32 fi = L.filt_begin; fi < L.filt_end; ++fi)
             filter(P.filters[fi], d);
+        if (counting && d + 1 == pg.nlevels && L.chk_begin == L.chk_end && d <= pg.first_exist)
+        {
+            // a leaf without checks: every candidate is a binding (an effect level), or the level's first candidate
+            // is the binding's witness (the one witness level)
+            o << "    n_ += ";
+            if (d < pg.first_exist)
+                for (u32 k = 0; k < OW; ++k)
+                    o << (k ? " + " : "") << "static_cast<u32>(__popcll(c" << D << "_" << k << "))";
+            else
+            {
+                o << "((";
+                for (u32 k = 0; k < OW; ++k)
+                    o << (k ? " | " : "") << "c" << D << "_" << k;
+                o << ") != 0ull ? 1u : 0u)";
+            }
+            o << ";\n  }\n";
+            return;
+        }
+        if (selecting && d + 1 == pg.nlevels && L.chk_begin == L.chk_end && d <= pg.first_exist)
+        {
+            const std::string bp = "b[" + std::to_string(L.param) + "]";
+            if (d < pg.first_exist)
+                for (u32 k = 0; k < OW; ++k)
+                {
+                    const std::string c = "c" + D + "_" + std::to_string(k);
+                    o << "    { const u32 p_ = static_cast<u32>(__popcll(" << c << "));\n"
+                      << "      if (sel_ < p_) { " << bp << " = " << 64 * k << "u + nth_bit64(" << c
+                      << ", static_cast<u32>(sel_)); emit(static_cast<const u32*>(b)); return true; }\n"
+                      << "      sel_ -= p_; }\n";
+                }
+            else
+            {
+                o << "    {\n";
+                for (u32 k = 0; k < OW; ++k)
+                {
+                    const std::string c = "c" + D + "_" + std::to_string(k);
+                    o << "      " << (k ? "else if (" : "if (") << c << ") { if (sel_ == 0) { " << bp << " = " << 64 * k
+                      << "u + (__ffsll(static_cast<long long>(" << c
+                      << ")) - 1); emit(static_cast<const u32*>(b)); return true; } --sel_; }\n";
+                }
+                o << "    }\n";
+            }
+            o << "  }\n";
+            return;
+        }
         // one loop per level over the candidates in ascending object order (lowest word first)
         o << "    for (;;) {\n      u32 o" << D << ";\n";
         for (u32 k = 0; k < OW; ++k)
@@ -234,11 +284,13 @@ struct Gen
         }
         else if (d + 1 == pg.nlevels)
         {
-            o << "      if (!emit(static_cast<const u32*>(b))) return false;\n";
+            o << (counting    ? "      ++n_;\n"
+                  : selecting ? "      if (sel_ == 0) { emit(static_cast<const u32*>(b)); return true; }\n      --sel_;\n"
+                              : "      if (!emit(static_cast<const u32*>(b))) return false;\n");
             if (pg.first_exist < pg.nlevels)
             {
                 if (pg.first_exist == 0)
-                    o << "      return true;\n";
+                    o << (counting ? "      return n_;\n" : selecting ? "      return false;\n" : "      return true;\n");
                 else
                     o << "      goto next_" << pg.first_exist - 1 << ";\n";
             }
@@ -283,6 +335,75 @@ struct Gen
                 o << "    if (!emit(static_cast<const u32*>(b))) return false;\n  }\n";
             }
             o << "  return true;\n";
+        }
+        o << "}\n};\n";
+    }
+
+    /// Count<s, pi>: the number of bindings Run<s, pi> emits, by the same levels without emitting (the order does not
+    /// matter, so a schema with a selectivity order counts in it); a leaf level without checks adds its candidates
+    /// by popcount.
+    void count(u32 s, u32 pi)
+    {
+        const DSchema& S = P.schemas[s];
+        const DProgram& pg = S.prog[pi];
+        o << "template<> struct Count<" << s << ", " << pi << "> {\n"
+          << "template<class St> B2_DI static u32 go(const St& st) {\n  (void)st;\n";
+        if (pg.never)
+        {
+            o << "  return 0u;\n}\n};\n";
+            return;
+        }
+        const bool fast = S.fast_on && pg.first_exist == pg.nlevels && pg.nlevels == S.arity && !pg.sorted;
+        const DProgram& cp = fast ? S.fast : pg;
+        o << "  u32 b[" << (S.arity ? S.arity : 1) << "] = {};\n  (void)b;\n  u32 n_ = 0;\n";
+        for (u32 c = cp.pre_begin; c < cp.pre_end; ++c)
+            o << "  if (!" << holds_expr(P.lits[P.checks[c]]) << ") return 0u;\n";
+        if (cp.nlevels == 0)
+            o << "  return 1u;\n";
+        else
+        {
+            counting = true;
+            level(cp, 0, S.arity);
+            counting = false;
+            o << "  return n_;\n";
+        }
+        o << "}\n};\n";
+    }
+
+    /// Select<s, pi>: emits the r-th binding (0-based) of Run<s, pi>'s canonical order and returns true, or returns
+    /// false when there are at most r. It walks the index-order program (the canonical order without buffering);
+    /// a leaf level without checks skips whole candidate sets by popcount. Programs whose bindings are emitted
+    /// sorted select through Run.
+    void select(u32 s, u32 pi)
+    {
+        const DSchema& S = P.schemas[s];
+        const DProgram& pg = S.prog[pi];
+        o << "template<> struct Select<" << s << ", " << pi << "> {\n"
+          << "template<class St, class E> B2_DI static bool go(const St& st, u64 sel_, E&& emit) {\n  (void)st;\n";
+        if (pg.never)
+        {
+            o << "  (void)sel_; (void)emit;\n  return false;\n}\n};\n";
+            return;
+        }
+        if (pg.sorted)
+        {
+            o << "  bool found_ = false;\n"
+              << "  Run<" << s << ", " << pi << ">::go(st, [&](const u32* b) {\n"
+              << "    if (sel_-- != 0) return true;\n    emit(b);\n    found_ = true;\n    return false;\n  });\n"
+              << "  return found_;\n}\n};\n";
+            return;
+        }
+        o << "  u32 b[" << (S.arity ? S.arity : 1) << "] = {};\n";
+        for (u32 c = pg.pre_begin; c < pg.pre_end; ++c)
+            o << "  if (!" << holds_expr(P.lits[P.checks[c]]) << ") return false;\n";
+        if (pg.nlevels == 0)
+            o << "  if (sel_ != 0) return false;\n  emit(static_cast<const u32*>(b));\n  return true;\n";
+        else
+        {
+            selecting = true;
+            level(pg, 0, S.arity);
+            selecting = false;
+            o << "  return false;\n";
         }
         o << "}\n};\n";
     }
@@ -357,6 +478,8 @@ struct Gen
         o << "}\n";
         o << "template<int S, int PI> struct Run;\ntemplate<int S, int PI> struct RunCanon;\n"
           << "template<int S, int PI> struct RunRaw;\n"
+          << "template<int S, int PI> struct Count;\n"
+          << "template<int S, int PI> struct Select;\n"
           << "template<int S> struct Eff;\n";
         for (u32 s = 0; s < P.nschemas; ++s)
         {
@@ -366,10 +489,16 @@ struct Gen
                 if (pi == 0 && pg.never == 0xFFFFFFFFu)
                 {
                     o << "template<> struct Run<" << s << ", 0> { template<class St, class E> B2_DI static bool go("
-                      << "const St&, E&&) { return true; } };\n";
+                      << "const St&, E&&) { return true; } };\n"
+                      << "template<> struct Count<" << s << ", 0> { template<class St> B2_DI static u32 go("
+                      << "const St&) { return 0u; } };\n"
+                      << "template<> struct Select<" << s << ", 0> { template<class St, class E> B2_DI static bool "
+                      << "go(const St&, u64, E&&) { return false; } };\n";
                     continue;
                 }
                 run(s, pi);
+                count(s, pi);
+                select(s, pi);
             }
             const DSchema& S = P.schemas[s];
             o << "template<> struct Eff<" << s << "> {\n  static constexpr int ND = " << (S.del_end - S.del_begin)

@@ -50,20 +50,28 @@ B2_DI u64 mix64(u64 x)
 
 B2_DI u64 mulfold(u64 a, u64 b) { return (a * b) ^ __umul64hi(a, b); }
 
-/// hash::state_words over words w(0..W-1) of a zero-padded row (trailing zero words ignored).
+/// hash::words over all n words w(0..n-1), untrimmed; `seed` as hash::words takes it.
 template<class Get>
-B2_DI u64 hash_words(Get&& w, u32 W)
+B2_DI u64 hash_span(Get&& w, u32 n, u64 seed = kHashSeed)
 {
-    u32 n = W;
-    while (n > 0 && w(n - 1) == 0)
-        --n;
-    u64 h = kHashSeed ^ (static_cast<u64>(n) * kHashP1);
+    u64 h = seed ^ (static_cast<u64>(n) * kHashP1);
     u32 i = 0;
     for (; i + 1 < n; i += 2)
         h = mulfold(h ^ w(i) ^ kHashP1, w(i + 1) ^ kHashP2);
     if (i < n)
         h = mulfold(h ^ w(i) ^ kHashP1, kHashP2);
     return mix64(h);
+}
+
+/// hash::state_words over words w(0..W-1) of a zero-padded row (trailing zero words ignored); a row with numeric
+/// words passes their hash_span as the seed (hash::state).
+template<class Get>
+B2_DI u64 hash_words(Get&& w, u32 W, u64 seed = kHashSeed)
+{
+    u32 n = W;
+    while (n > 0 && w(n - 1) == 0)
+        --n;
+    return hash_span(w, n, seed);
 }
 
 /// hash_words for a compile-time width NW (every loop unrolled, so register rows are indexed by constants); the
@@ -134,6 +142,13 @@ B2_DI u64 philox_bits64(u64 seed, u64 env, u64 draw, u32 purpose)
         k1 += 0xBB67AE85u;
     }
     return static_cast<u64>(c0) | (static_cast<u64>(c1) << 32);
+}
+
+/// The position of the r-th set bit (0-based, from the lowest) of x; x has more than r set bits.
+B2_DI u32 nth_bit64(u64 x, u32 r)
+{
+    const u32 lo = static_cast<u32>(x), k = static_cast<u32>(__popc(lo));
+    return r < k ? __fns(lo, 0u, static_cast<int>(r + 1)) : 32u + __fns(static_cast<u32>(x >> 32), 0u, static_cast<int>(r - k + 1));
 }
 
 /// high64(x * n) (rng::below).
@@ -319,6 +334,7 @@ B2_DI u64 canonical_hash(const St& st, u32 W)
 constexpr u32 kStatusProbeLimit = 1u;
 constexpr u32 kStatusEffectOverflow = 2u;
 constexpr u32 kStatusCapacity = 4u;
+constexpr u32 kStatusTaskId = 8u;  // an env's next_task_ids named a task it does not have
 
 // ------------------------------------------------------------------------------------------------ BrFS hash set
 constexpr u64 kEmpty = ~u64{0};

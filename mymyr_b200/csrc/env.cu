@@ -43,6 +43,17 @@ __global__ void k_env_init(DevTask T, const u64* __restrict__ init, u32 W, u32 p
     out[1] = total;
 }
 
+/// next_task_ids of a one-task env: every id must name its one instance (0); another id is reported by
+/// b2_env_check_errors, and the row keeps its instance (cuda::DeviceEnv::step, include/mymyr/cuda/env.hpp:180-184).
+__global__ void k_check_task_ids(const i32* __restrict__ ids, u64 rows, u32* status)
+{
+    bool bad = false;
+    for (u64 i = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; i < rows; i += static_cast<u64>(gridDim.x) * blockDim.x)
+        bad |= ids[i] != 0;
+    if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0)
+        atomicOr(status, dev::kStatusTaskId);
+}
+
 struct EnvParams
 {
     u64 seed;
@@ -331,6 +342,12 @@ b2_status b2_env_reset(b2_env* env, const b2_env_batch* batch, const uint8_t* ma
 b2_status b2_env_step(b2_env* env, const b2_env_batch* batch, const b2_step_out* out, const int64_t* actions,
                       void* stream)
 {
+    return b2_env_step_ex(env, batch, out, actions, nullptr, stream);
+}
+
+b2_status b2_env_step_ex(b2_env* env, const b2_env_batch* batch, const b2_step_out* out, const int64_t* actions,
+                         const int32_t* next_task_ids, void* stream)
+{
     return guarded([&] {
         if (!env || !out)
             throw std::invalid_argument("b2_env_step: null argument");
@@ -346,6 +363,9 @@ b2_status b2_env_step(b2_env* env, const b2_env_batch* batch, const b2_step_out*
             return;
         B2_CUDA(cudaSetDevice(env->task->ctx->device));
         cudaStream_t s = static_cast<cudaStream_t>(stream);
+        if (next_task_ids)
+            k_check_task_ids<<<grid_for(batch->rows, 256, static_cast<unsigned>(env->task->ctx->sms) * 8), 256, 0, s>>>(
+                next_task_ids, batch->rows, env->status.as<u32>());
         EnvParams p;
         p.seed = env->cfg.seed;
         p.max_steps = env->cfg.max_steps;
@@ -413,8 +433,13 @@ b2_status b2_env_check_errors(b2_env* env)
         u32 st = 0;
         B2_CUDA(cudaMemcpy(&st, env->status.p, 4, cudaMemcpyDeviceToHost));
         if (st)
+            B2_CUDA(cudaMemset(env->status.p, 0, 4));  // reported once; later steps flag anew
+        if (st & ~dev::kStatusTaskId)
             throw Error(B2_DEVICE_FAULT, "b2_env: the per-schema count cache disagreed with a state (status " +
                                              std::to_string(st) + "); refresh the batch with b2_env_reset");
+        if (st & dev::kStatusTaskId)
+            throw std::invalid_argument("b2_env: a next_task_ids entry outside the env's tasks (a one-task env "
+                                        "takes id 0 only); the rows kept their task");
     });
 }
 

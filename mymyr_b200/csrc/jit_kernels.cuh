@@ -69,12 +69,7 @@ template<int PI>
 B2_DI u32 count_all(const Row& st)
 {
     u32 c = 0;
-    for_each_schema([&]<int S>() {
-        Run<S, PI>::go(st, [&](const u32*) {
-            ++c;
-            return true;
-        });
-    });
+    for_each_schema([&]<int S>() { c += Count<S, PI>::go(st); });
     return c;
 }
 
@@ -443,11 +438,7 @@ B2_DI void env_init(const EnvArgs& a)
     u32* out = a.status;  // [2 + NS]: goal, total, per-schema counts
     u32 total = 0;
     for_each_schema([&]<int S>() {
-        u32 c = 0;
-        Run<S, PI>::go(st, [&](const u32*) {
-            ++c;
-            return true;
-        });
+        const u32 c = Count<S, PI>::go(st);
         out[2 + S] = c;
         total += c;
     });
@@ -502,11 +493,7 @@ B2_DI void env_step(const EnvArgs& a)
         {
             bool found = false;
             with_schema(schema, [&]<int S>() {
-                u64 seen = 0;
-                Run<S, PI>::go(st, [&](const u32* b) {
-                    if (seen++ != r)
-                        return true;
-                    found = true;
+                found = Select<S, PI>::go(st, r, [&](const u32* b) {
                     if (a.schema)
                         a.schema[i] = static_cast<i32>(S);
                     if (a.binding)
@@ -521,7 +508,6 @@ B2_DI void env_step(const EnvArgs& a)
                             row[q] = x;  // provisional: an autoreset overwrites it (wide rows: reads stay ahead)
                         }
                     });
-                    return false;
                 });
             });
             if (!found)
@@ -536,11 +522,7 @@ B2_DI void env_step(const EnvArgs& a)
                 g = goal(nx);
                 c2 = 0;
                 for_each_schema([&]<int S>() {
-                    u32 cs = 0;
-                    Run<S, PI>::go(nx, [&](const u32*) {
-                        ++cs;
-                        return true;
-                    });
+                    const u32 cs = Count<S, PI>::go(nx);
                     newc[S] = cs;
                     c2 += cs;
                 });
@@ -607,12 +589,7 @@ B2_DI void expand_count(const ExpandArgs& a)
         const u32 s = static_cast<u32>(q - r * NS);
         const Row st = RowSel<WR>::load(a.states + r * W);
         u32 c = 0;
-        with_schema(s, [&]<int S>() {
-            Run<S, PI>::go(st, [&](const u32*) {
-                ++c;
-                return true;
-            });
-        });
+        with_schema(s, [&]<int S>() { c = Count<S, PI>::go(st); });
         a.counts[q] = c;
     }
 }

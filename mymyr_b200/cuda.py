@@ -148,18 +148,21 @@ class _Search:
         self.close()
 
 
-def brfs(task: Task, ctx: Context | None = None, witness_pruning: bool = True, canonical_order: bool = True,
+def brfs(task: Task, *, ctx: Context | None = None, witness_pruning: bool = True, canonical_order: bool = True,
          max_states: int | None = None, stop_at_goal: bool = True, fingerprint: bool = False,
          chunk_states: int | None = None, expected_states: int | None = None, max_depth: int | None = None,
          timings: bool = False, stream=None, comm=None, max_exchange_records: int | None = None) -> BrfsResult:
-    """The device BrFS (cuda::brfs). Ids, per-layer counts and the fingerprint equal the reference CPU BrFS with
-    deterministic ids. ``chunk_states`` is accepted for signature compatibility: layers are never chunked here, and
-    ids do not depend on it. ``comm`` (a ``mymyr_b200.dist.Communicator``) shards the search over its ranks by state
-    hash: every rank calls brfs together and gets the same result; each rank reads its own states with
-    ``BrfsResult.local``. ``max_exchange_records`` bounds the successor records a rank takes in per layer (a layer
-    that needs more raises ValueError on every rank, B2_CAPACITY)."""
-    if not canonical_order:
-        raise ValueError("mymyr_b200 brfs: canonical_order=False is not supported (ids are defined in canonical order)")
+    """The device BrFS (mymyr.cuda.brfs, python/src/cuda_bindings.cpp:2715-2771: the same keywords and defaults).
+    Ids, per-layer counts and the fingerprint equal the reference CPU BrFS with deterministic ids.
+    ``canonical_order=False`` leaves the successor order of a (state, schema) to the matcher in the reference; here
+    the search runs in canonical order, one of the orders it allows. ``chunk_states`` is accepted for signature
+    compatibility: layers are never chunked here, and ids do not depend on it. ``comm`` (a
+    ``mymyr_b200.dist.Communicator``) shards the search over its ranks by state hash: every rank calls brfs together
+    and gets the same result; each rank reads its own states with ``BrfsResult.local``. ``max_exchange_records``
+    bounds the successor records a rank takes in per layer (a layer that needs more raises CapacityError on every
+    rank, B2_CAPACITY)."""
+    if chunk_states is not None and int(chunk_states) < 1:
+        raise ValueError("mymyr_b200 brfs: chunk_states must be at least 1")
     if ctx is not None and task.ctx is not None and ctx.device != task.ctx.device:
         raise ValueError("mymyr_b200 brfs: the task lives on another device than ctx")
     o = _lib.BrfsOptions()
@@ -196,20 +199,22 @@ def brfs(task: Task, ctx: Context | None = None, witness_pruning: bool = True, c
 
 
 def hash_rows(states, *, numeric_words: int = 0, stream=None, ctx: Context | None = None):
-    """hash::state of each row of a CUDA uint64/int64 tensor [N, W] -> [N] (same dtype)."""
+    """hash::state of each row of a CUDA uint64/int64 tensor [N, W] -> [N] (same dtype). With ``numeric_words`` the
+    last numeric_words words of a row are its numeric words, which seed the hash of the (trimmed) atom words."""
     import torch
 
     from .task import default_context
 
-    if numeric_words:
-        raise ValueError("mymyr_b200 hash_rows: numeric words are not supported")
     if not states.is_cuda or states.dim() != 2 or states.element_size() != 8:
         raise ValueError("hash_rows: states must be a CUDA [N, W] tensor of 64-bit words")
+    if numeric_words < 0 or numeric_words > states.shape[1]:
+        raise ValueError("hash_rows: numeric_words must be between 0 and the row width")
     states = states.contiguous()
     ctx = ctx or default_context(states.device.index)
     out = torch.empty(states.shape[0], dtype=states.dtype, device=states.device)
     st = stream if stream is not None else torch.cuda.current_stream(states.device).cuda_stream
-    check(lib().b2_hash_rows(ctx.handle, states.data_ptr(), states.shape[0], states.shape[1], out.data_ptr(), st))
+    check(lib().b2_hash_rows_numeric(ctx.handle, states.data_ptr(), states.shape[0], states.shape[1],
+                                     int(numeric_words), out.data_ptr(), st))
     return out
 
 

@@ -37,10 +37,9 @@ class Expansion:
 
 def expand(task: Task, states: torch.Tensor, *, canonical_order: bool = True, witness_pruning: bool = False,
            hashes: bool = True, succ: bool = False, capacity: int | None = None, stream=None) -> Expansion:
-    """The successors of states [N, W] (CUDA, 64-bit words) in canonical order. ``capacity`` bounds the rows written
-    (None: a count pass sizes the outputs exactly)."""
-    if not canonical_order:
-        raise ValueError("mymyr_b200 expand: canonical_order=False is not supported")
+    """The successors of states [N, W] (CUDA, 64-bit words) in canonical order (also for ``canonical_order=False``,
+    which leaves the order to the matcher). ``capacity`` bounds the rows written (None: a count pass sizes the
+    outputs exactly)."""
     if not states.is_cuda or states.dim() != 2 or states.element_size() != 8:
         raise ValueError("expand: states must be a CUDA [N, W] tensor of 64-bit words")
     states = states.contiguous()
@@ -131,15 +130,26 @@ class BatchedEnv:
                                  _stream(self.device, stream)))
         return self.states
 
-    def step(self, action: torch.Tensor | None = None, stream=None):
+    def step(self, action: torch.Tensor | None = None, stream=None, next_task_ids: torch.Tensor | None = None):
         """One step of every environment: action [N] int64 indexes the canonical successor order (None: the random
         policy). Outputs land in this object's tensors (reward, terminated, truncated, count, final_states, schema,
-        binding, invalid, goal)."""
+        binding, invalid, goal). ``next_task_ids`` [N] int32 (device) names the task an autoresetting row restarts
+        in; the env has one task (id 0), and another id is reported by check_errors() (ValueError) while the row
+        keeps its task."""
         if action is not None and (action.dtype != torch.int64 or not action.is_cuda):
             raise ValueError("step: action must be a CUDA int64 tensor")
-        check(lib().b2_env_step(self._h, C.byref(self._batch), C.byref(self._out), _ptr(action),
-                                _stream(self.device, stream)))
+        if next_task_ids is not None and (next_task_ids.dtype != torch.int32 or not next_task_ids.is_cuda or
+                                          next_task_ids.numel() != self.num_envs):
+            raise ValueError("step: next_task_ids must be a CUDA int32 tensor of num_envs entries")
+        check(lib().b2_env_step_ex(self._h, C.byref(self._batch), C.byref(self._out), _ptr(action),
+                                   _ptr(next_task_ids), _stream(self.device, stream)))
         return self.states
+
+    def check_errors(self):
+        """Synchronizes the device and raises what the steps since the last check flagged: RuntimeError for a state
+        whose count cache did not match it (states written without reset()), ValueError for next_task_ids outside
+        the env's tasks (cuda::DeviceEnv::check_errors)."""
+        check(lib().b2_env_check_errors(self._h))
 
     def __del__(self):
         h = getattr(self, "_h", None)

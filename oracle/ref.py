@@ -42,6 +42,8 @@ def lib():
         L.ref_initial_state.argtypes = [P, P, C.c_uint32]
         L.ref_hash_state.restype = C.c_uint64
         L.ref_hash_state.argtypes = [P, C.c_uint32]
+        L.ref_hash_state_numeric.restype = C.c_uint64
+        L.ref_hash_state_numeric.argtypes = [P, C.c_uint32, C.c_uint32]
         L.ref_canonical_hash.restype = C.c_uint64
         L.ref_canonical_hash.argtypes = [P, P, C.c_uint32]
         L.ref_philox_bits64.restype = C.c_uint64
@@ -254,8 +256,10 @@ class RefEnv:
         return sec.value
 
 
-def hash_state(row: np.ndarray) -> int:
+def hash_state(row: np.ndarray, numeric_words: int = 0) -> int:
     row = np.ascontiguousarray(row, np.uint64)
+    if numeric_words:
+        return int(lib().ref_hash_state_numeric(row.ctypes.data, len(row), numeric_words))
     return int(lib().ref_hash_state(row.ctypes.data, len(row)))
 
 

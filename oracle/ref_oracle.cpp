@@ -12,6 +12,7 @@
 //   ref_brfs_limited   mymyr::brfs with max_states               include/mymyr/search/brfs.hpp:79
 //   ref_ground_stats   heuristics::ground (GroundingStats)      include/mymyr/heuristics/heuristic.hpp:165
 //   ref_hash_state     mymyr::hash::state                       include/mymyr/core/hash.hpp:58
+//   ref_hash_state_numeric  the same with numeric words          include/mymyr/core/hash.hpp:55-60
 //   ref_philox_bits64  mymyr::rl::rng::bits64                   include/mymyr/rl/rng.hpp:68
 // Errors are caught here and reported as a negative return code plus ref_last_error().
 
@@ -141,6 +142,11 @@ int64_t ref_is_goal(void* h, const uint64_t* row, uint32_t words)
 }
 
 uint64_t ref_hash_state(const uint64_t* row, uint32_t words) { return hash::state(row, words, nullptr, 0); }
+/// hash::state of a row [words - nnum atom words | nnum numeric words].
+uint64_t ref_hash_state_numeric(const uint64_t* row, uint32_t words, uint32_t nnum)
+{
+    return hash::state(row, words - nnum, row + (words - nnum), nnum);
+}
 
 uint64_t ref_canonical_hash(void* h, const uint64_t* row, uint32_t words)
 {

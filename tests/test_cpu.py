@@ -34,6 +34,37 @@ def test_library_exports_every_declared_symbol():
     assert b"sm_100a" in L.b2_version()
 
 
+def _reference_keywords(source: Path, name: str) -> list[tuple[str, str | None]]:
+    """The keyword arguments ("x"_a or "x"_a = default) of m.def("<name>", ...) in a nanobind source, in order."""
+    text = source.read_text()
+    seg = text[re.search(r'm\.def\(\s*"' + name + r'",', text).end():]
+    seg = seg[re.search(r'"[a-z_]+"_a', seg).start():]
+    seg = seg[: seg.index('");')]
+    return [(k, v.strip() if v else None) for k, v in re.findall(r'"([a-z_]+)"_a(?:\s*=\s*([^,)]+))?', seg)]
+
+
+def test_brfs_keywords_match_the_reference_binding():
+    """cuda.brfs takes the keywords of the reference's mymyr.cuda.brfs with its defaults (extra keywords follow)."""
+    import inspect
+
+    src = REF_TASKS.parents[2] / "python" / "src" / "cuda_bindings.cpp"
+    if not src.exists():
+        pytest.skip("reference checkout absent")
+    from mymyr_b200 import cuda as b2cuda
+
+    ref_kw = _reference_keywords(src, "brfs")
+    assert [k for k, _ in ref_kw][:3] == ["task", "ctx", "witness_pruning"]
+    sig = inspect.signature(b2cuda.brfs).parameters
+    ours = list(sig)
+    assert ours[: len(ref_kw)] == [k for k, _ in ref_kw]
+    convert = {"true": True, "false": False, "nb::none(": None}  # the default up to its first comma or ")"
+    for k, d in ref_kw:
+        if d is not None:
+            assert sig[k].default == convert[d], (k, d, sig[k].default)
+        if k != "task":
+            assert sig[k].kind is inspect.Parameter.KEYWORD_ONLY, k
+
+
 def test_errors_cross_the_abi_as_status_codes():
     with pytest.raises(RuntimeError, match="task text"):
         Task.from_text("O 2\nP 1\nF 1 p\nSI 0\nFI 1\n0 5\n", host_only=True)  # object out of range

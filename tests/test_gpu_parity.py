@@ -58,6 +58,19 @@ def test_hash_rows_match_reference(ref):
         assert np.array_equal(got, want)
 
 
+def test_hash_rows_numeric_words_match_reference(ref):
+    # rows [atom words | numeric words]: the numeric words seed the hash of the trimmed atom words
+    for W, nnum in ((2, 1), (3, 1), (4, 2), (7, 3), (5, 5)):
+        rows = np.random.default_rng(W * 10 + nnum).integers(0, 2**63, (129, W), dtype=np.int64).view(np.uint64)
+        rows[::3, : W - nnum][:, (W - nnum) // 2:] = 0  # trimmed atom widths
+        rows[4, W - nnum:] = 0  # zero numeric words still seed
+        got = as_u64(b2cuda.hash_rows(to_dev(rows), numeric_words=nnum))
+        want = np.array([ref.hash_state(r, nnum) for r in rows], np.uint64)
+        assert np.array_equal(got, want)
+        assert np.array_equal(as_u64(b2cuda.hash_rows(to_dev(rows), numeric_words=0)),
+                              np.array([ref.hash_state(r) for r in rows], np.uint64))
+
+
 # ------------------------------------------------------------------------------------------------ BrFS
 
 BRFS_CASES = [
@@ -318,6 +331,34 @@ def test_env_given_actions_match_reference(ref, matcher):
         _compare_env(env, renv)
         assert np.array_equal(env.invalid.cpu().numpy(), renv.invalid)
         assert np.array_equal(env.reward.cpu().numpy(), renv.reward)
+
+
+def test_env_next_task_ids(ref):
+    """next_task_ids of a one-task env: ids of 0 change nothing; another id is reported once by check_errors
+    (ValueError) and the rows keep their task, so the trajectories still equal the reference's."""
+    text = tasks.transport(2, 4, 2, 3)
+    rt = ref.RefTask(text)
+    t = Task.from_text(text)
+    n = 256
+    env = b2rl.BatchedEnv(t, n, seed=9, max_steps=7)
+    renv = ref.RefEnv(rt, n, seed=9, max_steps=7)
+    env.reset()
+    renv.reset()
+    zeros = torch.zeros(n, dtype=torch.int32, device="cuda")
+    bad = zeros.clone()
+    bad[17] = 3
+    for s in range(30):
+        env.step(next_task_ids=bad if s == 11 else zeros)
+        renv.step()
+        _compare_env(env, renv)
+        assert np.array_equal(env.reward.cpu().numpy(), renv.reward), s
+        if s == 11:
+            with pytest.raises(ValueError, match="next_task_ids"):
+                env.check_errors()
+        else:
+            env.check_errors()
+    with pytest.raises(ValueError):
+        env.step(next_task_ids=zeros[:5])
 
 
 def _step_digest(reward, terminated, truncated, goal, schema, count, binding):
