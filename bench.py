@@ -104,6 +104,42 @@ def check_golden(r, depth: int, fingerprint: bool) -> bool:
     return True
 
 
+def random_accesses(layer_counts):
+    """Random DRAM accesses of expansion + dedup per search: one hash-set probe per candidate and one stored-row
+    compare per duplicate (G + D over the layers); parent rows and new states' rows are streams, not counted."""
+    return sum(G + (G - N) for _E, G, N in layer_counts)
+
+
+# DRAM traffic of one depth-22 search's expansion + resolve + winners scan (one-GPU, compiled matcher), from the ncu
+# launch list of profiles/launches_bench_tile4x4_depth22.md (dram__bytes_read.sum + dram__bytes_write.sum, the
+# presized search's launches)
+TRAFFIC_DEPTH22 = 5_573e6
+
+
+def random_read_peak(device) -> float:
+    """Random 8-byte reads per second over a 1 GiB table (torch.take of 2^25 random indices, CUDA events, best of 5):
+    the denominator of the random-access roofline. Every such read costs a DRAM burst, so a random-access-bound
+    kernel is bounded by this rate, not by the streaming copy bandwidth."""
+    import torch
+
+    g = torch.Generator(device=device)
+    g.manual_seed(0)
+    table = torch.zeros(1 << 27, dtype=torch.int64, device=device)
+    idx = torch.randint(0, 1 << 27, (1 << 25,), device=device, generator=g)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    best = float("inf")
+    for rep in range(7):
+        a.record()
+        torch.take(table, idx)
+        b.record()
+        b.synchronize()
+        if rep >= 2:
+            best = min(best, a.elapsed_time(b))
+    del table, idx
+    torch.cuda.empty_cache()
+    return (1 << 25) / (best / 1000.0)
+
+
 def measured_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -633,6 +669,8 @@ def main():
     peak, peak_kind = measured_peaks()
     achieved = bytes_run / (kern_ms / 1000.0) / 1e9
     launches = sum(r.stats.kernel_launches for r in results)
+    rand_run = random_accesses(results[-1].layer_counts) / world
+    rand_peak = random_read_peak(device)
 
     phases = {"rehashes": results[-1].stats.rehashes,
               "count": statistics.mean(r.stats.count_ms for r in phased),
@@ -696,11 +734,21 @@ def main():
                                   f"the reference's at depth {depth} (tests/golden/tile4x4_brfs.json)") if checked
                                  else f"no golden values for depth {depth}"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None,
+                         "frac": achieved / peak,
+                         "traffic": TRAFFIC_DEPTH22 if world == 1 and depth == 22 else None,
+                         "traffic_source": ("ncu launch list of the depth-22 search (expansion + resolve + winners "
+                                            "scan), profiles/launches_bench_tile4x4_depth22.md")
+                                           if world == 1 and depth == 22 else "not captured for this depth",
                          "kernel": "b2j_brfs_expand + k_resolve + winners scan" if world == 1 else
                                    "b2j_dbrfs_expand + k_push + k_dinsert + id scan (per rank)",
                          "algorithmic_bytes_per_run": bytes_run, "kernel_ms_per_run": kern_ms,
-                         "peak_source": peak_kind},
+                         "peak_source": peak_kind,
+                         "random_access": {"achieved": rand_run / (kern_ms / 1000.0) / 1e9,
+                                           "peak": rand_peak / 1e9, "unit": "G accesses/s",
+                                           "frac": rand_run / (kern_ms / 1000.0) / rand_peak,
+                                           "accesses_per_run": rand_run,
+                                           "peak_source": "random 8-byte reads over a 1 GiB table (torch.take), "
+                                                          "measured in this run"}},
             "cpu_baseline": base,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches,

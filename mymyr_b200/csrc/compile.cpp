@@ -769,11 +769,29 @@ struct Compiler
         std::vector<std::vector<DFilter>> filt(order.size());
         std::vector<std::vector<u32>> chk(order.size());
         std::vector<u32> pre;
+        // a level's candidates: the parameter's static domain, less the objects that have no slot at some position of
+        // a positive fluent precondition (such an atom is never true); the layout still follows the static domains
+        std::vector<std::vector<u64>> cand = dom0[s];
+        for (const Lit& l : sc.pre)
+        {
+            if (!l.pos || T.kind[l.pred] != kFluent)
+                continue;
+            const u32 P0 = L.pos_begin[l.pred];
+            for (u32 i = 0; i < l.terms.size(); ++i)
+            {
+                if (l.terms[i] < 0)
+                    continue;
+                std::vector<u64>& c = cand[static_cast<u32>(l.terms[i])];
+                for (u32 o = 0; o < n; ++o)
+                    if (L.rs[static_cast<std::size_t>(P0 + i) * n + o] == kOutside)
+                        c[o >> 6] &= ~(u64{1} << (o & 63));
+            }
+        }
         for (u32 v = 0; v < sc.arity; ++v)
         {
             bool any = false;
             for (u32 w = 0; w < OW; ++w)
-                any |= dom0[s][v][w] != 0;
+                any |= cand[v][w] != 0;
             if (!any)
                 pg.never = 1;
         }
@@ -881,7 +899,7 @@ struct Compiler
             P.checks.insert(P.checks.end(), chk[d].begin(), chk[d].end());
             lv.chk_end = static_cast<u32>(P.checks.size());
             lv.dom0 = P.pool.size();
-            P.pool.insert(P.pool.end(), dom0[s][order[d]].begin(), dom0[s][order[d]].end());
+            P.pool.insert(P.pool.end(), cand[order[d]].begin(), cand[order[d]].end());
             P.levels.push_back(lv);
         }
         pg.pre_begin = static_cast<u32>(P.checks.size());

@@ -689,6 +689,8 @@ struct ExpandArgs
     i32* binding;
     u64* succ_hash;
     u32* status;
+    const u64* total;     // the call's successors (device), for the hash pass
+    u32 hash_pass;        // successor hashes and rows by a separate pass over the written records
 };
 }  // namespace dev
 }  // namespace b2

@@ -136,6 +136,7 @@ extern "C" b2_status b2_expand(b2_task* task, const uint64_t* states, uint64_t r
         B2_CUDA(cudaMemsetAsync(status, 0, 4, s));
         const u32 pi = witness_pruning ? 0 : 1;
         const unsigned grid = grid_for(nseg, 128, static_cast<unsigned>(ctx->sms) * 64);
+        const unsigned grid_rows = grid_for(rows, 128, static_cast<unsigned>(ctx->sms) * 64);  // compiled: a thread per state
         dev::ExpandArgs a{};
         a.states = states;
         a.rows = rows;
@@ -152,15 +153,20 @@ extern "C" b2_status b2_expand(b2_task* task, const uint64_t* states, uint64_t r
         a.binding = out->binding;
         a.succ_hash = out->succ_hash;
         a.status = status;
+        a.total = total;
+        // the compiled path hashes the successors in a pass of its own when the records it reads are written
+        a.hash_pass = task->jit && (out->succ_hash || out->succ) && out->parent && out->schema && out->binding ? 1 : 0;
         if (nseg && task->jit)
-            jit_launch(task->jit->get(kJitExpandCount, pi), grid, 128, &a, s);
+            jit_launch(task->jit->get(kJitExpandCount, pi), grid_rows, 128, &a, s);
         else if (nseg)
             dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
                 k_expand_count<OW, WR><<<grid, 128, 0, s>>>(task->dev, states, rows, words, pi, counts);
             });
         device_scan(SegCountIn{counts}, SegCountOut{seg_off}, nseg, total, sums, s, status);
         if (nseg && task->jit)
-            jit_launch(task->jit->get(kJitExpandWrite, pi), grid, 128, &a, s);
+            jit_launch(task->jit->get(kJitExpandWrite, pi), grid_rows, 128, &a, s);
+        if (nseg && a.hash_pass)
+            jit_launch(task->jit->get(kJitExpandHash, pi), static_cast<unsigned>(ctx->sms) * 16, 128, &a, s);
         else if (nseg)
             dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
                 k_expand_write<OW, WR><<<grid, 128, 0, s>>>(task->dev, states, rows, words, pi, seg_off, *out, status);
@@ -284,6 +290,7 @@ extern "C" b2_status b2_expand_noalloc(b2_task* task, const uint64_t* states, ui
         B2_CUDA(cudaMemsetAsync(total, 0, 16, s));
         const u32 pi = witness_pruning ? 0 : 1;
         const unsigned grid = grid_for(nseg, 128, static_cast<unsigned>(ctx->sms) * 64);
+        const unsigned grid_rows = grid_for(rows, 128, static_cast<unsigned>(ctx->sms) * 64);  // compiled: a thread per state
         dev::ExpandArgs a{};
         a.states = states;
         a.rows = rows;
@@ -300,8 +307,11 @@ extern "C" b2_status b2_expand_noalloc(b2_task* task, const uint64_t* states, ui
         a.binding = out->binding;
         a.succ_hash = out->succ_hash;
         a.status = status;
+        a.total = total;
+        // the compiled path hashes the successors in a pass of its own when the records it reads are written
+        a.hash_pass = task->jit && (out->succ_hash || out->succ) && out->parent && out->schema && out->binding ? 1 : 0;
         if (nseg && task->jit)
-            jit_launch(task->jit->get(kJitExpandCount, pi), grid, 128, &a, s);
+            jit_launch(task->jit->get(kJitExpandCount, pi), grid_rows, 128, &a, s);
         else if (nseg)
             dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
                 k_expand_count<OW, WR><<<grid, 128, 0, s>>>(task->dev, states, rows, words, pi, counts);
@@ -309,7 +319,9 @@ extern "C" b2_status b2_expand_noalloc(b2_task* task, const uint64_t* states, ui
         if (nseg)
             device_scan(SegCountIn{counts}, SegCountOut{seg_off}, nseg, total, sums, s, status);
         if (nseg && task->jit)
-            jit_launch(task->jit->get(kJitExpandWrite, pi), grid, 128, &a, s);
+            jit_launch(task->jit->get(kJitExpandWrite, pi), grid_rows, 128, &a, s);
+        if (nseg && a.hash_pass)
+            jit_launch(task->jit->get(kJitExpandHash, pi), static_cast<unsigned>(ctx->sms) * 16, 128, &a, s);
         else if (nseg)
             dispatch_shapes(P.ow, P.words, [&]<int OW, int WR>() {
                 k_expand_write<OW, WR><<<grid, 128, 0, s>>>(task->dev, states, rows, words, pi, seg_off, *out, status);

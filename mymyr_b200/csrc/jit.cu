@@ -122,7 +122,7 @@ cudaKernel_t kernel(cudaLibrary_t lib, const char* name)
 
 constexpr const char* kKernelNames[kJitKernels] = {"brfs_count", "brfs_expand", "dbrfs_expand", "dbrfs_count",
                                                    "dbrfs_push", "env_init",    "env_step",     "expand_count",
-                                                   "expand_write"};
+                                                   "expand_write", "expand_hash"};
 
 /// The cubin of kernel pair `which` (kJitKernels: all) of a source, compiled once per process.
 std::shared_ptr<std::vector<char>> cubin_of(const std::string& src, u64 key, u32 which, std::string* log_out)
@@ -186,7 +186,7 @@ std::shared_ptr<JitModule> jit_module(int device, const Program& prog)
     m->source = std::move(src);
     // the batched expand's kernels are compiled and loaded on the device now, not at their first launch, so that
     // b2_expand_noalloc's calls load nothing
-    for (JitKernel which : {kJitExpandCount, kJitExpandWrite})
+    for (JitKernel which : {kJitExpandCount, kJitExpandWrite, kJitExpandHash})
         for (u32 pi = 0; pi < 2; ++pi)
         {
             cudaFuncAttributes attr{};

@@ -26,6 +26,7 @@ enum JitKernel : u32
     kJitEnvStep,
     kJitExpandCount,
     kJitExpandWrite,
+    kJitExpandHash,
     kJitKernels
 };
 

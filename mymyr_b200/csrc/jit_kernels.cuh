@@ -579,32 +579,27 @@ B2_DI void env_step(const EnvArgs& a)
 }
 
 // ------------------------------------------------------------------------------------------------ batched expand
+// One thread per state, all schemas in order: the lanes of a warp run the same schema's matcher on 32 states at once
+// (a thread per (state, schema) segment made every warp step through all schemas' code, a divergence of NS ways).
 template<int PI>
 B2_DI void expand_count(const ExpandArgs& a)
 {
-    const u64 nseg = a.rows * NS;
-    for (u64 q = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; q < nseg; q += static_cast<u64>(gridDim.x) * blockDim.x)
+    for (u64 r = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; r < a.rows; r += static_cast<u64>(gridDim.x) * blockDim.x)
     {
-        const u64 r = q / NS;
-        const u32 s = static_cast<u32>(q - r * NS);
         const Row st = RowSel<WR>::load(a.states + r * W);
-        u32 c = 0;
-        with_schema(s, [&]<int S>() { c = Count<S, PI>::go(st); });
-        a.counts[q] = c;
+        u32* out = a.counts + r * NS;
+        for_each_schema([&]<int S>() { out[S] = Count<S, PI>::go(st); });
     }
 }
 
 template<int PI>
 B2_DI void expand_write(const ExpandArgs& a)
 {
-    const u64 nseg = a.rows * NS;
-    for (u64 q = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; q < nseg; q += static_cast<u64>(gridDim.x) * blockDim.x)
+    for (u64 r = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; r < a.rows; r += static_cast<u64>(gridDim.x) * blockDim.x)
     {
-        const u64 r = q / NS;
-        const u32 s = static_cast<u32>(q - r * NS);
         const Row st = RowSel<WR>::load(a.states + r * W);
-        u64 idx = a.seg_off[q];
-        with_schema(s, [&]<int S>() {
+        for_each_schema([&]<int S>() {
+            u64 idx = a.seg_off[r * NS + S];
             Run<S, PI>::go(st, [&](const u32* b) {
                 if (idx < a.capacity)
                 {
@@ -615,7 +610,7 @@ B2_DI void expand_write(const ExpandArgs& a)
                     if (a.binding)
                         for (u32 k = 0; k < a.label_width; ++k)
                             a.binding[idx * a.label_width + k] = k < ARITY[S] ? static_cast<i32>(b[k]) : -1;
-                    if (a.succ_hash || a.succ)
+                    if (!a.hash_pass && (a.succ_hash || a.succ))
                         with_successor<S>(st, b, [&](const auto& nx, u64 h) {
                             if (a.succ_hash)
                                 a.succ_hash[idx] = h;
@@ -626,6 +621,33 @@ B2_DI void expand_write(const ExpandArgs& a)
                 }
                 ++idx;
                 return true;
+            });
+        });
+    }
+}
+
+/// The successors' hashes and rows from the written records (parent, schema, binding), one thread per successor:
+/// the lanes of a warp hash 32 successors at once (in the writing pass only the few lanes whose matcher found a
+/// binding would hash, one successor at a time), and consecutive successors share their parent's row.
+template<int PI>
+B2_DI void expand_hash(const ExpandArgs& a)
+{
+    const u64 m = *a.total < a.capacity ? *a.total : a.capacity;
+    for (u64 idx = blockIdx.x * static_cast<u64>(blockDim.x) + threadIdx.x; idx < m; idx += static_cast<u64>(gridDim.x) * blockDim.x)
+    {
+        const u64 r = static_cast<u64>(a.parent[idx]);
+        const u32 s = static_cast<u32>(a.schema[idx]);
+        u32 b[NLW];
+        for (u32 k = 0; k < NLW; ++k)
+            b[k] = k < a.label_width ? static_cast<u32>(a.binding[idx * a.label_width + k]) : 0u;
+        const Row st = RowSel<WR>::load(a.states + r * W);
+        with_schema(s, [&]<int S>() {
+            with_successor<S>(st, b, [&](const auto& nx, u64 h) {
+                if (a.succ_hash)
+                    a.succ_hash[idx] = h;
+                if (a.succ)
+                    for (u32 w = 0; w < a.out_words; ++w)
+                        a.succ[idx * a.out_words + w] = w < W ? nx.word(w) : 0;
             });
         });
     }
@@ -669,4 +691,8 @@ extern "C" __global__ void __launch_bounds__(128) b2j_expand_count_nw(b2::dev::E
 #if defined(B2J_ALL) || defined(B2J_K8)
 extern "C" __global__ void __launch_bounds__(128) b2j_expand_write_w(b2::dev::ExpandArgs a) { b2::gen::expand_write<0>(a); }
 extern "C" __global__ void __launch_bounds__(128) b2j_expand_write_nw(b2::dev::ExpandArgs a) { b2::gen::expand_write<1>(a); }
+#endif
+#if defined(B2J_ALL) || defined(B2J_K9)
+extern "C" __global__ void __launch_bounds__(128) b2j_expand_hash_w(b2::dev::ExpandArgs a) { b2::gen::expand_hash<0>(a); }
+extern "C" __global__ void __launch_bounds__(128) b2j_expand_hash_nw(b2::dev::ExpandArgs a) { b2::gen::expand_hash<1>(a); }
 #endif
