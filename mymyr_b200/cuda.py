@@ -180,6 +180,7 @@ def brfs(task: Task, *, ctx: Context | None = None, witness_pruning: bool = True
     if stream is not None:
         o.stream = stream
     if comm is not None:
+        comm.check()  # a rank that left: fail here, before any launch
         o.comm = comm.handle
         o.world_rank, o.world_size = comm.rank, comm.world
     if max_exchange_records is not None:
@@ -347,6 +348,7 @@ def astar(task: Task, ctx: Context | None = None, heuristic="max", *, witness_pr
     if chunk_candidates is not None:
         o.chunk_candidates = int(chunk_candidates)
     if comm is not None:
+        comm.check()
         o.comm = comm.handle
     if isinstance(heuristic, Heuristic):
         o.heuristic = heuristic.handle

@@ -40,11 +40,50 @@ def broadcast_comm_id(group=None) -> bytes:
     return obj[0]
 
 
+class RankLeft(RuntimeError):
+    """A rank of the communicator has left it: a search over it is not started."""
+
+
+class Membership:
+    """Which ranks are still in a communicator, kept in a torch.distributed Store under `key`: a rank that leaves
+    says so (leave()), and every rank checks before a search's first launch (check(): one store round trip), so that
+    the others fail on the host, with no kernel or collective in flight, instead of waiting in a collective for a
+    rank that is gone. A rank that dies without leaving is caught by the communicator's timeout instead."""
+
+    def __init__(self, store, key: str, rank: int):
+        self.store, self.key, self.rank = store, key, rank
+        self.left = False
+
+    def leave(self) -> None:
+        if not self.left:
+            self.left = True
+            self.store.set(f"{self.key}/left/{self.rank}", b"1")
+            self.store.add(f"{self.key}/left", 1)
+
+    def check(self) -> None:
+        n = int(self.store.add(f"{self.key}/left", 0))
+        if n:
+            raise RankLeft(f"mymyr_b200: {n} rank(s) left the communicator ({self.key}); the search is not started")
+
+
+def default_store():
+    """The default process group's store (None when torch.distributed keeps none)."""
+    try:
+        from torch.distributed import distributed_c10d
+
+        return distributed_c10d._get_default_store()
+    except Exception:
+        return None
+
+
 class Communicator:
     """The device library's communicator over the ranks of a torch.distributed group (collective to create).
-    ``timeout_s``: how long a rank waits for the others in a collective before it fails the search (default 600)."""
+    ``timeout_s``: how long a rank waits for the others in a collective before it fails the search (default 600).
+    ``store``: where the ranks record that they left (default: the default process group's store); a search over a
+    communicator that a rank has left raises RankLeft on the other ranks before it launches anything."""
 
-    def __init__(self, ctx: Context, group=None, comm_id: bytes | None = None, timeout_s: float | None = None):
+    def __init__(self, ctx: Context, group=None, comm_id: bytes | None = None, timeout_s: float | None = None,
+                 store=None):
         import torch.distributed as tdist
 
         self.ctx = ctx
@@ -55,6 +94,8 @@ class Communicator:
             raise ValueError("Communicator: an NCCL id has 128 bytes")
         cid = _lib.CommId()
         C.memmove(C.addressof(cid), cid_bytes, len(cid_bytes))
+        store = store if store is not None else default_store()
+        self.members = Membership(store, "b2comm/" + cid_bytes[:16].hex(), self.rank) if store is not None else None
         h = C.c_void_p()
         check(lib().b2_comm_create(ctx.handle, C.byref(cid), self.rank, self.world, C.byref(h)))
         self._h = h
@@ -65,9 +106,23 @@ class Communicator:
     def handle(self) -> C.c_void_p:
         return self._h
 
+    def check(self) -> None:
+        """Raises RankLeft if a rank has left the communicator (every search over it calls this first)."""
+        if self._h is None:
+            raise RankLeft("mymyr_b200: this rank's communicator is closed")
+        if self.members is not None:
+            self.members.check()
+
     def close(self) -> None:
+        """Leaves the communicator: the other ranks' next search over it raises RankLeft before it launches."""
         h = getattr(self, "_h", None)
         if h is not None and h.value and _lib._lib is not None:
+            members = getattr(self, "members", None)
+            if members is not None:
+                try:
+                    members.leave()
+                except Exception:  # the store may be gone at interpreter exit
+                    pass
             _lib._lib.b2_comm_destroy(h)
         self._h = None
 

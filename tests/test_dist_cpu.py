@@ -194,6 +194,41 @@ def test_comm_id_broadcast_gloo():
     assert len(out[0]) == 128 and out[0] == out[1]
 
 
+def _membership_worker(rank, world, port, out):
+    _init(rank, world, port)
+    try:
+        store = bdist.default_store()
+        m = bdist.Membership(store, "b2comm/test", rank)
+        m.check()  # everyone is in
+        td.barrier()
+        if rank == world - 1:
+            m.leave()  # between searches: nothing of this rank is in flight
+            m.leave()  # leaving twice counts once
+            store.set("left-done", b"1")
+            out[rank] = "left"
+        else:
+            store.wait(["left-done"])
+            try:
+                m.check()
+                out[rank] = "not detected"
+            except bdist.RankLeft as e:
+                out[rank] = str(e)
+        td.barrier()
+    finally:
+        td.destroy_process_group()
+
+
+def test_rank_that_leaves_between_searches_is_detected_before_launch():
+    """A rank that leaves the communicator between searches (Communicator.close) is seen by the others on the host,
+    through the process group's store, before their next search launches anything: the search raises RankLeft."""
+    mgr = mp.get_context("spawn").Manager()
+    out = mgr.dict()
+    mp.start_processes(_membership_worker, args=(3, _free_port(), out), nprocs=3, join=True, start_method="spawn")
+    assert out[2] == "left"
+    for r in (0, 1):
+        assert "1 rank(s) left" in out[r], out[r]
+
+
 class _FakeResult:
     def __init__(self, shard):
         self.shard = shard

@@ -299,3 +299,55 @@ def test_sharded_brfs_receive_buffer_overflow_fails_every_rank(ref, world, match
         assert "receive buffer" in out[("small", r)]
         states, fp, lc = out[("full", r)]
         assert (states, fp, lc) == (exp["states"], exp["fingerprint"], exp["layer_counts"])
+
+
+def _leave_worker(rank, world, port, out):
+    import torch.distributed as td
+
+    from mymyr_b200 import Context, Task, cuda
+    from mymyr_b200 import dist as bdist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"  # no NVLink multicast object outlives a rank that leaves
+    torch.cuda.set_device(rank)
+    td.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                          timeout=datetime.timedelta(seconds=60))
+    try:
+        ctx = Context(rank)
+        comm = bdist.Communicator(ctx, timeout_s=30)
+        store = bdist.default_store()
+        task = Task.from_text(tasks.sliding_tile(3, 3, 30, 0), ctx)
+        r = cuda.brfs(task, comm=comm, stop_at_goal=False)
+        out[("first", rank)] = r.states
+        r.close()
+        if rank == world - 1:
+            comm.close()  # leaves between searches: none of its kernels or collectives is in flight
+            store.set("b2-test-left", b"1")
+        else:
+            store.wait(["b2-test-left"])
+            try:
+                cuda.brfs(task, comm=comm, stop_at_goal=False)
+                out[("second", rank)] = "ran"
+            except bdist.RankLeft as e:
+                out[("second", rank)] = "left: " + str(e)
+            comm.close()
+        td.barrier()
+    finally:
+        td.destroy_process_group()
+
+
+def test_rank_leaving_between_searches_fails_the_others_on_the_host(ref):
+    """A rank that leaves the communicator between searches: the other ranks' next search raises RankLeft on the host
+    before it launches a kernel or a collective, so that no rank waits in a collective for a rank that is gone."""
+    world = 2
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+
+    mgr = mp.get_context("spawn").Manager()
+    out = mgr.dict()
+    mp.start_processes(_leave_worker, args=(world, _free_port(), out), nprocs=world, join=True, start_method="spawn")
+    exp = ref.RefTask(tasks.sliding_tile(3, 3, 30, 0)).brfs(stop_at_goal=False)
+    assert out[("first", 0)] == out[("first", 1)] == exp["states"]
+    assert out[("second", 0)].startswith("left: "), out[("second", 0)]
