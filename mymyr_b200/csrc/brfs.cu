@@ -677,7 +677,7 @@ void build_device_layers(b2_brfs& B, const std::vector<u64>& key, DevLayerState*
         a.S = S;
         a.pi = pi;
         a.dyn = d;
-        jit_launch(B.task->jit->get(kJitBrfsExpand, pi), sms * 10, 128, &a, c);
+        jit_launch(B.task->jit->get(kJitBrfsExpand, pi), sms * dev::kBrfsExpandBlocksPerSm, 128, &a, c);
     }
     k_resolve<<<sms * 8, 256, 0, c>>>(S, d);
     device_scan_dev(WinIn{S.claimed, S.lost}, WinOutDyn{B.state_g.as<u32>(), d}, &d->G, B.cap_flags,

@@ -336,6 +336,9 @@ constexpr u32 kStatusEffectOverflow = 2u;
 constexpr u32 kStatusCapacity = 4u;
 constexpr u32 kStatusTaskId = 8u;  // an env's next_task_ids named a task it does not have
 
+/// Resident blocks per SM of the compiled BrFS expansion (its launch bound, and the device-driven loop's grid).
+constexpr u32 kBrfsExpandBlocksPerSm = 8;
+
 // ------------------------------------------------------------------------------------------------ BrFS hash set
 constexpr u64 kEmpty = ~u64{0};
 

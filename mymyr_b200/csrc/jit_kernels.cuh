@@ -141,10 +141,10 @@ struct QEntry
     u64 g;
     u32 i, k;
 };
-/// Queue entries per warp: about 21 KB per 128-thread block (ten blocks per SM).
+/// Queue entries per warp: about 21 KB per 128-thread block (kBrfsExpandBlocksPerSm blocks per SM).
 constexpr u32 kQueue = W <= 4 ? 96u : W <= 6 ? 80u : 64u;
 /// Queued successors a lane inserts at once (their probes interleaved).
-constexpr int kInsertBatch = 2;
+constexpr int kInsertBatch = 4;
 
 /// The expansion with warp-cooperative inserts (rows in registers): each lane runs its parent's matcher and queues
 /// every successor (row, hash, candidate index) in shared memory; after the round all 32 lanes insert the queued
@@ -661,8 +661,8 @@ extern "C" __global__ void __launch_bounds__(128) b2j_brfs_count_w(b2::dev::Brfs
 extern "C" __global__ void __launch_bounds__(128) b2j_brfs_count_nw(b2::dev::BrfsArgs a) { b2::gen::brfs_count<1>(a); }
 #endif
 #if defined(B2J_ALL) || defined(B2J_K1)
-extern "C" __global__ void __launch_bounds__(128, 10) b2j_brfs_expand_w(b2::dev::BrfsArgs a) { b2::gen::brfs_expand<0>(a); }
-extern "C" __global__ void __launch_bounds__(128, 10) b2j_brfs_expand_nw(b2::dev::BrfsArgs a) { b2::gen::brfs_expand<1>(a); }
+extern "C" __global__ void __launch_bounds__(128, b2::dev::kBrfsExpandBlocksPerSm) b2j_brfs_expand_w(b2::dev::BrfsArgs a) { b2::gen::brfs_expand<0>(a); }
+extern "C" __global__ void __launch_bounds__(128, b2::dev::kBrfsExpandBlocksPerSm) b2j_brfs_expand_nw(b2::dev::BrfsArgs a) { b2::gen::brfs_expand<1>(a); }
 #endif
 #if defined(B2J_ALL) || defined(B2J_K2)
 extern "C" __global__ void __launch_bounds__(128) b2j_dbrfs_expand_w(b2::dev::DExpandArgs a) { b2::gen::dbrfs_expand<0>(a); }

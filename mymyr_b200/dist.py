@@ -113,16 +113,22 @@ class Communicator:
         if self.members is not None:
             self.members.check()
 
+    def leave(self) -> None:
+        """Announces between searches that this rank takes part in no further search: the other ranks' next search
+        over the communicator raises RankLeft before it launches anything. Not collective; close() still is."""
+        members = getattr(self, "members", None)
+        if members is not None:
+            try:
+                members.leave()
+            except Exception:  # the store may be gone at interpreter exit
+                pass
+
     def close(self) -> None:
-        """Leaves the communicator: the other ranks' next search over it raises RankLeft before it launches."""
+        """Leaves the communicator and releases it. Collective: every rank closes it (NCCL's communicator teardown
+        waits for the other ranks), after any search over it has ended on every rank."""
         h = getattr(self, "_h", None)
         if h is not None and h.value and _lib._lib is not None:
-            members = getattr(self, "members", None)
-            if members is not None:
-                try:
-                    members.leave()
-                except Exception:  # the store may be gone at interpreter exit
-                    pass
+            self.leave()
             _lib._lib.b2_comm_destroy(h)
         self._h = None
 

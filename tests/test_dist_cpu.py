@@ -219,7 +219,7 @@ def _membership_worker(rank, world, port, out):
 
 
 def test_rank_that_leaves_between_searches_is_detected_before_launch():
-    """A rank that leaves the communicator between searches (Communicator.close) is seen by the others on the host,
+    """A rank that leaves the communicator between searches (Communicator.leave) is seen by the others on the host,
     through the process group's store, before their next search launches anything: the search raises RankLeft."""
     mgr = mp.get_context("spawn").Manager()
     out = mgr.dict()

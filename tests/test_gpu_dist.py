@@ -322,7 +322,7 @@ def _leave_worker(rank, world, port, out):
         out[("first", rank)] = r.states
         r.close()
         if rank == world - 1:
-            comm.close()  # leaves between searches: none of its kernels or collectives is in flight
+            comm.leave()  # between searches: none of its kernels or collectives is in flight
             store.set("b2-test-left", b"1")
         else:
             store.wait(["b2-test-left"])
@@ -331,7 +331,9 @@ def _leave_worker(rank, world, port, out):
                 out[("second", rank)] = "ran"
             except bdist.RankLeft as e:
                 out[("second", rank)] = "left: " + str(e)
-            comm.close()
+            store.set("b2-test-checked", b"1")
+        store.wait(["b2-test-checked"])
+        comm.close()  # the communicator's teardown is collective: every rank, after the check
         td.barrier()
     finally:
         td.destroy_process_group()
