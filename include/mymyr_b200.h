@@ -225,6 +225,10 @@ typedef struct b2_brfs_options {
     uint64_t max_exchange_records; /* multi-GPU: the most successor records a rank takes in per layer (0: as many
                                     * as the layer needs; the receive buffers grow to them). A layer that needs more
                                     * fails on every rank with B2_CAPACITY: records past a buffer are never written */
+    uint64_t shard_from_states;    /* multi-GPU: every rank runs the layers alone, the same search with no exchange,
+                                    * until a layer's frontier holds at least this many states; the ranks then keep
+                                    * the states they own and shard the rest of the search (0: 2^20; 1: shard from
+                                    * the root). The result does not depend on it */
 } b2_brfs_options;
 
 void b2_brfs_options_default(b2_brfs_options* o);

@@ -75,7 +75,8 @@ class BrfsOptions(C.Structure):
     _fields_ = [("witness_pruning", C.c_int32), ("stop_at_goal", C.c_int32), ("fingerprint", C.c_int32),
                 ("max_depth", C.c_uint32), ("max_states", C.c_uint64), ("expected_states", C.c_uint64),
                 ("timings", C.c_int32), ("world_rank", C.c_int32), ("world_size", C.c_int32),
-                ("stream", C.c_void_p), ("comm", C.c_void_p), ("max_exchange_records", C.c_uint64)]
+                ("stream", C.c_void_p), ("comm", C.c_void_p), ("max_exchange_records", C.c_uint64),
+                ("shard_from_states", C.c_uint64)]
 
 
 class BrfsResult(C.Structure):

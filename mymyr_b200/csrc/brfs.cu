@@ -690,7 +690,10 @@ void build_device_layers(b2_brfs& B, const std::vector<u64>& key, DevLayerState*
     B.graph_key = key;
 }
 
-void run_search(b2_brfs& B, b2_brfs_result& R)
+/// The one-GPU search. With prefix_states, it stops after the first layer whose new states number at least
+/// prefix_states, before expanding them, and returns true (the search goes on elsewhere: a sharded search takes over
+/// from there); such a search runs in the host loop. Otherwise, and when it ends before that layer, it returns false.
+bool run_search(b2_brfs& B, b2_brfs_result& R, u64 prefix_states = 0)
 {
     const auto t0 = std::chrono::steady_clock::now();
     const Program& P = B.task->prog;
@@ -718,8 +721,9 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
     {
         R.status = B2_SEARCH_UNSOLVABLE;
         B.n_states = 1;
-        return;
+        return false;
     }
+    bool cut = false;
     // root
     cache_take(B);
     if (B.table_slots)  // kept from an earlier search: emptied (a table grown below is emptied on allocation)
@@ -792,7 +796,7 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
     bool finished = false;
     // With the buffers presized (expected_states), no per-layer events and no max_states cut, the layers run as one
     // graph launch on the device; a layer that outgrows the buffers continues in the host loop below.
-    if (B.task->jit && !o.timings && o.max_states == ~u64{0} && o.expected_states > 0)
+    if (B.task->jit && !o.timings && o.max_states == ~u64{0} && o.expected_states > 0 && !prefix_states)
     {
         DevLayerState init{};
         init.layer_begin = 0;
@@ -986,9 +990,15 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
         B.layer_begin.push_back(layer_begin);
         if (stop)
             break;
+        if (prefix_states && layer_end - layer_begin >= prefix_states && layers < o.max_depth)
+        {
+            cut = true;  // the next layer is large enough to shard
+            break;
+        }
         if (counted)
             B.slot ^= 1;
     }
+    stream_wait(s);  // a next layer's count launched before the cut has finished with the buffers
     B.layer_begin.push_back(B.n_states);
     if (o.fingerprint)
     {
@@ -1028,8 +1038,11 @@ void run_search(b2_brfs& B, b2_brfs_result& R)
             for (int k = 0; k < 3; ++k)
                 R.layer_counts[3 * i + k] = counts[i][k];
     R.search_s = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    return cut;
 }
 }  // namespace
+
+bool run_prefix(b2_brfs& B, b2_brfs_result& R, u64 prefix_states) { return run_search(B, R, prefix_states); }
 
 extern "C" {
 
@@ -1231,7 +1244,7 @@ void b2_brfs_destroy(b2_brfs* search)
         shard_free(*search);
     if (search->stream)
     {
-        if (!search->shard && search->ran)
+        if (search->ran && (!search->shard || search->from_cache))
         {
             // an idle search's buffers (and layer-loop graph) are kept by the context for its next search
             stream_drain(search->stream);

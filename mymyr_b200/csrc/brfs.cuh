@@ -385,6 +385,9 @@ namespace b2
 {
 /// The sharded search (dbrfs.cu): run, the rank's states, release.
 void shard_run(b2_brfs& B, b2_brfs_result& R);
+/// The one-GPU search of B up to the first layer whose frontier holds at least prefix_states states (brfs.cu): true
+/// when it stopped there, false when the search ended before (R is then its whole result).
+bool run_prefix(b2_brfs& B, b2_brfs_result& R, u64 prefix_states);
 u64 shard_local_count(const b2_brfs& B);
 void shard_local(b2_brfs& B, u64 first, u64 count, u64* ids, u64* rows, u32 words, u64* hashes, u32* parent,
                  u32* index);

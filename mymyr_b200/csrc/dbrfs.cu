@@ -69,6 +69,67 @@ __global__ void k_dseed(u64* __restrict__ rows, u64* __restrict__ hash, u32 W, u
     misc->new_packed = 1 | (u64{1} << 32);
 }
 
+/// The states a rank owns among those of a one-GPU search that every rank ran alone (the replicated small layers):
+/// scanned over the state ids, in id order, so that local index l of the rank's states is the exclusive count of
+/// owned ids before it.
+struct OwnIn
+{
+    const u32* state_g;  // id -> candidate index of the one-GPU store
+    const u64* hash;     // per candidate
+    u32 me, world;
+    __device__ __forceinline__ u32 operator()(u64 id) const { return owner_of(hash[state_g[id]], world) == me ? 1u : 0u; }
+};
+/// Copies an owned state into the rank's arena and state lists (arena index = local index) and records the local
+/// index of the frontier's first id.
+struct OwnOut
+{
+    const u32* state_g;
+    const u64* rows;  // one-GPU rows, hashes and node records (parent index in its layer, successor index)
+    const u64* hash;
+    const u32* par;
+    const u32* kid;
+    const u64* layer_begin;  // the one-GPU search's layer starts, nlayers of them
+    u32 nlayers;
+    u32 W;
+    u64 frontier_begin;  // id of the frontier's first state
+    u64* rows_out;
+    u64* hash_out;
+    u32* state_lc;
+    u32* state_id;
+    u32* state_par;
+    u32* state_kid;
+    u64* frontier_local;  // out: the local index of the frontier's first state
+    __device__ __forceinline__ void operator()(u64 id, u64 l, u32 own) const
+    {
+        if (id == frontier_begin)
+            *frontier_local = l;
+        if (!own)
+            return;
+        const u64 g = state_g[id];
+        for (u32 q = 0; q < W; ++q)
+            rows_out[l * W + q] = rows[g * W + q];
+        hash_out[l] = hash[g];
+        state_lc[l] = static_cast<u32>(l);
+        state_id[l] = static_cast<u32>(id);
+        state_kid[l] = id == 0 ? 0u : kid[g];
+        if (id == 0)
+        {
+            state_par[l] = 0xFFFFFFFFu;
+            return;
+        }
+        u32 lo = 0, hi = nlayers;  // layer L of id: layer_begin[L] <= id < layer_begin[L + 1]
+        while (hi - lo > 1)
+        {
+            const u32 mid = (lo + hi) / 2;
+            if (layer_begin[mid] <= id)
+                lo = mid;
+            else
+                hi = mid;
+        }
+        state_par[l] = static_cast<u32>(layer_begin[lo - 1] + par[g]);
+    }
+};
+
 /// The local successor counts into the layer-wide lane array (by parent id: bytes for lane 1, words for lane 4), then
 /// after the lanes: the rank's goal parents, its parents whose count does not fit a byte lane (saturated, counted), and
 /// its row of the per-owner successor counts M[rank][owner]; and the rank's first goal id. A parent's lane and a rank's
@@ -392,6 +453,10 @@ namespace
 {
 u64 grown(u64 need, u64 cap) { return std::max<u64>(need, cap + cap / 2); }
 
+/// The frontier from which a sharded search exchanges (b2_brfs_options::shard_from_states 0): below it a sharded
+/// layer's fixed cost (its collectives, one host wait, some twenty launches) exceeds what splitting its work saves.
+constexpr u64 kShardFromStates = u64{1} << 20;
+
 void ensure_scan(ShardState& S, u64 n, cudaStream_t s)
 {
     if (S.sums.bytes < scan_scratch_bytes(n))
@@ -572,32 +637,124 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
     if (comm->cursors.bytes)  // a search that ended early may have left it advanced; no rank pushes before the
         B2_CUDA(cudaMemsetAsync(comm->cursors.local.p, 0, 8, s));  // first layer's collectives
     ensure_table(S, expect, S.misc_at(0), s, B.launches);
-    // the root: arena index 0 on every rank, stored by its owner
-    B2_CUDA(cudaMemcpyAsync(S.rows.p, P.initial.data(), W * 8, cudaMemcpyHostToDevice, s));
-    k_dseed<<<1, 1, 0, s>>>(S.rows.as<u64>(), S.hash.as<u64>(), W, S.table.as<u64>(), S.table_slots - 1,
-                            max_probe(S.table_slots), me, world, S.state_lc.as<u32>(), S.state_id.as<u32>(),
-                            S.state_par.as<u32>(), S.state_kid.as<u32>(), S.misc_at(0));
-    B2_CUDA(cudaGetLastError());
-    ++B.launches;
-    S.n_local = read_misc(S, comm, s).new_packed >> 32;
-    S.cand_next = 1;
-    S.n_total = 1;
-    B.n_states = 1;
-    if (o.stop_at_goal && P.goal_unsat)
-    {
-        R.status = B2_SEARCH_UNSOLVABLE;
-        S.layer_begin = {0, 1};
-        return;
-    }
-    u64 layer_begin = 0, layer_end = 1, lb_local = 0, le_local = S.n_local;
-    S.layer_begin.assign(1, 0);
+    u64 layer_begin = 0, layer_end = 1, lb_local = 0, le_local = 0;
     u32 layers = 0;
     bool exhausted = false, solved = false, full = false;
+    bool finished = false;  // the replicated layers ended the search
     u64 expanded = 0, generated = 0, goals = 0, goal_id = 0;
     double count_ms = 0, gen_ms = 0, dedup_ms = 0, exchange_ms = 0;
+    std::vector<std::array<u64, 3>> counts;
+    const u64 shard_from = o.shard_from_states ? o.shard_from_states : kShardFromStates;
+    if (shard_from > 1)
+    {
+        // The small layers: every rank runs the same one-GPU search alone, with no exchange and no collective (its
+        // per-layer cost is far below a sharded layer's), up to the first frontier of shard_from states. Each rank
+        // then keeps the states it owns, in id order, with their node records, and the sharded loop goes on from
+        // that frontier. The ids, counts and fingerprint are the one-GPU search's either way.
+        const b2_brfs_options saved = B.opt;
+        B.opt.expected_states = 0;  // the host loop, its buffers grown as the layers need
+        B.opt.fingerprint = 0;
+        B.opt.timings = 0;
+        std::vector<u64> plc(3 * 4096);
+        b2_brfs_result PR{};
+        PR.layer_counts = plc.data();
+        PR.layer_capacity = 4096;
+        bool cut = false;
+        try
+        {
+            cut = run_prefix(B, PR, shard_from);
+        }
+        catch (...)
+        {
+            B.opt = saved;
+            throw;
+        }
+        B.opt = saved;
+        if (PR.status == B2_SEARCH_UNSOLVABLE)
+        {
+            R.status = B2_SEARCH_UNSOLVABLE;
+            S.layer_begin = {0, 1};
+            B.n_states = 1;
+            S.n_total = 1;
+            return;
+        }
+        const u64 n = B.n_states;
+        const std::vector<u64> lbv = B.layer_begin;  // [0, the layers' starts..., n]
+        const u64 frontier_begin = lbv.size() >= 2 ? lbv[lbv.size() - 2] : 0;
+        ensure_cand(S, W, n, s);
+        ensure_states(S, n, s);
+        ensure_scan(S, n, s);
+        DeviceBuffer lbd;
+        lbd.alloc(lbv.size() * 8);
+        B2_CUDA(cudaMemcpyAsync(lbd.p, lbv.data(), lbv.size() * 8, cudaMemcpyHostToDevice, s));
+        DistMisc* m0 = S.misc_at(0);
+        device_scan(OwnIn{B.state_g.as<u32>(), B.hash.as<u64>(), me, world},
+                    OwnOut{B.state_g.as<u32>(), B.rows.as<u64>(), B.hash.as<u64>(), B.par.as<u32>(), B.kid.as<u32>(),
+                           lbd.as<u64>(), static_cast<u32>(lbv.size()), W, frontier_begin, S.rows.as<u64>(),
+                           S.hash.as<u64>(), S.state_lc.as<u32>(), S.state_id.as<u32>(), S.state_par.as<u32>(),
+                           S.state_kid.as<u32>(), &m0->kept},
+                    n, &m0->total_local, S.sums.as<u64>(), s, &m0->lm.status);
+        B.launches += 3;
+        const DistMisc mp = read_misc(S, comm, s);
+        // the rank's states into its hash set (sized first, while it holds none)
+        ensure_table(S, std::max<u64>(expect, mp.total_local), m0, s, B.launches);
+        S.n_local = mp.total_local;
+        S.cand_next = S.n_local;
+        if (S.n_local)
+        {
+            k_rehash<<<grid_for(S.n_local, 256), 256, 0, s>>>(S.table.as<u64>(), S.table_slots - 1,
+                                                                max_probe(S.table_slots), S.state_lc.as<u32>(),
+                                                                S.n_local, S.hash.as<u64>(), &m0->lm.status);
+            B2_CUDA(cudaGetLastError());
+            ++B.launches;
+        }
+        read_misc(S, comm, s);  // the status of the inserts
+        S.n_total = n;
+        S.layer_begin.assign(lbv.begin(), lbv.end() - 1);
+        layers = PR.layers;
+        expanded = PR.expanded;
+        generated = PR.generated;
+        goals = PR.num_goal_states;
+        solved = PR.solved != 0;
+        goal_id = PR.goal_id;
+        for (u32 i = 0; i < PR.layers && i < PR.layer_capacity; ++i)
+            counts.push_back({plc[3 * i], plc[3 * i + 1], plc[3 * i + 2]});
+        layer_begin = frontier_begin;
+        layer_end = n;
+        lb_local = cut ? mp.kept : S.n_local;
+        le_local = S.n_local;
+        if (!cut)
+        {
+            finished = true;
+            exhausted = PR.exhausted != 0;
+            full = PR.status == B2_SEARCH_OUT_OF_STATES && !solved;
+        }
+        B2_CUDA(cudaMemsetAsync(S.misc.p, 0, 2 * sizeof(DistMisc), s));
+    }
+    else
+    {
+        // the root: arena index 0 on every rank, stored by its owner
+        B2_CUDA(cudaMemcpyAsync(S.rows.p, P.initial.data(), W * 8, cudaMemcpyHostToDevice, s));
+        k_dseed<<<1, 1, 0, s>>>(S.rows.as<u64>(), S.hash.as<u64>(), W, S.table.as<u64>(), S.table_slots - 1,
+                                max_probe(S.table_slots), me, world, S.state_lc.as<u32>(), S.state_id.as<u32>(),
+                                S.state_par.as<u32>(), S.state_kid.as<u32>(), S.misc_at(0));
+        B2_CUDA(cudaGetLastError());
+        ++B.launches;
+        S.n_local = read_misc(S, comm, s).new_packed >> 32;
+        S.cand_next = 1;
+        S.n_total = 1;
+        B.n_states = 1;
+        if (o.stop_at_goal && P.goal_unsat)
+        {
+            R.status = B2_SEARCH_UNSOLVABLE;
+            S.layer_begin = {0, 1};
+            return;
+        }
+        le_local = S.n_local;
+        S.layer_begin.assign(1, 0);
+    }
     S.lane = 1;
     S.owner_counts = world > 2;
-    std::vector<std::array<u64, 3>> counts;
     u64* fill = nullptr;  // this rank's receive-buffer cursor (mapped on the first exchange)
     // The count pass of a layer into counter slot `misc`: the local parents' successor counts and goals, their local
     // offsets (staging), and the layer's counts by parent id summed over the ranks and their offsets. The local
@@ -675,7 +832,7 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
     };
     bool counted = false;  // this layer's count ran with the previous layer; its counters are in `next`
     DistMisc next{};
-    for (;;)
+    while (!finished)
     {
         const u64 E = layer_end - layer_begin, El = le_local - lb_local;
         if (E == 0)

@@ -151,7 +151,8 @@ class _Search:
 def brfs(task: Task, *, ctx: Context | None = None, witness_pruning: bool = True, canonical_order: bool = True,
          max_states: int | None = None, stop_at_goal: bool = True, fingerprint: bool = False,
          chunk_states: int | None = None, expected_states: int | None = None, max_depth: int | None = None,
-         timings: bool = False, stream=None, comm=None, max_exchange_records: int | None = None) -> BrfsResult:
+         timings: bool = False, stream=None, comm=None, max_exchange_records: int | None = None,
+         shard_from_states: int | None = None) -> BrfsResult:
     """The device BrFS (mymyr.cuda.brfs, python/src/cuda_bindings.cpp:2715-2771: the same keywords and defaults).
     Ids, per-layer counts and the fingerprint equal the reference CPU BrFS with deterministic ids.
     ``canonical_order=False`` leaves the successor order of a (state, schema) to the matcher in the reference; here
@@ -160,7 +161,9 @@ def brfs(task: Task, *, ctx: Context | None = None, witness_pruning: bool = True
     ``mymyr_b200.dist.Communicator``) shards the search over its ranks by state hash: every rank calls brfs together
     and gets the same result; each rank reads its own states with ``BrfsResult.local``. ``max_exchange_records``
     bounds the successor records a rank takes in per layer (a layer that needs more raises CapacityError on every
-    rank, B2_CAPACITY)."""
+    rank, B2_CAPACITY). ``shard_from_states``: with ``comm``, every rank runs the layers alone (the same search, no
+    exchange) until a frontier holds this many states (default 2^20; 1: shard from the root); the result does not
+    depend on it."""
     if chunk_states is not None and int(chunk_states) < 1:
         raise ValueError("mymyr_b200 brfs: chunk_states must be at least 1")
     if ctx is not None and task.ctx is not None and ctx.device != task.ctx.device:
@@ -185,6 +188,8 @@ def brfs(task: Task, *, ctx: Context | None = None, witness_pruning: bool = True
         o.world_rank, o.world_size = comm.rank, comm.world
     if max_exchange_records is not None:
         o.max_exchange_records = int(max_exchange_records)
+    if shard_from_states is not None:
+        o.shard_from_states = int(shard_from_states)
     s = _Search(task, o)
     r = s.run()
     res = BrfsResult(status=STATUS.get(r.status, str(r.status)), states=r.states, expanded=r.expanded,

@@ -31,6 +31,11 @@ CASES = [
 ]
 
 
+# shard_from_states: 1 shards from the root (every layer exchanges), 64 runs the first layers on every rank alone and
+# shards from the first frontier of 64 states, 0 is the default (2^20: these small searches run replicated to the end)
+SHARD_FROM = (1, 64, 0)
+
+
 def _free_port() -> int:
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -53,16 +58,18 @@ def _worker(rank, world, port, matcher, out):
         comm = bdist.Communicator(ctx, timeout_s=60)
         for name, text, depth, witness, stop in CASES:
             task = Task.from_text(text, ctx, matcher=matcher)
-            r = cuda.brfs(task, comm=comm, max_depth=depth, stop_at_goal=stop, fingerprint=True,
-                          witness_pruning=witness)
-            g = bdist.gather_states(r)
-            if rank == 0:
-                out[name] = {"states": r.states, "expanded": r.expanded, "generated": r.generated,
-                             "layer_counts": r.layer_counts, "fingerprint": r.fingerprint, "solved": r.solved,
-                             "goal_id": r.goal_id, "num_goal_states": r.num_goal_states, "rows": g["rows"],
-                             "parent": g["parent"], "index": g["index"], "hashes": g["hashes"]}
-            out[(name, rank)] = (r.stats.local_states, r.stats.exchanged, r.states, r.fingerprint)
-            r.close()
+            for sf in SHARD_FROM:
+                r = cuda.brfs(task, comm=comm, max_depth=depth, stop_at_goal=stop, fingerprint=True,
+                              witness_pruning=witness, shard_from_states=sf)
+                g = bdist.gather_states(r)
+                if rank == 0:
+                    out[(name, sf)] = {"states": r.states, "expanded": r.expanded, "generated": r.generated,
+                                       "layer_counts": r.layer_counts, "fingerprint": r.fingerprint,
+                                       "solved": r.solved, "goal_id": r.goal_id,
+                                       "num_goal_states": r.num_goal_states, "rows": g["rows"],
+                                       "parent": g["parent"], "index": g["index"], "hashes": g["hashes"]}
+                out[(name, sf, rank)] = (r.stats.local_states, r.stats.exchanged, r.states, r.fingerprint)
+                r.close()
         comm.close()
         td.barrier()
     finally:
@@ -93,25 +100,26 @@ def test_sharded_brfs_matches_reference(ref, world, matcher):
 
     out = _run(world, matcher)
     for name, text, depth, witness, stop in CASES:
-        got = out[name]
         t = oref.RefTask(text)
         exp = t.brfs(max_depth=depth, stop_at_goal=stop, witness_pruning=witness, fingerprint=True)
-        assert got["states"] == exp["states"], name
-        assert got["layer_counts"] == exp["layer_counts"], name
-        assert got["fingerprint"] == exp["fingerprint"], name
-        assert bool(got["solved"]) == bool(exp["solved"]), name
-        assert got["num_goal_states"] == exp["num_goal_states"], name
-        per_rank = [out[(name, r)] for r in range(world)]
-        assert sum(p[0] for p in per_rank) == got["states"], name  # the shards partition the states
-        assert len({(p[2], p[3]) for p in per_rank}) == 1, name    # every rank reports the same result
-        if not stop:
-            rows, par, idx = t.brfs_states(max_depth=depth, witness_pruning=witness)
-            np.testing.assert_array_equal(got["rows"], rows, err_msg=name)
-            np.testing.assert_array_equal(got["parent"], par, err_msg=name)
-            np.testing.assert_array_equal(got["index"], idx, err_msg=name)
-            assert [int(h) for h in got["hashes"]] == [oref.hash_state(r) for r in rows], name
-            if world > 1:
-                assert sum(p[1] for p in per_rank) > 0, name  # successors crossed between ranks
+        rows, par, idx = t.brfs_states(max_depth=depth, witness_pruning=witness)
+        for sf in SHARD_FROM:
+            got, what = out[(name, sf)], (name, sf)
+            assert got["states"] == exp["states"], what
+            assert got["layer_counts"] == exp["layer_counts"], what
+            assert got["fingerprint"] == exp["fingerprint"], what
+            assert bool(got["solved"]) == bool(exp["solved"]), what
+            assert got["num_goal_states"] == exp["num_goal_states"], what
+            per_rank = [out[(name, sf, r)] for r in range(world)]
+            assert sum(p[0] for p in per_rank) == got["states"], what  # the shards partition the states
+            assert len({(p[2], p[3]) for p in per_rank}) == 1, what    # every rank reports the same result
+            if not stop:
+                np.testing.assert_array_equal(got["rows"], rows, err_msg=str(what))
+                np.testing.assert_array_equal(got["parent"], par, err_msg=str(what))
+                np.testing.assert_array_equal(got["index"], idx, err_msg=str(what))
+                assert [int(h) for h in got["hashes"]] == [oref.hash_state(r) for r in rows], what
+                if world > 1 and sf == 1:
+                    assert sum(p[1] for p in per_rank) > 0, what  # successors crossed between ranks
 
 
 MAX_STATES_CASES = [
@@ -138,17 +146,16 @@ def _max_states_worker(rank, world, port, limits, out):
         comm = bdist.Communicator(ctx, timeout_s=60)
         for name, text, depth in MAX_STATES_CASES:
             task = Task.from_text(text, ctx)
-            for stop in (False, True):
-                for M in limits[name]:
-                    r = cuda.brfs(task, comm=comm, max_states=M, max_depth=depth, stop_at_goal=stop,
-                                  fingerprint=True)
-                    g = bdist.gather_states(r)
-                    if rank == 0:
-                        out[(name, stop, M)] = {
-                            "got": (r.states, r.expanded, r.generated, r.num_goal_states, r.layers, r.layer_counts,
-                                    r.status, r.fingerprint),
-                            "rows": g["rows"], "parent": g["parent"], "index": g["index"]}
-                    r.close()
+            for stop, M, sf in [(st, m, sf) for st in (False, True) for m in limits[name] for sf in (1, 16, 0)]:
+                r = cuda.brfs(task, comm=comm, max_states=M, max_depth=depth, stop_at_goal=stop,
+                              fingerprint=True, shard_from_states=sf)
+                g = bdist.gather_states(r)
+                if rank == 0:
+                    out[(name, stop, M, sf)] = {
+                        "got": (r.states, r.expanded, r.generated, r.num_goal_states, r.layers, r.layer_counts,
+                                r.status, r.fingerprint),
+                        "rows": g["rows"], "parent": g["parent"], "index": g["index"]}
+                r.close()
         comm.close()
         td.barrier()
     finally:
@@ -181,12 +188,13 @@ def test_sharded_brfs_max_states_matches_reference(ref, world):
                 exp = rt.brfs_limited(M, max_depth=depth, stop_at_goal=stop, fingerprint=True)
                 want = (exp["states"], exp["expanded"], exp["generated"], exp["num_goal_states"], exp["layers"],
                         exp["layer_counts"], REF_STATUS[exp["status"]], exp["fingerprint"])
-                got = out[(name, stop, M)]
-                assert got["got"] == want, (name, stop, M, got["got"], want)
-                k = exp["states"]
-                np.testing.assert_array_equal(got["rows"], rows[:k], err_msg=f"{name} {M}")
-                np.testing.assert_array_equal(got["parent"], par[:k], err_msg=f"{name} {M}")
-                np.testing.assert_array_equal(got["index"], idx[:k], err_msg=f"{name} {M}")
+                for sf in (1, 16, 0):
+                    got = out[(name, stop, M, sf)]
+                    assert got["got"] == want, (name, stop, M, sf, got["got"], want)
+                    k = exp["states"]
+                    np.testing.assert_array_equal(got["rows"], rows[:k], err_msg=f"{name} {M} {sf}")
+                    np.testing.assert_array_equal(got["parent"], par[:k], err_msg=f"{name} {M} {sf}")
+                    np.testing.assert_array_equal(got["index"], idx[:k], err_msg=f"{name} {M} {sf}")
 
 
 ASTAR_CASES = [
@@ -265,7 +273,7 @@ def _overflow_worker(rank, world, port, matcher, out):
         comm = bdist.Communicator(ctx, timeout_s=60)
         task = Task.from_text(tasks.sliding_tile(3, 3, 30, 0), ctx, matcher=matcher)
         try:
-            cuda.brfs(task, comm=comm, stop_at_goal=False, max_exchange_records=40)
+            cuda.brfs(task, comm=comm, stop_at_goal=False, max_exchange_records=40, shard_from_states=1)
             out[("small", rank)] = "ran"
         except _lib.CapacityError as e:
             out[("small", rank)] = "capacity: " + str(e)
