@@ -1042,7 +1042,7 @@ bool run_search(b2_brfs& B, b2_brfs_result& R, u64 prefix_states = 0)
 }
 }  // namespace
 
-bool run_prefix(b2_brfs& B, b2_brfs_result& R, u64 prefix_states) { return run_search(B, R, prefix_states); }
+bool b2::run_prefix(b2_brfs& B, b2_brfs_result& R, u64 prefix_states) { return run_search(B, R, prefix_states); }
 
 extern "C" {
 
