@@ -199,6 +199,8 @@ b2_status b2_comm_create(b2_ctx* ctx, const b2_comm_id* id, uint32_t rank, uint3
 /* Seconds a rank waits for the others' part of a collective before it aborts the communicator and fails the call
  * with B2_CUDA_ERROR (default 600): a rank that stopped taking part ends the others' searches instead of hanging them. */
 b2_status b2_comm_set_timeout(b2_comm* comm, double seconds);
+/* Releases the communicator. Collective: every rank destroys it, after the last search over it has ended on every
+ * rank (NCCL's teardown waits for the other ranks). */
 void b2_comm_destroy(b2_comm* comm);
 
 /* ------------------------------------------------------------------------------------------------ BrFS
