@@ -286,6 +286,8 @@ __global__ void k_g_end(DevLayerState* d, cudaGraphConditionalHandle loop)
         d->layers += 1;
         if (d->stop || d->misc.status)
             d->done = 1;
+        else if (d->stop_frontier && d->layer_end - d->layer_begin >= d->stop_frontier && d->layers < d->max_depth)
+            d->done = d->cut = 1;
     }
     cudaGraphSetConditional(loop, d->done || d->overflow ? 0u : 1u);
 }
@@ -692,7 +694,7 @@ void build_device_layers(b2_brfs& B, const std::vector<u64>& key, DevLayerState*
 
 /// The one-GPU search. With prefix_states, it stops after the first layer whose new states number at least
 /// prefix_states, before expanding them, and returns true (the search goes on elsewhere: a sharded search takes over
-/// from there); such a search runs in the host loop. Otherwise, and when it ends before that layer, it returns false.
+/// from there). Otherwise, and when it ends before that layer, it returns false.
 bool run_search(b2_brfs& B, b2_brfs_result& R, u64 prefix_states = 0)
 {
     const auto t0 = std::chrono::steady_clock::now();
@@ -796,7 +798,7 @@ bool run_search(b2_brfs& B, b2_brfs_result& R, u64 prefix_states = 0)
     bool finished = false;
     // With the buffers presized (expected_states), no per-layer events and no max_states cut, the layers run as one
     // graph launch on the device; a layer that outgrows the buffers continues in the host loop below.
-    if (B.task->jit && !o.timings && o.max_states == ~u64{0} && o.expected_states > 0 && !prefix_states)
+    if (B.task->jit && !o.timings && o.max_states == ~u64{0} && o.expected_states > 0)
     {
         DevLayerState init{};
         init.layer_begin = 0;
@@ -805,6 +807,7 @@ bool run_search(b2_brfs& B, b2_brfs_result& R, u64 prefix_states = 0)
         init.cand_next = 1;
         init.max_depth = o.max_depth;
         init.stop_at_goal = o.stop_at_goal ? 1 : 0;
+        init.stop_frontier = prefix_states;
         std::vector<u64> log;
         const DevLayerState r = run_device_layers(B, init, log);
         if (r.misc.status & kStatusProbeLimit)
@@ -832,6 +835,7 @@ bool run_search(b2_brfs& B, b2_brfs_result& R, u64 prefix_states = 0)
         layer_begin = r.layer_begin;
         layer_end = r.layer_end;
         finished = r.done != 0;
+        cut = r.cut != 0;
     }
     while (!finished)
     {

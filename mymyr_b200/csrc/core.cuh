@@ -567,7 +567,8 @@ struct DevLayerState
     u32 layers, max_depth, stop_at_goal;
     u32 done;                    // the search is over (exhausted, depth bound, goal stop)
     u32 overflow;                // a buffer is too small for the current layer: left to the host, nothing of it done
-    u32 exhausted, solved, stop, pad;
+    u32 exhausted, solved, stop, cut;  // cut: ended at stop_frontier, the search goes on elsewhere
+    u64 stop_frontier;           // 0, or end the loop after the first layer with at least this many new states
     LayerMisc misc;              // the current layer's counters
 };
 
