@@ -635,10 +635,12 @@ def main():
         torch.cuda.synchronize(device)
 
     # ---------------------------------------------------------------- timed region (device events)
-    barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     results = []
+    # rank 0's sampler thread starts before the barrier: its start-up and first NVML queries overlap the barrier, not
+    # the first search (whose collectives would make every other rank wait for it)
     with clk:
+        barrier()
         ev0.record(stream)
         for _ in range(args.steps):
             results.append(one(expected))

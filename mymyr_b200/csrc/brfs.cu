@@ -1046,7 +1046,11 @@ bool run_search(b2_brfs& B, b2_brfs_result& R, u64 prefix_states = 0)
 }
 }  // namespace
 
-bool b2::run_prefix(b2_brfs& B, b2_brfs_result& R, u64 prefix_states) { return run_search(B, R, prefix_states); }
+bool b2::run_prefix(b2_brfs& B, b2_brfs_result& R, u64 prefix_states)
+{
+    B.ran_one_gpu = true;  // its buffers (and any layer-loop graph) go to the context's cache for the next search
+    return run_search(B, R, prefix_states);
+}
 
 extern "C" {
 
@@ -1248,7 +1252,7 @@ void b2_brfs_destroy(b2_brfs* search)
         shard_free(*search);
     if (search->stream)
     {
-        if (search->ran && (!search->shard || search->from_cache))
+        if (search->ran && (!search->shard || search->ran_one_gpu))
         {
             // an idle search's buffers (and layer-loop graph) are kept by the context for its next search
             stream_drain(search->stream);

@@ -374,6 +374,7 @@ struct b2_brfs
     cudaGraphExec_t graph_exec = nullptr;
     std::vector<b2::u64> graph_key;
     bool from_cache = false;  // the buffers (and graph) came from the context's cache and go back to it
+    bool ran_one_gpu = false; // the one-GPU buffers were used (a one-GPU search, or a sharded search's small layers)
     bool ran = false;
     bool own_stream = false;
     // sharded search (options.comm set)

@@ -652,8 +652,9 @@ void shard_run(b2_brfs& B, b2_brfs_result& R)
         // then keeps the states it owns, in id order, with their node records, and the sharded loop goes on from
         // that frontier. The ids, counts and fingerprint are the one-GPU search's either way.
         const b2_brfs_options saved = B.opt;
-        // presized for the device-driven layer loop (a layer that outgrows the buffers goes on in the host loop)
-        B.opt.expected_states = std::max<u64>(4 * shard_from, u64{1} << 16);
+        // the host loop, its buffers grown as the layers need (the device-driven loop would instantiate its graph for
+        // the prefix's buffers once per process and keep it in the context's cache)
+        B.opt.expected_states = 0;
         B.opt.fingerprint = 0;
         B.opt.timings = 0;
         std::vector<u64> plc(3 * 4096);
