@@ -41,8 +41,12 @@ def owner_of(h: int, world: int) -> int:
     return ((int(h) >> 32) * world) >> 32
 
 
-def sharded_brfs_model(text: str, rank: int, world: int, max_depth: int | None, witness: bool = True) -> dict:
-    """One rank of the sharded BrFS protocol (dbrfs.cu); successors from the compiled reference (rl::expand)."""
+def sharded_brfs_model(text: str, rank: int, world: int, max_depth: int | None, witness: bool = True,
+                       shard_from: int = 1) -> dict:
+    """One rank of the sharded BrFS protocol (dbrfs.cu); successors from the compiled reference (rl::expand). With
+    shard_from > 1 every rank first runs the same one-GPU search alone (here the reference's BrFS) up to the first
+    layer of at least shard_from new states, keeps the states it owns (id order, global parent ids) and goes on from
+    there, as shard_run does after run_prefix."""
     from oracle import ref as oref
 
     t = oref.RefTask(text)
@@ -57,6 +61,24 @@ def sharded_brfs_model(text: str, rank: int, world: int, max_depth: int | None, 
     counts = []
     layers = 0
     lane = 1
+    if shard_from > 1:
+        full = t.brfs(max_depth=max_depth, stop_at_goal=False, witness_pruning=witness)["layer_counts"]
+        cut = next((L for L, (_, _, n) in enumerate(full) if n >= shard_from and (max_depth is None or L + 1 < max_depth)),
+                   None)
+        if cut is not None:
+            rows, par, idx = t.brfs_states(max_depth=cut + 1, witness_pruning=witness)
+            counts = [tuple(c) for c in full[: cut + 1]]
+            layers = cut + 1
+            n_total = len(rows)
+            layer_end = n_total
+            layer_begin = n_total - counts[-1][2]
+            store.clear()
+            mine.clear()
+            for sid in range(n_total):  # the conversion: owned states in id order
+                if owner_of(oref.hash_state(rows[sid]), world) == rank:
+                    store[rows[sid].tobytes()] = sid
+                    mine.append((sid, rows[sid].copy(), 0xFFFFFFFF if sid == 0 else int(par[sid]), int(idx[sid])))
+            lb_local = next((i for i, m in enumerate(mine) if m[0] >= layer_begin), len(mine))
     while layer_end > layer_begin and (max_depth is None or layers < max_depth):
         layers += 1
         E = layer_end - layer_begin
@@ -128,11 +150,11 @@ def sharded_brfs_model(text: str, rank: int, world: int, max_depth: int | None, 
     return {"states": n_total, "layer_counts": counts, "local": mine}
 
 
-def _protocol_worker(rank, world, port, cases, out):
+def _protocol_worker(rank, world, port, cases, out, shard_from=1):
     _init(rank, world, port)
     try:
         for name, text, depth in cases:
-            r = sharded_brfs_model(text, rank, world, depth)
+            r = sharded_brfs_model(text, rank, world, depth, shard_from=shard_from)
             shards: list = [None] * world
             td.all_gather_object(shards, r["local"])
             if rank == 0:
@@ -150,9 +172,11 @@ def _protocol_worker(rank, world, port, cases, out):
         td.destroy_process_group()
 
 
+@pytest.mark.parametrize("shard_from", [1, 40])
 @pytest.mark.parametrize("world", [2, 3])
-def test_sharded_protocol_matches_reference_ids(ref, world):
-    """Hash-owner sharding, global candidate indices and owner-side minimum discovery give the reference's ids."""
+def test_sharded_protocol_matches_reference_ids(ref, world, shard_from):
+    """Hash-owner sharding, global candidate indices and owner-side minimum discovery give the reference's ids; with
+    shard_from 40 the small layers are replicated first and the ranks shard from the first frontier of 40 states."""
     from oracle import ref as oref
 
     cases = [("tower5", tasks.tower(5, 3), None), ("transport", tasks.transport(2, 6, 2, 0), None),
@@ -161,8 +185,8 @@ def test_sharded_protocol_matches_reference_ids(ref, world):
              ("transport200", tasks.transport(2, 200, 3, 0), 2)]
     mgr = mp.get_context("spawn").Manager()
     out = mgr.dict()
-    mp.start_processes(_protocol_worker, args=(world, _free_port(), cases, out), nprocs=world, join=True,
-                       start_method="spawn")
+    mp.start_processes(_protocol_worker, args=(world, _free_port(), cases, out, shard_from), nprocs=world,
+                       join=True, start_method="spawn")
     for name, text, depth in cases:
         got = out[name]
         t = oref.RefTask(text)
